@@ -1,0 +1,252 @@
+/*
+ * rtgpu.h -- C ABI of the B200 (sm_100a) backend for rtensor's training hot
+ * path: Dense-layer GEMMs (Y = XW, dX = dY W^T, dW = X^T dY), fused bias/ReLU
+ * and ReLU-mask epilogues, softmax cross-entropy, SGD/Adam, and the whole-step
+ * plan (GpuMlp) with optional NCCL data parallelism.
+ *
+ * Every entry point replaces one item of rtensor's wgpu backend
+ * (MMMejias39/RGPU, crates/rtensor/src/gpu/mod.rs) or of its CPU optimiser
+ * API; the cited file:line is the interface it stands in for.  Conventions:
+ *   - every call returns an rt_status (0 = RT_OK); where the reference panics
+ *     on misuse (shape mismatch, batch mismatch) this ABI returns
+ *     RT_ERR_INVALID and rt_last_error() describes the problem;
+ *   - all work is enqueued asynchronously on the context's CUDA stream; only
+ *     the *_download / *_weights / *_grads / *_logits / *_last_loss readers
+ *     and rt_ctx_sync block, as Gpu::download / GpuMlp::last_loss do
+ *     (gpu/mod.rs:530-566, 1529);
+ *   - tensors are row-major with an explicit leading dimension (elements);
+ *   - there is no CPU fallback: every compute call runs a CUDA kernel of this
+ *     library or fails.
+ */
+#ifndef RTGPU_H
+#define RTGPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RTGPU_ABI_VERSION 1
+
+typedef enum {
+    RT_OK = 0,
+    RT_ERR_INVALID = 1,        /* bad argument or shape (reference: panic!/assert!) */
+    RT_ERR_CUDA = 2,           /* CUDA runtime/driver error */
+    RT_ERR_NCCL = 3,           /* NCCL error */
+    RT_ERR_OOM = 4,            /* device allocation failed */
+    RT_ERR_DEVICE_TIMEOUT = 5, /* a bounded device-side wait expired */
+    RT_ERR_UNSUPPORTED = 6     /* no device, wrong architecture, feature off */
+} rt_status;
+
+typedef enum { RT_F32 = 0, RT_BF16 = 1, RT_U32 = 2 } rt_dtype;
+
+typedef struct rt_ctx rt_ctx;       /* gpu::Gpu        (gpu/mod.rs:224-247) */
+typedef struct rt_tensor rt_tensor; /* gpu::GpuTensor  (gpu/mod.rs:191-195) */
+typedef struct rt_mlp rt_mlp;       /* gpu::GpuMlp     (gpu/mod.rs:1319-1336) */
+typedef struct rt_comm rt_comm;     /* NCCL communicator (no reference counterpart:
+                                       data parallelism is absent, crates/rtensor/README.md:123) */
+
+/* ---------------------------------------------------------------- errors */
+/* Message of the last failing call on this thread (Result<_, String> Err payload,
+ * gpu/mod.rs:263-277). */
+const char* rt_last_error(void);
+int rt_abi_version(void);
+
+/* --------------------------------------------------------------- context */
+/* Gpu::new / Gpu::com_adaptador (gpu/mod.rs:263-298): bind CUDA device
+ * `device`, create the context stream, check for sm_100. */
+int rt_ctx_create(int device, rt_ctx** out);
+int rt_ctx_destroy(rt_ctx* ctx);
+/* Gpu::info (gpu/mod.rs:411-413). */
+int rt_ctx_info(const rt_ctx* ctx, char* buf, size_t len);
+/* Gpu::sync (gpu/mod.rs:564-566); also reports RT_ERR_DEVICE_TIMEOUT when a
+ * kernel's bounded wait expired since the last sync. */
+int rt_ctx_sync(rt_ctx* ctx);
+/* The cudaStream_t work is enqueued on (Gpu::queue, gpu/mod.rs:422-424). */
+void* rt_ctx_stream(rt_ctx* ctx);
+/* Use a caller-owned cudaStream_t instead (NULL restores the context's own). */
+int rt_ctx_set_stream(rt_ctx* ctx, void* stream);
+/* Gpu::set_fast_gemm (gpu/mod.rs:442-448): 1 = tcgen05/TMA tensor-core GEMM
+ * where the operands allow it (default), 0 = tiled SIMT GEMM everywhere. */
+int rt_ctx_set_fast_gemm(rt_ctx* ctx, int on);
+/* Gpu::set_grupo_l2 (gpu/mod.rs:452-458): tile rows per L2 raster group. */
+int rt_ctx_set_l2_group(rt_ctx* ctx, int group);
+/* Number of kernels this context has launched so far (evidence counter). */
+int rt_ctx_launch_count(const rt_ctx* ctx, uint64_t* out);
+
+/* Page-locked host memory for asynchronous copies. */
+int rt_host_alloc(size_t bytes, void** out);
+int rt_host_free(void* p);
+
+/* --------------------------------------------------------------- tensors */
+/* Gpu::zeros (gpu/mod.rs:501-506): rank 1 or 2, leading dimension padded so
+ * that every row starts 16-byte aligned. */
+int rt_tensor_zeros(rt_ctx* ctx, rt_dtype dtype, int rank, const int64_t* shape, rt_tensor** out);
+/* Gpu::upload (gpu/mod.rs:509-516): host f32 -> device tensor of `dtype`
+ * (RT_BF16 rounds to nearest even on the device). */
+int rt_tensor_upload(rt_ctx* ctx, rt_dtype dtype, const float* host, int rank, const int64_t* shape,
+                     rt_tensor** out);
+/* upload_labels (gpu/mod.rs:1671-1675). */
+int rt_upload_labels(rt_ctx* ctx, const uint32_t* labels, int64_t n, rt_tensor** out);
+/* Gpu::download (gpu/mod.rs:530-545): blocking; bf16 widens to f32.  `host`
+ * holds rows*cols floats, packed (no padding). */
+int rt_tensor_download(rt_ctx* ctx, const rt_tensor* t, float* host);
+/* Non-owning view of caller memory (cudarc-style raw handle).  `ld` in
+ * elements; 0 means packed. */
+int rt_tensor_wrap(rt_ctx* ctx, void* device_ptr, rt_dtype dtype, int rank, const int64_t* shape,
+                   int64_t ld, rt_tensor** out);
+int rt_tensor_free(rt_tensor* t);
+void* rt_tensor_ptr(const rt_tensor* t);
+/* rows, cols, ld (rank-1 tensors report rows = 1). */
+int rt_tensor_dims(const rt_tensor* t, int64_t* rows, int64_t* cols, int64_t* ld);
+
+/* ------------------------------------------------------------------- ops */
+/* All ops enqueue on the context stream.  GEMM operands are f32 or bf16 (both
+ * operands of one GEMM share a type); outputs are f32 or bf16; accumulation is
+ * always f32. */
+
+/* Gpu::op_matmul (gpu/mod.rs:685-688): C[m,n] = A[m,k] B[k,n]. */
+int rt_matmul(rt_ctx* ctx, const rt_tensor* a, const rt_tensor* b, rt_tensor* c);
+/* Gpu::op_matmul_at_b (gpu/mod.rs:691-694): C = A^T B with A stored [k,m] (dW = X^T dY). */
+int rt_matmul_at_b(rt_ctx* ctx, const rt_tensor* a, const rt_tensor* b, rt_tensor* c);
+/* Gpu::op_matmul_a_bt (gpu/mod.rs:697-700): C = A B^T with B stored [n,k] (dX = dY W^T). */
+int rt_matmul_a_bt(rt_ctx* ctx, const rt_tensor* a, const rt_tensor* b, rt_tensor* c);
+/* Gpu::op_matmul_bias (gpu/mod.rs:722-749): C = A B + 1 bias, ReLU if relu != 0. */
+int rt_matmul_bias(rt_ctx* ctx, const rt_tensor* a, const rt_tensor* b, rt_tensor* c,
+                   const rt_tensor* bias, int relu);
+/* Gpu::ops_split_k (gpu/mod.rs:1095-1146): C = A B (transposed = 0) or A^T B
+ * (transposed = 1) with k split in `slices`; `partials` holds >= slices*m*n
+ * f32 (rt_split_k_workspace).  The slices are summed in a fixed order. */
+int rt_matmul_split_k(rt_ctx* ctx, const rt_tensor* a, const rt_tensor* b, rt_tensor* c,
+                      rt_tensor* partials, int slices, int transposed);
+/* Gpu::fatias_sugeridas (gpu/mod.rs:1079-1088), same rule: 64-block target,
+ * 64x64 blocks, at least 4 16-deep k tiles per slice. */
+int rt_split_k_suggest(int64_t m, int64_t n, int64_t k);
+int64_t rt_split_k_workspace(int64_t m, int64_t n, int slices);
+
+/* Full-control GEMM used by the plan (and by Rust callers that manage their
+ * own buffers).  Logical A is [m,k], logical B is [k,n]:
+ *   RT_NN: A stored [m,k] (lda), B stored [k,n] (ldb)      Y  = X W
+ *   RT_NT: A stored [m,k],       B stored [n,k]            dX = dY W^T
+ *   RT_TN: A stored [k,m],       B stored [k,n]            dW = X^T dY
+ * Epilogues (gemm.rs:372-494 MM_EPILOGO and kernels.rs:119-131 RELU_BWD):
+ *   RT_EPI_NONE       C = acc
+ *   RT_EPI_BIAS       C = acc + bias[j]
+ *   RT_EPI_BIAS_RELU  C = max(acc + bias[j], 0)
+ *   RT_EPI_RELU_MASK  C = acc * 1[mask[i,j] > 0]   (mask has the output dtype)
+ * split_k: 0 = choose, 1 = none, >1 = that many k slices (needs workspace of
+ * rt_gemm_workspace_size bytes). */
+typedef enum { RT_NN = 0, RT_NT = 1, RT_TN = 2 } rt_layout;
+typedef enum { RT_EPI_NONE = 0, RT_EPI_BIAS = 1, RT_EPI_BIAS_RELU = 2, RT_EPI_RELU_MASK = 3 } rt_epilogue;
+typedef struct {
+    rt_layout layout;
+    rt_dtype in_dtype;  /* RT_F32 or RT_BF16 */
+    rt_dtype out_dtype; /* RT_F32 or RT_BF16 */
+    int64_t m, n, k;
+    const void* a; int64_t lda;
+    const void* b; int64_t ldb;
+    void* c; int64_t ldc;
+    rt_epilogue epilogue;
+    const float* bias;
+    const void* mask; int64_t ldmask;
+    int split_k;
+    void* workspace; size_t workspace_bytes;
+} rt_gemm_args;
+int rt_gemm(rt_ctx* ctx, const rt_gemm_args* args);
+size_t rt_gemm_workspace_size(rt_ctx* ctx, const rt_gemm_args* args);
+
+/* Gpu::op_bias_add (gpu/mod.rs:752-762): Z += 1 b. */
+int rt_bias_add(rt_ctx* ctx, rt_tensor* z, const rt_tensor* b);
+/* Gpu::op_relu (gpu/mod.rs:765-775): Y = max(X, 0). */
+int rt_relu(rt_ctx* ctx, const rt_tensor* x, rt_tensor* y);
+/* Gpu::op_relu_bwd (gpu/mod.rs:778-788): dz *= 1[a > 0], in place. */
+int rt_relu_bwd(rt_ctx* ctx, const rt_tensor* a, rt_tensor* dz);
+/* Gpu::op_softmax_xent (gpu/mod.rs:791-808): per-row loss
+ * -ln(max(p_y, 1e-12)) and delta = (P - Y) * scale (scale = 1/n for the
+ * losses.rs:99-115 adjoint; pass 1/n_global under data parallelism). */
+int rt_softmax_xent(rt_ctx* ctx, const rt_tensor* logits, const rt_tensor* labels, rt_tensor* delta,
+                    rt_tensor* loss, float scale);
+/* Gpu::ops_colsum (gpu/mod.rs:838-855): dst[1,m] = 1^T src, two fixed-order
+ * stages through `scratch` (>= ceil(rows/64) x cols f32). */
+int rt_colsum(rt_ctx* ctx, const rt_tensor* src, rt_tensor* dst, rt_tensor* scratch);
+/* Gpu::op_adam + atualizar_adam (gpu/mod.rs:859-907) with the CPU optimiser's
+ * arithmetic (optim.rs:163-198: pre-inverted bias corrections for step t). */
+int rt_adam(rt_ctx* ctx, rt_tensor* theta, rt_tensor* m, rt_tensor* v, const rt_tensor* g,
+            float lr, float beta1, float beta2, float eps, int t);
+/* Sgd::step without momentum (optim.rs:80-95): theta -= g * lr.  The
+ * reference has no GPU kernel for it. */
+int rt_sgd(rt_ctx* ctx, rt_tensor* theta, const rt_tensor* g, float lr);
+/* Gpu::op_empacota_f16 (gpu/mod.rs:1170-1182), bf16 instead of f16:
+ * dst (bf16) = round-to-nearest-even(src (f32)). */
+int rt_cast(rt_ctx* ctx, const rt_tensor* src, rt_tensor* dst);
+
+/* ------------------------------------------------------------ MLP plan */
+typedef enum { RT_OPT_NONE = 0, RT_OPT_SGD = 1, RT_OPT_ADAM = 2 } rt_optimizer;
+typedef struct {
+    int n_layers;          /* Dense layers; dims has n_layers + 1 entries */
+    const int64_t* dims;   /* d_0 (inputs) .. d_L (classes) */
+    int64_t batch;         /* rows per step on this device */
+    int64_t global_batch;  /* rows per step over all ranks (0 = batch) */
+    rt_dtype dtype;        /* RT_F32, or RT_BF16: bf16 operands/activations,
+                              f32 accumulate, f32 master weights + bf16 shadow */
+    rt_optimizer optimizer;
+    float lr, beta1, beta2, eps;
+} rt_mlp_config;
+
+/* GpuMlp::from_params (gpu/mod.rs:1341-1482): hidden layers ReLU, output
+ * linear + softmax-CE.  weights[l] is W_l [d_l, d_{l+1}] row-major f32,
+ * biases[l] is b_l [d_{l+1}] (NULL = zeros).  The step is captured into a
+ * CUDA graph on first use. */
+int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* weights,
+                  const float* const* biases, rt_mlp** out);
+int rt_mlp_destroy(rt_mlp* mlp);
+/* GpuMlp::step (gpu/mod.rs:1499-1511): x [batch, d_0] and labels [batch]
+ * already on the device (copied into the plan's input buffers, as
+ * GpuMlp::carregar does, gpu/mod.rs:1486-1495), then forward, backward,
+ * (allreduce,) update.  x_dtype is RT_F32 or RT_BF16. */
+int rt_mlp_step(rt_mlp* mlp, const void* x_dev, rt_dtype x_dtype, const uint32_t* labels_dev);
+/* The same step from page-locked or pageable HOST buffers: the host->device
+ * copies and, when loss_rows_host != NULL, the device->host copy of the
+ * per-row losses ([batch] f32) are enqueued with the step.  Returns once
+ * enqueued; the loss buffer is valid after rt_ctx_sync. */
+int rt_mlp_step_host(rt_mlp* mlp, const void* x_host, rt_dtype x_dtype, const uint32_t* labels_host,
+                     float* loss_rows_host);
+/* GpuMlp::forward_only (gpu/mod.rs:1514-1521). */
+int rt_mlp_forward_only(rt_mlp* mlp, const void* x_dev, rt_dtype x_dtype);
+/* GpuMlp::logits (gpu/mod.rs:1524-1526): [batch, classes] f32, blocking. */
+int rt_mlp_logits(rt_mlp* mlp, float* host);
+/* GpuMlp::last_loss (gpu/mod.rs:1529-1531): mean row loss, blocking. */
+int rt_mlp_last_loss(rt_mlp* mlp, float* out);
+/* GpuMlp::weights / grads (gpu/mod.rs:1534-1551) for one layer, blocking,
+ * packed f32 (w: d_l*d_{l+1}, b: d_{l+1}); either pointer may be NULL. */
+int rt_mlp_weights(rt_mlp* mlp, int layer, float* w, float* b);
+int rt_mlp_grads(rt_mlp* mlp, int layer, float* dw, float* db);
+/* Param::set (tape.rs:119-121) on the device copy: overwrite W_l / b_l. */
+int rt_mlp_set_weights(rt_mlp* mlp, int layer, const float* w, const float* b);
+/* GpuMlp::dispatches_por_passo (gpu/mod.rs:1559-1561): kernels per step. */
+int rt_mlp_dispatches_per_step(rt_mlp* mlp, int* out);
+/* Gpu::perfilar (gpu/mod.rs:1245-1286): when on, the captured step records a
+ * CUDA event around every kernel; rt_mlp_op_times then reports, for the last
+ * step, the label, the algorithmic FLOPs (0 for non-GEMM kernels) and the
+ * device milliseconds of op i < count. */
+int rt_mlp_enable_timing(rt_mlp* mlp, int on);
+int rt_mlp_op_count(rt_mlp* mlp, int* count);
+int rt_mlp_op_time(rt_mlp* mlp, int i, const char** label, double* flops, float* ms);
+/* Attach a communicator: dW/db are summed over ranks with ncclAllReduce on a
+ * second stream, layer by layer as backward produces them. */
+int rt_mlp_set_comm(rt_mlp* mlp, rt_comm* comm);
+
+/* ------------------------------------------------------------------ NCCL */
+/* 128-byte ncclUniqueId, created on one rank and shared out of band. */
+int rt_comm_unique_id(unsigned char id[128]);
+int rt_comm_init(rt_ctx* ctx, int rank, int world, const unsigned char id[128], rt_comm** out);
+int rt_comm_destroy(rt_comm* comm);
+/* In-place sum over ranks on the context stream. */
+int rt_comm_allreduce_f32(rt_comm* comm, float* dev_buf, int64_t count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RTGPU_H */

@@ -1,0 +1,135 @@
+// NCCL communicator for data parallelism.  rtensor has no data-parallel mode
+// (crates/rtensor/README.md:123 lists it as absent); this is the new exchange
+// step of the B200 design: every rank holds a full replica, takes its slice of
+// the global batch, and dW/db are summed over ranks with ncclAllReduce before
+// the identical optimiser step runs everywhere.
+//
+// NCCL is resolved at run time (dlopen) instead of at link time: a process
+// that already holds a libnccl.so.2 (PyTorch ships its own) keeps using that
+// one, and processes that never form a communicator never load NCCL at all.
+// RT_NCCL_LIB overrides the library path.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "internal.h"
+
+namespace {
+
+struct NcclApi {
+    bool loaded = false;
+    std::string error;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+NcclApi& nccl_api() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        const char* env = getenv("RT_NCCL_LIB");
+        void* h = nullptr;
+        if (env && *env) h = dlopen(env, RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) {
+            api.error = std::string("cannot load libnccl.so.2: ") + dlerror();
+            return;
+        }
+        api.GetUniqueId = (decltype(api.GetUniqueId))dlsym(h, "ncclGetUniqueId");
+        api.CommInitRank = (decltype(api.CommInitRank))dlsym(h, "ncclCommInitRank");
+        api.CommDestroy = (decltype(api.CommDestroy))dlsym(h, "ncclCommDestroy");
+        api.AllReduce = (decltype(api.AllReduce))dlsym(h, "ncclAllReduce");
+        api.GetErrorString = (decltype(api.GetErrorString))dlsym(h, "ncclGetErrorString");
+        if (!api.GetUniqueId || !api.CommInitRank || !api.CommDestroy || !api.AllReduce || !api.GetErrorString) {
+            api.error = "libnccl.so.2 lacks a required symbol";
+            return;
+        }
+        api.loaded = true;
+    });
+    return api;
+}
+
+int need_nccl() {
+    NcclApi& a = nccl_api();
+    if (!a.loaded) return rt::fail(RT_ERR_NCCL, "%s", a.error.c_str());
+    return RT_OK;
+}
+
+}  // namespace
+
+struct rt_comm {
+    rt_ctx* ctx = nullptr;
+    ncclComm_t nccl = nullptr;
+    int rank = 0, world = 1;
+};
+
+namespace rt {
+
+int comm_allreduce(rt_comm* comm, float* buf, int64_t count, cudaStream_t st) {
+    if (!comm || count == 0) return RT_OK;
+    NcclApi& A = nccl_api();
+    ncclResult_t r = A.AllReduce(buf, buf, (size_t)count, ncclFloat32, ncclSum, comm->nccl, st);
+    if (r != ncclSuccess) return fail(RT_ERR_NCCL, "ncclAllReduce failed: %s", A.GetErrorString(r));
+    return RT_OK;
+}
+
+}  // namespace rt
+
+using namespace rt;
+
+extern "C" {
+
+int rt_comm_unique_id(unsigned char id[128]) {
+    RT_CHECK(id, "id buffer is NULL");
+    static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId is 128 bytes");
+    RT_TRY(need_nccl());
+    NcclApi& A = nccl_api();
+    ncclUniqueId u;
+    ncclResult_t r = A.GetUniqueId(&u);
+    if (r != ncclSuccess) return fail(RT_ERR_NCCL, "ncclGetUniqueId failed: %s", A.GetErrorString(r));
+    memcpy(id, &u, 128);
+    return RT_OK;
+}
+
+int rt_comm_init(rt_ctx* ctx, int rank, int world, const unsigned char id[128], rt_comm** out) {
+    RT_CHECK(ctx && id && out, "rt_comm_init: bad arguments");
+    RT_CHECK(world >= 1 && rank >= 0 && rank < world, "rt_comm_init: rank %d / world %d", rank, world);
+    RT_TRY(need_nccl());
+    NcclApi& A = nccl_api();
+    RT_CUDA(cudaSetDevice(ctx->device));
+    ncclUniqueId u;
+    memcpy(&u, id, 128);
+    rt_comm* c = new rt_comm;
+    c->ctx = ctx;
+    c->rank = rank;
+    c->world = world;
+    ncclResult_t r = A.CommInitRank(&c->nccl, world, u, rank);
+    if (r != ncclSuccess) {
+        delete c;
+        return fail(RT_ERR_NCCL, "ncclCommInitRank(rank %d of %d) failed: %s", rank, world, A.GetErrorString(r));
+    }
+    *out = c;
+    return RT_OK;
+}
+
+int rt_comm_destroy(rt_comm* c) {
+    if (!c) return RT_OK;
+    if (c->nccl) nccl_api().CommDestroy(c->nccl);
+    delete c;
+    return RT_OK;
+}
+
+int rt_comm_allreduce_f32(rt_comm* c, float* buf, int64_t count) {
+    RT_CHECK(c && buf && count >= 0, "rt_comm_allreduce_f32: bad arguments");
+    return comm_allreduce(c, buf, count, c->ctx->stream);
+}
+
+}  // extern "C"

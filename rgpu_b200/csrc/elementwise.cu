@@ -1,0 +1,415 @@
+// Memory-bound kernels of the training step: softmax cross-entropy, the
+// bias-gradient column reduction, bias/ReLU helpers, casts and the SGD/Adam
+// updates.  Counterparts of rtensor's WGSL kernels in
+// crates/rtensor/src/gpu/kernels.rs (XENT 138-167, COLSUM 182-199, ADAM
+// 205-224, VEC 86-112, RELU_BWD 119-131) and mista.rs:326-341 (EMPACOTA), with
+// the arithmetic of the CPU optimiser (optim.rs:80-198) that the parity tests
+// hold them to.
+#include "internal.h"
+
+namespace rt {
+namespace {
+
+template <typename T>
+__device__ __forceinline__ float ldf(const T* p, int64_t i);
+template <>
+__device__ __forceinline__ float ldf<float>(const float* p, int64_t i) { return p[i]; }
+template <>
+__device__ __forceinline__ float ldf<__nv_bfloat16>(const __nv_bfloat16* p, int64_t i) {
+    return __bfloat162float(p[i]);
+}
+template <typename T>
+__device__ __forceinline__ void stf(T* p, int64_t i, float v);
+template <>
+__device__ __forceinline__ void stf<float>(float* p, int64_t i, float v) { p[i] = v; }
+template <>
+__device__ __forceinline__ void stf<__nv_bfloat16>(__nv_bfloat16* p, int64_t i, float v) {
+    p[i] = __float2bfloat16_rn(v);
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ------------------------------------------------------------------ xent
+// One warp per row (kernels.rs:146-166 uses one thread per row).  Loss is
+// -ln(max(p_y, 1e-12)) as losses.rs:104-111 computes it; delta is
+// (p - 1[j == y]) * scale (losses.rs:114, scale = g/n).
+template <typename TD>
+__global__ void xent_kernel(const float* __restrict__ logits, int64_t ldz, const uint32_t* __restrict__ labels,
+                            int64_t n, int64_t C, float scale, TD* __restrict__ delta, int64_t ldd,
+                            float* __restrict__ loss) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+    if (r >= n) return;
+    const float* z = logits + r * ldz;
+    float mx = -INFINITY;
+    for (int64_t j = lane; j < C; j += 32) mx = fmaxf(mx, z[j]);
+    mx = warp_max(mx);
+    float s = 0.0f;
+    for (int64_t j = lane; j < C; j += 32) s += expf(z[j] - mx);
+    s = warp_sum(s);
+    const uint32_t y = labels[r];
+    TD* d = delta + r * ldd;
+    for (int64_t j = lane; j < C; j += 32) {
+        float p = expf(z[j] - mx) / s;
+        stf<TD>(d, j, (p - (j == (int64_t)y ? 1.0f : 0.0f)) * scale);
+    }
+    if (lane == 0) {
+        float l;
+        if ((int64_t)y < C)
+            l = -logf(fmaxf(expf(z[y] - mx) / s, 1e-12f));
+        else
+            l = __int_as_float(0x7fc00000);  // label out of range: NaN loss, as a visible error
+        loss[r] = l;
+    }
+}
+
+// --------------------------------------------------------------- colsum
+constexpr int kColsumChunk = 64;
+
+template <typename T>
+__global__ void colsum_stage_kernel(const T* __restrict__ src, int64_t rows, int64_t cols, int64_t ld,
+                                    int64_t chunk, float* __restrict__ dst) {
+    int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= cols) return;
+    int64_t r0 = (int64_t)blockIdx.y * chunk;
+    int64_t r1 = min(rows, r0 + chunk);
+    float acc = 0.0f;
+    for (int64_t i = r0; i < r1; ++i) acc += ldf<T>(src, i * ld + j);
+    dst[(int64_t)blockIdx.y * cols + j] = acc;
+}
+
+// ---------------------------------------------------------- elementwise
+template <typename T>
+__global__ void bias_add_kernel(T* z, int64_t rows, int64_t cols, int64_t ld, const float* b) {
+    int64_t total = rows * cols;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        int64_t i = idx / cols, j = idx % cols;
+        stf<T>(z, i * ld + j, ldf<T>(z, i * ld + j) + b[j]);
+    }
+}
+
+template <typename T>
+__global__ void relu_kernel(const T* x, T* y, int64_t rows, int64_t cols, int64_t ldx, int64_t ldy) {
+    int64_t total = rows * cols;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        int64_t i = idx / cols, j = idx % cols;
+        stf<T>(y, i * ldy + j, fmaxf(ldf<T>(x, i * ldx + j), 0.0f));
+    }
+}
+
+template <typename T>
+__global__ void relu_bwd_kernel(const T* a, T* dz, int64_t rows, int64_t cols, int64_t lda, int64_t ldz) {
+    int64_t total = rows * cols;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        int64_t i = idx / cols, j = idx % cols;
+        float m = ldf<T>(a, i * lda + j) > 0.0f ? 1.0f : 0.0f;
+        stf<T>(dz, i * ldz + j, ldf<T>(dz, i * ldz + j) * m);
+    }
+}
+
+template <typename TS, typename TD>
+__global__ void cast_kernel(const TS* s, int64_t lds, TD* d, int64_t ldd, int64_t rows, int64_t cols) {
+    int64_t total = rows * cols;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        int64_t i = idx / cols, j = idx % cols;
+        stf<TD>(d, i * ldd + j, ldf<TS>(s, i * lds + j));
+    }
+}
+
+// ------------------------------------------------------------ optimisers
+struct OptBatch {
+    OptTensor t[kMaxOptTensors];
+    int count;
+};
+
+// f32::powi with a runtime exponent (compiler-rt __powisf2: square and
+// multiply), as Adam::step computes beta^t (optim.rs:163-164).
+__device__ float powi_f32(float a, int b) {
+    bool recip = b < 0;
+    float r = 1.0f;
+    for (;;) {
+        if (b & 1) r = __fmul_rn(r, a);
+        b /= 2;
+        if (b == 0) break;
+        a = __fmul_rn(a, a);
+    }
+    return recip ? 1.0f / r : r;
+}
+
+__global__ void opt_step_begin_kernel(OptScalars* s, float beta1, float beta2) {
+    int t = s->t + 1;
+    s->t = t;
+    float c1 = __fsub_rn(1.0f, powi_f32(beta1, t));
+    float c2 = __fsub_rn(1.0f, powi_f32(beta2, t));
+    s->inv_c1 = __fdiv_rn(1.0f, c1);
+    s->inv_c2 = __fdiv_rn(1.0f, c2);
+}
+
+// One fused pass per element with the exact rounding sequence of
+// optim.rs:586-593 (no FMA contraction: __fmul_rn / __fadd_rn), 128-bit
+// vector loads where the buffers allow.
+__device__ __forceinline__ float adam_one(float th, float g, float& m, float& v, float b1, float b2, float omb1,
+                                          float omb2, float inv_c1, float inv_c2, float eps, float lr) {
+    m = __fadd_rn(__fmul_rn(m, b1), __fmul_rn(g, omb1));
+    v = __fadd_rn(__fmul_rn(v, b2), __fmul_rn(__fmul_rn(g, g), omb2));
+    float m_hat = __fmul_rn(m, inv_c1);
+    float v_hat = __fmul_rn(v, inv_c2);
+    return __fsub_rn(th, __fmul_rn(__fdiv_rn(m_hat, __fadd_rn(__fsqrt_rn(v_hat), eps)), lr));
+}
+
+__global__ void adam_kernel(OptBatch batch, const OptScalars* __restrict__ sc, float lr, float b1, float b2,
+                            float eps) {
+    const OptTensor& T = batch.t[blockIdx.y];
+    const float inv_c1 = sc->inv_c1, inv_c2 = sc->inv_c2;
+    const float omb1 = __fsub_rn(1.0f, b1), omb2 = __fsub_rn(1.0f, b2);
+    const int64_t n = T.n;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    bool vec = ((reinterpret_cast<uintptr_t>(T.theta) | reinterpret_cast<uintptr_t>(T.g) |
+                 reinterpret_cast<uintptr_t>(T.m) | reinterpret_cast<uintptr_t>(T.v)) & 15) == 0 &&
+               (!T.shadow || (reinterpret_cast<uintptr_t>(T.shadow) & 7) == 0);
+    int64_t nv = vec ? n / 4 : 0;
+    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nv; q += stride) {
+        float4 th = reinterpret_cast<const float4*>(T.theta)[q];
+        float4 g = reinterpret_cast<const float4*>(T.g)[q];
+        float4 m = reinterpret_cast<const float4*>(T.m)[q];
+        float4 v = reinterpret_cast<const float4*>(T.v)[q];
+        th.x = adam_one(th.x, g.x, m.x, v.x, b1, b2, omb1, omb2, inv_c1, inv_c2, eps, lr);
+        th.y = adam_one(th.y, g.y, m.y, v.y, b1, b2, omb1, omb2, inv_c1, inv_c2, eps, lr);
+        th.z = adam_one(th.z, g.z, m.z, v.z, b1, b2, omb1, omb2, inv_c1, inv_c2, eps, lr);
+        th.w = adam_one(th.w, g.w, m.w, v.w, b1, b2, omb1, omb2, inv_c1, inv_c2, eps, lr);
+        reinterpret_cast<float4*>(T.theta)[q] = th;
+        reinterpret_cast<float4*>(T.m)[q] = m;
+        reinterpret_cast<float4*>(T.v)[q] = v;
+        if (T.shadow) {
+            __nv_bfloat162 lo = __floats2bfloat162_rn(th.x, th.y);
+            __nv_bfloat162 hi = __floats2bfloat162_rn(th.z, th.w);
+            uint2 packed;
+            packed.x = *reinterpret_cast<uint32_t*>(&lo);
+            packed.y = *reinterpret_cast<uint32_t*>(&hi);
+            reinterpret_cast<uint2*>(T.shadow)[q] = packed;
+        }
+    }
+    for (int64_t i = nv * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        float m = T.m[i], v = T.v[i];
+        float th = adam_one(T.theta[i], T.g[i], m, v, b1, b2, omb1, omb2, inv_c1, inv_c2, eps, lr);
+        T.theta[i] = th;
+        T.m[i] = m;
+        T.v[i] = v;
+        if (T.shadow) T.shadow[i] = __float2bfloat16_rn(th);
+    }
+}
+
+// optim.rs:486-493: theta -= g * lr.
+__global__ void sgd_kernel(OptBatch batch, float lr) {
+    const OptTensor& T = batch.t[blockIdx.y];
+    const int64_t n = T.n;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    bool vec = ((reinterpret_cast<uintptr_t>(T.theta) | reinterpret_cast<uintptr_t>(T.g)) & 15) == 0 &&
+               (!T.shadow || (reinterpret_cast<uintptr_t>(T.shadow) & 7) == 0);
+    int64_t nv = vec ? n / 4 : 0;
+    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nv; q += stride) {
+        float4 th = reinterpret_cast<const float4*>(T.theta)[q];
+        float4 g = reinterpret_cast<const float4*>(T.g)[q];
+        th.x = __fsub_rn(th.x, __fmul_rn(g.x, lr));
+        th.y = __fsub_rn(th.y, __fmul_rn(g.y, lr));
+        th.z = __fsub_rn(th.z, __fmul_rn(g.z, lr));
+        th.w = __fsub_rn(th.w, __fmul_rn(g.w, lr));
+        reinterpret_cast<float4*>(T.theta)[q] = th;
+        if (T.shadow) {
+            __nv_bfloat162 lo = __floats2bfloat162_rn(th.x, th.y);
+            __nv_bfloat162 hi = __floats2bfloat162_rn(th.z, th.w);
+            uint2 packed;
+            packed.x = *reinterpret_cast<uint32_t*>(&lo);
+            packed.y = *reinterpret_cast<uint32_t*>(&hi);
+            reinterpret_cast<uint2*>(T.shadow)[q] = packed;
+        }
+    }
+    for (int64_t i = nv * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        float th = __fsub_rn(T.theta[i], __fmul_rn(T.g[i], lr));
+        T.theta[i] = th;
+        if (T.shadow) T.shadow[i] = __float2bfloat16_rn(th);
+    }
+}
+
+unsigned grid_for(const rt_ctx* ctx, int64_t work, int per_thread = 1) {
+    int64_t blocks = (work / per_thread + 255) / 256;
+    int64_t cap = (int64_t)ctx->sm_count * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    return (unsigned)blocks;
+}
+
+}  // namespace
+
+int launch_xent(rt_ctx* ctx, const float* logits, int64_t ldz, const uint32_t* labels, int64_t n, int64_t classes,
+                float scale, void* delta, rt_dtype ddt, int64_t ldd, float* loss_rows, cudaStream_t st) {
+    if (n == 0) return RT_OK;
+    unsigned blocks = (unsigned)((n + 7) / 8);
+    if (ddt == RT_BF16)
+        xent_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(logits, ldz, labels, n, classes, scale,
+                                                            (__nv_bfloat16*)delta, ldd, loss_rows);
+    else
+        xent_kernel<float><<<blocks, 256, 0, st>>>(logits, ldz, labels, n, classes, scale, (float*)delta, ldd,
+                                                    loss_rows);
+    count_launch(ctx);
+    RT_CUDA(cudaGetLastError());
+    return RT_OK;
+}
+
+int64_t colsum_scratch_rows(int64_t rows) { return (rows + kColsumChunk - 1) / kColsumChunk; }
+
+int launch_colsum(rt_ctx* ctx, const void* src, rt_dtype dt, int64_t rows, int64_t cols, int64_t ld,
+                  float* scratch, float* dst, cudaStream_t st) {
+    if (cols == 0) return RT_OK;
+    if (rows == 0) {
+        RT_CUDA(cudaMemsetAsync(dst, 0, (size_t)cols * 4, st));
+        return RT_OK;
+    }
+    dim3 block(256);
+    if (rows <= kColsumChunk) {
+        dim3 grid((unsigned)((cols + 255) / 256), 1);
+        if (dt == RT_BF16)
+            colsum_stage_kernel<__nv_bfloat16><<<grid, block, 0, st>>>((const __nv_bfloat16*)src, rows, cols, ld,
+                                                                       rows, dst);
+        else
+            colsum_stage_kernel<float><<<grid, block, 0, st>>>((const float*)src, rows, cols, ld, rows, dst);
+        count_launch(ctx);
+        RT_CUDA(cudaGetLastError());
+        return RT_OK;
+    }
+    int64_t parts = colsum_scratch_rows(rows);
+    if (parts > 65535) return fail(RT_ERR_INVALID, "colsum: %lld rows exceed the two-stage limit", (long long)rows);
+    dim3 grid((unsigned)((cols + 255) / 256), (unsigned)parts);
+    if (dt == RT_BF16)
+        colsum_stage_kernel<__nv_bfloat16><<<grid, block, 0, st>>>((const __nv_bfloat16*)src, rows, cols, ld,
+                                                                   kColsumChunk, scratch);
+    else
+        colsum_stage_kernel<float><<<grid, block, 0, st>>>((const float*)src, rows, cols, ld, kColsumChunk, scratch);
+    dim3 grid2((unsigned)((cols + 255) / 256), 1);
+    colsum_stage_kernel<float><<<grid2, block, 0, st>>>(scratch, parts, cols, cols, parts, dst);
+    count_launch(ctx, 2);
+    RT_CUDA(cudaGetLastError());
+    return RT_OK;
+}
+
+int launch_bias_add(rt_ctx* ctx, void* z, rt_dtype dt, int64_t rows, int64_t cols, int64_t ld, const float* b,
+                    cudaStream_t st) {
+    if (rows * cols == 0) return RT_OK;
+    unsigned g = grid_for(ctx, rows * cols);
+    if (dt == RT_BF16)
+        bias_add_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((__nv_bfloat16*)z, rows, cols, ld, b);
+    else
+        bias_add_kernel<float><<<g, 256, 0, st>>>((float*)z, rows, cols, ld, b);
+    count_launch(ctx);
+    RT_CUDA(cudaGetLastError());
+    return RT_OK;
+}
+
+int launch_relu(rt_ctx* ctx, const void* x, void* y, rt_dtype dt, int64_t rows, int64_t cols, int64_t ldx,
+                int64_t ldy, cudaStream_t st) {
+    if (rows * cols == 0) return RT_OK;
+    unsigned g = grid_for(ctx, rows * cols);
+    if (dt == RT_BF16)
+        relu_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((const __nv_bfloat16*)x, (__nv_bfloat16*)y, rows, cols, ldx,
+                                                      ldy);
+    else
+        relu_kernel<float><<<g, 256, 0, st>>>((const float*)x, (float*)y, rows, cols, ldx, ldy);
+    count_launch(ctx);
+    RT_CUDA(cudaGetLastError());
+    return RT_OK;
+}
+
+int launch_relu_bwd(rt_ctx* ctx, const void* a, void* dz, rt_dtype dt, int64_t rows, int64_t cols, int64_t lda,
+                    int64_t ldz, cudaStream_t st) {
+    if (rows * cols == 0) return RT_OK;
+    unsigned g = grid_for(ctx, rows * cols);
+    if (dt == RT_BF16)
+        relu_bwd_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((const __nv_bfloat16*)a, (__nv_bfloat16*)dz, rows, cols,
+                                                          lda, ldz);
+    else
+        relu_bwd_kernel<float><<<g, 256, 0, st>>>((const float*)a, (float*)dz, rows, cols, lda, ldz);
+    count_launch(ctx);
+    RT_CUDA(cudaGetLastError());
+    return RT_OK;
+}
+
+int launch_cast(rt_ctx* ctx, const void* src, rt_dtype sdt, int64_t lds, void* dst, rt_dtype ddt, int64_t ldd,
+                int64_t rows, int64_t cols, cudaStream_t st) {
+    if (rows * cols == 0) return RT_OK;
+    unsigned g = grid_for(ctx, rows * cols);
+    if (sdt == RT_F32 && ddt == RT_BF16)
+        cast_kernel<float, __nv_bfloat16><<<g, 256, 0, st>>>((const float*)src, lds, (__nv_bfloat16*)dst, ldd, rows,
+                                                             cols);
+    else if (sdt == RT_BF16 && ddt == RT_F32)
+        cast_kernel<__nv_bfloat16, float><<<g, 256, 0, st>>>((const __nv_bfloat16*)src, lds, (float*)dst, ldd, rows,
+                                                             cols);
+    else if (sdt == RT_F32 && ddt == RT_F32)
+        cast_kernel<float, float><<<g, 256, 0, st>>>((const float*)src, lds, (float*)dst, ldd, rows, cols);
+    else if (sdt == RT_BF16 && ddt == RT_BF16)
+        cast_kernel<__nv_bfloat16, __nv_bfloat16><<<g, 256, 0, st>>>((const __nv_bfloat16*)src, lds,
+                                                                     (__nv_bfloat16*)dst, ldd, rows, cols);
+    else
+        return fail(RT_ERR_INVALID, "cast: unsupported dtype pair");
+    count_launch(ctx);
+    RT_CUDA(cudaGetLastError());
+    return RT_OK;
+}
+
+int launch_opt_step_begin(rt_ctx* ctx, OptScalars* s, float beta1, float beta2, cudaStream_t st) {
+    opt_step_begin_kernel<<<1, 1, 0, st>>>(s, beta1, beta2);
+    count_launch(ctx);
+    RT_CUDA(cudaGetLastError());
+    return RT_OK;
+}
+
+static int fill_batch(OptBatch& b, const OptTensor* ts, int count, int64_t& max_n) {
+    if (count < 1 || count > kMaxOptTensors)
+        return fail(RT_ERR_INVALID, "optimizer: %d tensors (1..%d supported per launch)", count, kMaxOptTensors);
+    max_n = 0;
+    for (int i = 0; i < count; ++i) {
+        b.t[i] = ts[i];
+        if (ts[i].n > max_n) max_n = ts[i].n;
+    }
+    b.count = count;
+    return RT_OK;
+}
+
+int launch_adam(rt_ctx* ctx, const OptTensor* ts, int count, const OptScalars* s, float lr, float beta1, float beta2,
+                float eps, cudaStream_t st) {
+    OptBatch b;
+    int64_t max_n;
+    RT_TRY(fill_batch(b, ts, count, max_n));
+    if (max_n == 0) return RT_OK;
+    dim3 grid(grid_for(ctx, max_n, 4), (unsigned)count);
+    adam_kernel<<<grid, 256, 0, st>>>(b, s, lr, beta1, beta2, eps);
+    count_launch(ctx);
+    RT_CUDA(cudaGetLastError());
+    return RT_OK;
+}
+
+int launch_sgd(rt_ctx* ctx, const OptTensor* ts, int count, float lr, cudaStream_t st) {
+    OptBatch b;
+    int64_t max_n;
+    RT_TRY(fill_batch(b, ts, count, max_n));
+    if (max_n == 0) return RT_OK;
+    dim3 grid(grid_for(ctx, max_n, 4), (unsigned)count);
+    sgd_kernel<<<grid, 256, 0, st>>>(b, lr);
+    count_launch(ctx);
+    RT_CUDA(cudaGetLastError());
+    return RT_OK;
+}
+
+}  // namespace rt

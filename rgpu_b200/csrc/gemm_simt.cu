@@ -1,0 +1,273 @@
+// Tiled SIMT GEMM (f32 FMA, f32 accumulate) for every layout and epilogue.
+//
+// This is the counterpart of rtensor's scalar tiled GEMM MM_FAST
+// (crates/rtensor/src/gpu/gemm.rs:65-342: mm / mm_atb / mm_abt) and of its
+// fused epilogue MM_EPILOGO (gemm.rs:372-494), and of the split-K product
+// (splitk.rs:33-237).  On B200 it is the path for operands the tensor-core
+// kernel cannot take (rows not 16-byte aligned, odd leading dimensions) and
+// the exact-f32 reference path when fast GEMM is switched off
+// (Gpu::set_fast_gemm, gpu/mod.rs:442-448).
+//
+// Tile: 128x128 outputs per 256-thread block, 8 outputs x 8 outputs per
+// thread, k depth 8 per stage, register-prefetched double buffer in shared
+// memory.
+#include "internal.h"
+
+namespace rt {
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 8, THREADS = 256;
+
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ void store_out(void* c, int64_t idx, float v);
+template <>
+__device__ __forceinline__ void store_out<float>(void* c, int64_t idx, float v) {
+    static_cast<float*>(c)[idx] = v;
+}
+template <>
+__device__ __forceinline__ void store_out<__nv_bfloat16>(void* c, int64_t idx, float v) {
+    static_cast<__nv_bfloat16*>(c)[idx] = __float2bfloat16_rn(v);
+}
+
+template <typename T>
+__device__ __forceinline__ float load_mask(const void* mask, int64_t idx) {
+    return to_f(static_cast<const T*>(mask)[idx]);
+}
+
+struct SimtParams {
+    const void* a;
+    const void* b;
+    void* c;
+    float* ws;
+    const float* bias;
+    const void* mask;
+    int64_t m, n, k, lda, ldb, ldc, ldmask;
+    int64_t k_per_slice;
+    int epi;
+    int out_bf16;
+};
+
+// Applies the epilogue to one accumulator and stores it.
+template <typename TOut>
+__device__ __forceinline__ void finish(const SimtParams& p, int64_t i, int64_t j, float v) {
+    if (p.epi == RT_EPI_BIAS || p.epi == RT_EPI_BIAS_RELU) v = v + p.bias[j];
+    if (p.epi == RT_EPI_BIAS_RELU) v = fmaxf(v, 0.0f);
+    if (p.epi == RT_EPI_RELU_MASK) v = v * (load_mask<TOut>(p.mask, i * p.ldmask + j) > 0.0f ? 1.0f : 0.0f);
+    store_out<TOut>(p.c, i * p.ldc + j, v);
+}
+
+// A_KMAJOR: A(i,k) = a[i*lda + k], else a[k*lda + i].
+// B_KMAJOR: B(k,j) = b[j*ldb + k], else b[k*ldb + j].
+template <typename TIn, bool A_KMAJOR, bool B_KMAJOR>
+__global__ void __launch_bounds__(THREADS) gemm_simt_kernel(SimtParams p) {
+    __shared__ __align__(16) float As[2][BK][BM];
+    __shared__ __align__(16) float Bs[2][BK][BN];
+
+    const TIn* A = static_cast<const TIn*>(p.a);
+    const TIn* B = static_cast<const TIn*>(p.b);
+    const int tid = threadIdx.x;
+    const int64_t m0 = (int64_t)blockIdx.y * BM;
+    const int64_t n0 = (int64_t)blockIdx.x * BN;
+    const int64_t kbeg = (int64_t)blockIdx.z * p.k_per_slice;
+    const int64_t kend = min(p.k, kbeg + p.k_per_slice);
+
+    // Each thread stages 4 elements of A and 4 of B per k tile.
+    float ra[4], rb[4];
+    auto load_tile = [&](int64_t k0) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            int row, kk;
+            if (A_KMAJOR) {
+                row = tid / BK + q * (THREADS / BK);
+                kk = tid % BK;
+            } else {
+                row = tid % BM;
+                kk = tid / BM + q * (THREADS / BM);
+            }
+            int64_t gi = m0 + row, gk = k0 + kk;
+            float v = 0.0f;
+            if (gi < p.m && gk < kend) v = to_f(A_KMAJOR ? A[gi * p.lda + gk] : A[gk * p.lda + gi]);
+            ra[q] = v;
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            int col, kk;
+            if (B_KMAJOR) {
+                col = tid / BK + q * (THREADS / BK);
+                kk = tid % BK;
+            } else {
+                col = tid % BN;
+                kk = tid / BN + q * (THREADS / BN);
+            }
+            int64_t gj = n0 + col, gk = k0 + kk;
+            float v = 0.0f;
+            if (gj < p.n && gk < kend) v = to_f(B_KMAJOR ? B[gj * p.ldb + gk] : B[gk * p.ldb + gj]);
+            rb[q] = v;
+        }
+    };
+    auto store_tile = [&](int buf) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            int row, kk;
+            if (A_KMAJOR) {
+                row = tid / BK + q * (THREADS / BK);
+                kk = tid % BK;
+            } else {
+                row = tid % BM;
+                kk = tid / BM + q * (THREADS / BM);
+            }
+            As[buf][kk][row] = ra[q];
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            int col, kk;
+            if (B_KMAJOR) {
+                col = tid / BK + q * (THREADS / BK);
+                kk = tid % BK;
+            } else {
+                col = tid % BN;
+                kk = tid / BN + q * (THREADS / BN);
+            }
+            Bs[buf][kk][col] = rb[q];
+        }
+    };
+
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+
+    const int ty = tid / 16, tx = tid % 16;
+    int buf = 0;
+    if (kbeg < kend) {
+        load_tile(kbeg);
+        store_tile(0);
+    }
+    __syncthreads();
+    for (int64_t k0 = kbeg; k0 < kend; k0 += BK) {
+        bool more = k0 + BK < kend;
+        if (more) load_tile(k0 + BK);
+#pragma unroll
+        for (int kk = 0; kk < BK; ++kk) {
+            float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+            float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][64 + ty * 4]);
+            float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
+            float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][64 + tx * 4]);
+            float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        if (more) {
+            store_tile(buf ^ 1);
+            __syncthreads();
+            buf ^= 1;
+        }
+    }
+
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        int64_t gi = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+        if (gi >= p.m) continue;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            int64_t gj = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
+            if (gj >= p.n) continue;
+            if (p.ws) {
+                p.ws[(int64_t)blockIdx.z * p.m * p.n + gi * p.n + gj] = acc[i][j];
+            } else if (p.out_bf16) {
+                finish<__nv_bfloat16>(p, gi, gj, acc[i][j]);
+            } else {
+                finish<float>(p, gi, gj, acc[i][j]);
+            }
+        }
+    }
+}
+
+// Deterministic split-K reduction: slices summed in ascending order, then the
+// epilogue (splitk.rs:240-256 REDUZ, plus bias/ReLU/mask).
+__global__ void splitk_reduce_kernel(SimtParams p, int slices) {
+    int64_t total = p.m * p.n;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        float s = 0.0f;
+        for (int z = 0; z < slices; ++z) s += p.ws[(int64_t)z * total + idx];
+        int64_t i = idx / p.n, j = idx % p.n;
+        if (p.out_bf16)
+            finish<__nv_bfloat16>(p, i, j, s);
+        else
+            finish<float>(p, i, j, s);
+    }
+}
+
+SimtParams make_params(const GemmDesc& g) {
+    SimtParams p;
+    p.a = g.a;
+    p.b = g.b;
+    p.c = g.c;
+    p.ws = g.split_k > 1 ? g.workspace : nullptr;
+    p.bias = g.bias;
+    p.mask = g.mask;
+    p.m = g.m;
+    p.n = g.n;
+    p.k = g.k;
+    p.lda = g.lda;
+    p.ldb = g.ldb;
+    p.ldc = g.ldc;
+    p.ldmask = g.ldmask;
+    int s = g.split_k > 1 ? g.split_k : 1;
+    int64_t kps = (g.k + s - 1) / s;
+    kps = (kps + BK - 1) / BK * BK;
+    p.k_per_slice = kps > 0 ? kps : BK;
+    p.epi = g.epi;
+    p.out_bf16 = g.out_dtype == RT_BF16;
+    return p;
+}
+
+template <typename TIn>
+void launch_typed(const GemmDesc& g, const SimtParams& p, dim3 grid, cudaStream_t st) {
+    switch (g.layout) {
+        case RT_NN: gemm_simt_kernel<TIn, true, false><<<grid, THREADS, 0, st>>>(p); break;
+        case RT_NT: gemm_simt_kernel<TIn, true, true><<<grid, THREADS, 0, st>>>(p); break;
+        case RT_TN: gemm_simt_kernel<TIn, false, false><<<grid, THREADS, 0, st>>>(p); break;
+    }
+}
+
+}  // namespace
+
+int launch_gemm_simt(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream) {
+    if (g.m == 0 || g.n == 0) return RT_OK;
+    SimtParams p = make_params(g);
+    int slices = g.split_k > 1 ? g.split_k : 1;
+    dim3 grid((unsigned)((g.n + BN - 1) / BN), (unsigned)((g.m + BM - 1) / BM), (unsigned)slices);
+    if (grid.y > 65535u) return fail(RT_ERR_INVALID, "GEMM m=%lld too large for the SIMT grid", (long long)g.m);
+    if (g.in_dtype == RT_BF16)
+        launch_typed<__nv_bfloat16>(g, p, grid, stream);
+    else
+        launch_typed<float>(g, p, grid, stream);
+    count_launch(ctx);
+    RT_CUDA(cudaGetLastError());
+    if (slices > 1) return launch_splitk_reduce(ctx, g, stream);
+    return RT_OK;
+}
+
+int launch_splitk_reduce(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream) {
+    SimtParams p = make_params(g);
+    int64_t total = g.m * g.n;
+    int64_t blocks = (total + 255) / 256;
+    int64_t cap = (int64_t)ctx->sm_count * 16;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    splitk_reduce_kernel<<<(unsigned)blocks, 256, 0, stream>>>(p, g.split_k);
+    count_launch(ctx);
+    RT_CUDA(cudaGetLastError());
+    return RT_OK;
+}
+
+}  // namespace rt

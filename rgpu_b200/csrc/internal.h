@@ -1,0 +1,133 @@
+// Internal declarations shared by the translation units of librtgpu.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "rtgpu.h"
+
+namespace rt {
+
+// ------------------------------------------------------------------ errors
+void set_error(const std::string& msg);
+int fail(int code, const char* fmt, ...);
+
+#define RT_CUDA(call)                                                                   \
+    do {                                                                                \
+        cudaError_t e_ = (call);                                                        \
+        if (e_ != cudaSuccess)                                                          \
+            return ::rt::fail(RT_ERR_CUDA, "%s failed: %s (%s:%d)", #call,              \
+                              cudaGetErrorString(e_), __FILE__, __LINE__);              \
+    } while (0)
+
+#define RT_CHECK(cond, ...)                                                             \
+    do {                                                                                \
+        if (!(cond)) return ::rt::fail(RT_ERR_INVALID, __VA_ARGS__);                    \
+    } while (0)
+
+#define RT_TRY(expr)                                                                    \
+    do {                                                                                \
+        int s_ = (expr);                                                                \
+        if (s_ != RT_OK) return s_;                                                     \
+    } while (0)
+
+// Device-side error codes written to ctx->dev_err[0] by kernels whose
+// bounded waits expire (never a trap: the context stays usable).
+enum DevErr : int { DEV_OK = 0, DEV_TIMEOUT_PRODUCER = 1, DEV_TIMEOUT_MMA = 2, DEV_TIMEOUT_EPILOGUE = 3 };
+
+inline size_t dtype_size(rt_dtype d) { return d == RT_BF16 ? 2 : 4; }
+
+}  // namespace rt
+
+struct rt_ctx {
+    int device = 0;
+    int sm_count = 0;
+    int cc_major = 0, cc_minor = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    int* dev_err = nullptr;  // [4] ints: first device error code, detail
+    bool fast_gemm = true;
+    int l2_group = 8;
+    uint64_t launches = 0;
+    char name[256] = {0};
+};
+
+struct rt_tensor {
+    rt_ctx* ctx = nullptr;
+    void* ptr = nullptr;
+    rt_dtype dtype = RT_F32;
+    int rank = 2;
+    int64_t rows = 0, cols = 0, ld = 0;
+    bool owned = false;
+};
+
+namespace rt {
+
+// ------------------------------------------------------------- kernels
+// GEMM problem in "logical" form: C[m,n] = op(A)[m,k] * op(B)[k,n].
+struct GemmDesc {
+    rt_layout layout;
+    rt_dtype in_dtype, out_dtype;
+    int64_t m, n, k;
+    const void* a; int64_t lda;
+    const void* b; int64_t ldb;
+    void* c; int64_t ldc;
+    rt_epilogue epi;
+    const float* bias;
+    const void* mask; int64_t ldmask;
+    int split_k;       // >= 1 after planning
+    float* workspace;  // split_k * m * n f32 when split_k > 1
+};
+
+// Kernel launchers: enqueue on `stream`, return RT_OK or an error code.
+int launch_gemm_simt(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream);
+// tcgen05/TMA GEMM; returns RT_ERR_UNSUPPORTED when the operands do not meet
+// its alignment rules (caller falls back to the SIMT kernel).
+int launch_gemm_tc(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream);
+bool gemm_tc_supported(const rt_ctx* ctx, const GemmDesc& g);
+int launch_splitk_reduce(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream);
+
+int launch_xent(rt_ctx* ctx, const float* logits, int64_t ldz, const uint32_t* labels, int64_t n,
+                int64_t classes, float scale, void* delta, rt_dtype delta_dtype, int64_t ldd,
+                float* loss_rows, cudaStream_t stream);
+int launch_colsum(rt_ctx* ctx, const void* src, rt_dtype dt, int64_t rows, int64_t cols, int64_t ld,
+                  float* scratch, float* dst, cudaStream_t stream);
+int64_t colsum_scratch_rows(int64_t rows);
+int launch_bias_add(rt_ctx* ctx, void* z, rt_dtype dt, int64_t rows, int64_t cols, int64_t ld,
+                    const float* b, cudaStream_t stream);
+int launch_relu(rt_ctx* ctx, const void* x, void* y, rt_dtype dt, int64_t rows, int64_t cols,
+                int64_t ldx, int64_t ldy, cudaStream_t stream);
+int launch_relu_bwd(rt_ctx* ctx, const void* a, void* dz, rt_dtype dt, int64_t rows, int64_t cols,
+                    int64_t lda, int64_t ldz, cudaStream_t stream);
+int launch_cast(rt_ctx* ctx, const void* src, rt_dtype sdt, int64_t lds, void* dst, rt_dtype ddt,
+                int64_t ldd, int64_t rows, int64_t cols, cudaStream_t stream);
+
+// Multi-tensor optimiser.  Each entry updates a packed f32 buffer of n
+// elements (theta, g, m, v) and optionally writes a bf16 shadow copy.
+struct OptTensor {
+    float* theta;
+    const float* g;
+    float* m;
+    float* v;
+    __nv_bfloat16* shadow;  // may be null
+    int64_t shadow_ld;      // row stride of the shadow (elements)
+    int64_t cols;           // row length of theta (for the shadow's stride)
+    int64_t n;
+};
+constexpr int kMaxOptTensors = 16;
+struct OptScalars {       // lives in device memory, written by launch_opt_step_begin
+    int t;
+    float inv_c1, inv_c2;
+    float pad;
+};
+int launch_opt_step_begin(rt_ctx* ctx, OptScalars* s, float beta1, float beta2, cudaStream_t stream);
+int launch_adam(rt_ctx* ctx, const OptTensor* ts, int count, const OptScalars* s, float lr, float beta1,
+                float beta2, float eps, cudaStream_t stream);
+int launch_sgd(rt_ctx* ctx, const OptTensor* ts, int count, float lr, cudaStream_t stream);
+
+inline void count_launch(rt_ctx* ctx, int n = 1) { ctx->launches += (uint64_t)n; }
+
+}  // namespace rt

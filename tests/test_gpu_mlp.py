@@ -1,0 +1,200 @@
+"""Whole-step parity of GpuMlp (the captured CUDA-graph train step) against the
+CPU oracle's tape-driven step, on identical seeded inputs and weights.
+
+Mirrors crates/rtensor/tests/gpu.rs:62-213 and adds the BASELINE configs at
+sizes the oracle finishes in seconds, with the north-star tolerances:
+relative L2 <= 1e-4 per gradient for f32, <= 2e-2 for bf16 operands.
+"""
+import numpy as np
+import pytest
+
+import oracle
+import rgpu_b200
+from tests.helpers import baseline_inputs, erro_rel, glorot_model, quadrant_data, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def gpu():
+    g = rgpu_b200.Gpu(0)
+    yield g
+    g.close()
+
+
+def _one_step_parity(gpu, cpu_model, x, labels, dtype, tol_l2, fast=True, opt="none"):
+    params = cpu_model.params()
+    n = x.shape[0]
+    gpu.set_fast_gemm(fast)
+    try:
+        mlp = rgpu_b200.GpuMlp.from_params(gpu, params, n, 0.0, dtype=dtype, optimizer=opt)
+        gx = gpu.upload(x)
+        gy = rgpu_b200.upload_labels(gpu, labels)
+        mlp.step(gx, gy)
+        loss_gpu = mlp.last_loss()
+        grads_gpu = mlp.grads()
+    finally:
+        gpu.set_fast_gemm(True)
+    loss_cpu = cpu_model.train_step(x, labels)
+    grads_cpu = cpu_model.grads()
+    worst = 0.0
+    for i, (gc, gg) in enumerate(zip(grads_cpu, grads_gpu)):
+        e = rel_l2(gg, gc)
+        worst = max(worst, e)
+        assert e <= tol_l2, f"param {i} ({'W' if i % 2 == 0 else 'b'}{i // 2 + 1}): rel L2 {e:.3e} > {tol_l2}"
+    return loss_cpu, loss_gpu, worst
+
+
+@pytest.mark.parametrize("fast", [True, False])
+def test_gradients_match_cpu(gpu, fast):
+    # gpu.rs:62-97: N=64, D=8, H=16, C=4, Rng::new(42).
+    x, labels = quadrant_data(64, 8)
+    model = glorot_model([8, 16, 16, 4], 42)
+    loss_cpu, loss_gpu, _ = _one_step_parity(gpu, model, x, labels, "f32", 1e-4, fast)
+    assert abs(loss_cpu - loss_gpu) < 1e-4
+    # and the reference's own max-relative metric, 2e-4
+    model2 = glorot_model([8, 16, 16, 4], 42)
+    mlp = rgpu_b200.GpuMlp.from_params(gpu, model2.params(), 64, 0.0, optimizer="none")
+    mlp.step(gpu.upload(x), rgpu_b200.upload_labels(gpu, labels))
+    model2.train_step(x, labels)
+    for gc, gg in zip(model2.grads(), mlp.grads()):
+        assert erro_rel(gc, gg) < 2e-4
+
+
+def test_training_follows_cpu_trajectory(gpu):
+    # gpu.rs:99-139: 120 Adam(0.05) steps; per-step loss within 2e-3, final
+    # weights within 2e-3, converged below 0.15.
+    x, labels = quadrant_data(64, 8)
+    model = glorot_model([8, 16, 16, 4], 7)
+    mlp = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 64, 0.05, optimizer="adam")
+    gx, gy = gpu.upload(x), rgpu_b200.upload_labels(gpu, labels)
+    loss_cpu = None
+    for step in range(1, 121):
+        loss_cpu = model.train_step(x, labels, oracle.OPT_ADAM, 0.05)
+        mlp.step(gx, gy)
+        loss_gpu = mlp.last_loss()
+        assert abs(loss_cpu - loss_gpu) < 2e-3, f"step {step}: CPU {loss_cpu:.6f} GPU {loss_gpu:.6f}"
+    for i, (wc, wg) in enumerate(zip(model.params(), mlp.weights())):
+        assert erro_rel(wc, wg) < 2e-3, f"param {i} diverged"
+    assert loss_cpu < 0.15
+
+
+def test_split_k_training_follows_cpu(gpu):
+    # gpu.rs:145-213: batch 512, 8 -> 128 -> 4, where dW of the output layer
+    # is K-dominant; 60 Adam steps.
+    x, labels = quadrant_data(512, 8)
+    model = glorot_model([8, 128, 4], 7)
+    mlp = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 512, 0.05, optimizer="adam")
+    assert mlp.dispatches_por_passo() > 0
+    gx, gy = gpu.upload(x), rgpu_b200.upload_labels(gpu, labels)
+    loss_cpu = None
+    for step in range(1, 61):
+        loss_cpu = model.train_step(x, labels, oracle.OPT_ADAM, 0.05)
+        mlp.step(gx, gy)
+        assert abs(loss_cpu - mlp.last_loss()) < 2e-3, f"step {step}"
+    for wc, wg in zip(model.params(), mlp.weights()):
+        assert erro_rel(wc, wg) < 2e-3
+    assert loss_cpu < 0.2
+
+
+def test_config1_f32_batch32_sgd(gpu):
+    # 512 -> 1024 -> 1024 -> 10, f32, batch 32, SGD 0.01.
+    dims = [512, 1024, 1024, 10]
+    model, x, labels = baseline_inputs(dims, 32, 2025)
+    _, _, worst = _one_step_parity(gpu, model, x, labels, "f32", 1e-4)
+    # after the SGD update the weights must agree too
+    model, x, labels = baseline_inputs(dims, 32, 2025)
+    mlp = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 32, 0.01, optimizer="sgd")
+    mlp.step(gpu.upload(x), rgpu_b200.upload_labels(gpu, labels))
+    model.train_step(x, labels, oracle.OPT_SGD, 0.01, threads=4)
+    for wc, wg in zip(model.params(), mlp.weights()):
+        assert rel_l2(wg, wc) < 1e-6
+
+
+def test_config2_f32_batch2048(gpu):
+    # same MLP at batch 2048 on one B200, gradients vs CPU.
+    dims = [512, 1024, 1024, 10]
+    model, x, labels = baseline_inputs(dims, 2048, 2026)
+    params = model.params()
+    mlp = rgpu_b200.GpuMlp.from_params(gpu, params, 2048, 0.0, optimizer="none")
+    mlp.step(gpu.upload(x), rgpu_b200.upload_labels(gpu, labels))
+    grads_gpu = mlp.grads()
+    loss_gpu = mlp.last_loss()
+    loss_cpu = model.train_step(x, labels, threads=8)
+    for i, (gc, gg) in enumerate(zip(model.grads(), grads_gpu)):
+        assert rel_l2(gg, gc) <= 1e-4, f"param {i}: {rel_l2(gg, gc):.3e}"
+    assert abs(loss_cpu - loss_gpu) < 1e-4
+
+
+def test_bf16_wide_mlp_reduced_batch(gpu):
+    # BASELINE config 3 architecture (4096 -> 8192 x3 -> 1000) with bf16
+    # operands, f32 accumulate and f32 master weights, at a batch the oracle
+    # finishes in seconds.  Tolerance 2e-2 relative L2 per gradient.
+    dims = [4096, 8192, 8192, 8192, 1000]
+    model, x, labels = baseline_inputs(dims, 64, 2027)
+    params = model.params()
+    mlp = rgpu_b200.GpuMlp.from_params(gpu, params, 64, 0.0, dtype="bf16", optimizer="none")
+    mlp.step(gpu.upload(x), rgpu_b200.upload_labels(gpu, labels))
+    grads_gpu = mlp.grads()
+    del mlp
+    model.train_step(x, labels, threads=8, input_grad=False)
+    for i, (gc, gg) in enumerate(zip(model.grads(), grads_gpu)):
+        assert rel_l2(gg, gc) <= 2e-2, f"param {i}: {rel_l2(gg, gc):.3e}"
+
+
+def test_bf16_adam_step_updates_master_and_shadow(gpu):
+    dims = [256, 512, 512, 100]
+    model, x, labels = baseline_inputs(dims, 256, 2028)
+    mlp = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 256, 1e-3, dtype="bf16", optimizer="adam")
+    gx, gy = gpu.upload(x), rgpu_b200.upload_labels(gpu, labels)
+    for _ in range(5):
+        model.train_step(x, labels, oracle.OPT_ADAM, 1e-3, threads=4)
+        mlp.step(gx, gy)
+    for i, (wc, wg) in enumerate(zip(model.params(), mlp.weights())):
+        assert erro_rel(wc, wg) < 2e-2, f"param {i}"
+    assert abs(model.forward(x, labels) - mlp.last_loss()) < 5e-2
+
+
+def test_host_step_equals_device_step(gpu):
+    x, labels = quadrant_data(64, 8)
+    model = glorot_model([8, 16, 16, 4], 42)
+    a = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 64, 0.05, optimizer="adam")
+    b = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 64, 0.05, optimizer="adam")
+    rows = np.zeros(64, np.float32)
+    for _ in range(3):
+        a.step(gpu.upload(x), rgpu_b200.upload_labels(gpu, labels))
+        b.step_host(x, labels, rows)
+    gpu.sync()
+    for wa, wb in zip(a.weights(), b.weights()):
+        assert np.array_equal(wa, wb)
+    assert abs(float(np.float32(rows.sum()) / 64) - b.last_loss()) < 1e-7
+
+
+def test_forward_only_and_logits(gpu):
+    x, labels = quadrant_data(64, 8)
+    model = glorot_model([8, 16, 16, 4], 3)
+    mlp = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 64, 0.0, optimizer="none")
+    mlp.forward_only(gpu.upload(x))
+    model.forward(x)
+    assert erro_rel(model.logits(64), mlp.logits()) < 1e-5
+
+
+def test_batch_mismatch_is_an_error(gpu):
+    model = glorot_model([8, 16, 4], 3)
+    mlp = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 64, 0.0)
+    x, labels = quadrant_data(32, 8)
+    with pytest.raises(rgpu_b200.RtError):
+        mlp.step(gpu.upload(x), rgpu_b200.upload_labels(gpu, labels))
+
+
+def test_timing_records_every_op(gpu):
+    dims = [512, 1024, 1024, 10]
+    model, x, labels = baseline_inputs(dims, 256, 1)
+    mlp = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 256, 0.01, optimizer="sgd")
+    mlp.enable_timing(True)
+    mlp.step(gpu.upload(x), rgpu_b200.upload_labels(gpu, labels))
+    gpu.sync()
+    ops = mlp.op_times()
+    labels_seen = [o[0] for o in ops]
+    assert labels_seen.count("dw_gemm") == 3 and "softmax_xent" in labels_seen and "sgd" in labels_seen
+    assert all(ms >= 0 for _, _, ms in ops)

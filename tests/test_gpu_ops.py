@@ -1,0 +1,252 @@
+"""Op-level parity of the CUDA kernels against the CPU oracle.
+
+Mirrors crates/rtensor/tests/gpu.rs (round trip, GEMM in every layout on
+ragged shapes, split-K, mixed precision) and adds the kernels the reference
+has only on the CPU (SGD) or that the B200 design fuses (bias/ReLU/mask
+epilogues).  Every call goes through librtgpu.so's C ABI.
+"""
+import numpy as np
+import pytest
+
+import oracle
+import rgpu_b200
+from rgpu_b200 import gpu as G
+from tests.helpers import erro_rel, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+# gpu.rs:250-258: degenerate (1), below a tile (17), one tile (64), just past
+# (65), unaligned (130, 199) and a larger multiple.
+SHAPES = [(1, 1, 1), (17, 33, 65), (64, 64, 64), (65, 64, 63), (130, 96, 80), (199, 130, 71), (256, 512, 128)]
+
+
+@pytest.fixture(scope="module")
+def gpu():
+    g = rgpu_b200.Gpu(0)
+    yield g
+    g.close()
+
+
+def _ab(m, n, k):
+    a = np.sin(np.arange(m * k, dtype=np.float32) * np.float32(0.013)).reshape(m, k).astype(np.float32)
+    b = np.cos(np.arange(k * n, dtype=np.float32) * np.float32(0.007)).reshape(k, n).astype(np.float32)
+    return a, b
+
+
+def test_upload_download_roundtrip(gpu):
+    # gpu.rs:215-221
+    t = (np.arange(15, dtype=np.float32) * 0.5 - 3.0).reshape(3, 5)
+    assert np.array_equal(gpu.download(gpu.upload(t)), t)
+
+
+def test_matmul_37x23x19(gpu):
+    # gpu.rs:223-240
+    a = np.sin(np.arange(37 * 23, dtype=np.float32) * np.float32(0.11)).reshape(37, 23)
+    b = np.cos(np.arange(23 * 19, dtype=np.float32) * np.float32(0.07)).reshape(23, 19)
+    ga, gb, gc = gpu.upload(a), gpu.upload(b), gpu.zeros((37, 19))
+    gpu.matmul(ga, gb, gc)
+    assert erro_rel(oracle.matmul(a, b), gpu.download(gc)) < 1e-5
+
+
+@pytest.mark.parametrize("fast", [False, True])
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_gemm_all_layouts_f32(gpu, fast, m, n, k):
+    # gpu.rs:244-295: all three variants, f32, error < 1e-5 against the CPU.
+    gpu.set_fast_gemm(fast)
+    try:
+        a, b = _ab(m, n, k)
+        want = oracle.matmul(a, b)
+        ga, gb = gpu.upload(a), gpu.upload(b)
+        gat, gbt = gpu.upload(np.ascontiguousarray(a.T)), gpu.upload(np.ascontiguousarray(b.T))
+        c1, c2, c3 = gpu.zeros((m, n)), gpu.zeros((m, n)), gpu.zeros((m, n))
+        gpu.matmul(ga, gb, c1)
+        gpu.matmul_at_b(gat, gb, c2)
+        gpu.matmul_a_bt(ga, gbt, c3)
+        for name, c in (("mm", c1), ("mm_atb", c2), ("mm_abt", c3)):
+            e = erro_rel(want, gpu.download(c))
+            assert e < 1e-5, f"{name} {m}x{n}x{k} fast={fast}: {e:.2e}"
+    finally:
+        gpu.set_fast_gemm(True)
+
+
+@pytest.mark.parametrize("m,n,k", [(64, 64, 64), (256, 128, 512), (512, 512, 256), (200, 136, 72)])
+def test_gemm_bf16_operands(gpu, m, n, k):
+    # gpu.rs:445-503 (f16 there): error < 10 sqrt(K) 2^-8 for bf16's 8-bit mantissa.
+    a, b = _ab(m, n, k)
+    want = oracle.matmul(a, b)
+    bound = 10.0 * np.sqrt(k) * 2.0 ** -8
+    ga, gb = gpu.upload(a, "bf16"), gpu.upload(b, "bf16")
+    gat = gpu.upload(np.ascontiguousarray(a.T), "bf16")
+    gbt = gpu.upload(np.ascontiguousarray(b.T), "bf16")
+    for name, fn, x, y in (("A.B", gpu.matmul, ga, gb), ("At.B", gpu.matmul_at_b, gat, gb),
+                           ("A.Bt", gpu.matmul_a_bt, ga, gbt)):
+        c = gpu.zeros((m, n))
+        fn(x, y, c)
+        e = erro_rel(want, gpu.download(c))
+        assert e < bound, f"{name} {m}x{n}x{k}: {e:.2e} >= {bound:.2e}"
+
+
+def test_bf16_output_store(gpu):
+    a, b = _ab(96, 80, 48)
+    ga, gb = gpu.upload(a, "bf16"), gpu.upload(b, "bf16")
+    c = gpu.zeros((96, 80), "bf16")
+    gpu.matmul(ga, gb, c)
+    got = gpu.download(c)
+    ref = oracle.matmul(rgpu_b200.bf16_to_f32(rgpu_b200.f32_to_bf16(a)),
+                        rgpu_b200.bf16_to_f32(rgpu_b200.f32_to_bf16(b)))
+    assert rel_l2(got, ref) < 4e-3
+
+
+@pytest.mark.parametrize("relu", [False, True])
+def test_matmul_bias_epilogue(gpu, relu):
+    # gemm.rs:372-494 (MM_EPILOGO): C = A B + 1 b, ReLU in registers.
+    m, n, k = 130, 96, 80
+    a, b = _ab(m, n, k)
+    bias = np.linspace(-1, 1, n, dtype=np.float32).reshape(1, n)
+    want = oracle.matmul(a, b) + bias
+    if relu:
+        want = np.maximum(want, 0)
+    c = gpu.zeros((m, n))
+    gpu.matmul_bias(gpu.upload(a), gpu.upload(b), c, gpu.upload(bias), relu)
+    assert erro_rel(want, gpu.download(c)) < 1e-5
+
+
+def test_relu_mask_epilogue_via_rt_gemm(gpu):
+    # kernels.rs:119-131 fused into the dX GEMM: C = (A B^T) * 1[mask > 0].
+    m, n, k = 199, 130, 71
+    a, b = _ab(m, n, k)
+    bt = np.ascontiguousarray(b.T)
+    mask = np.sin(np.arange(m * n, dtype=np.float32) * 0.5).reshape(m, n).astype(np.float32)
+    want = oracle.matmul(a, b) * (mask > 0)
+    ga, gbt, gm = gpu.upload(a), gpu.upload(bt), gpu.upload(mask)
+    c = gpu.zeros((m, n))
+    args = G.GemmArgs(G.RT_NT, G.RT_F32, G.RT_F32, m, n, k, ga.ptr, ga.ld, gbt.ptr, gbt.ld, c.ptr, c.ld,
+                      G.RT_EPI_RELU_MASK, None, gm.ptr, gm.ld, 1, None, 0)
+    gpu.gemm(args)
+    assert erro_rel(want, gpu.download(c)) < 1e-5
+
+
+@pytest.mark.parametrize("m,n,k", [(64, 64, 4096), (32, 96, 2048), (128, 64, 1024)])
+def test_split_k_matches_unsplit(gpu, m, n, k):
+    # gpu.rs:383-430: 1/2/4/8/16 slices, NN and TN, error <= 3x the unsplit GEMM.
+    a, b = _ab(m, n, k)
+    want = oracle.matmul(a, b)
+    ga, gat, gb = gpu.upload(a), gpu.upload(np.ascontiguousarray(a.T)), gpu.upload(b)
+    c0 = gpu.zeros((m, n))
+    gpu.matmul(ga, gb, c0)
+    e0 = erro_rel(want, gpu.download(c0))
+    for slices in (1, 2, 4, 8, 16):
+        for transposed, x in ((False, ga), (True, gat)):
+            c = gpu.zeros((m, n))
+            parts = gpu.zeros((slices * m, n))
+            gpu.split_k(x, gb, c, parts, slices, transposed)
+            e = erro_rel(want, gpu.download(c))
+            assert e < max(3 * e0, 2e-5), f"{m}x{n}x{k} slices={slices} T={transposed}: {e:.2e} vs {e0:.2e}"
+
+
+def test_gemm_empty_and_zero_k(gpu):
+    # k = 0 must give exactly the epilogue of a zero accumulator.
+    a = gpu.zeros((5, 0))
+    b = gpu.zeros((0, 7))
+    c = gpu.upload(np.full((5, 7), 3.0, np.float32))
+    gpu.matmul(a, b, c)
+    assert np.array_equal(gpu.download(c), np.zeros((5, 7), np.float32))
+    e = gpu.zeros((0, 4))
+    gpu.matmul(e, gpu.zeros((4, 3)), gpu.zeros((0, 3)))
+    gpu.sync()
+
+
+def test_shape_mismatch_is_an_error_not_a_crash(gpu):
+    with pytest.raises(rgpu_b200.RtError) as ei:
+        gpu.matmul(gpu.zeros((4, 5)), gpu.zeros((6, 3)), gpu.zeros((4, 3)))
+    assert ei.value.code == G.RT_ERR_INVALID
+
+
+@pytest.mark.parametrize("n,c", [(64, 4), (37, 10), (512, 1000), (3, 1)])
+def test_softmax_xent_matches_oracle(gpu, n, c):
+    # kernels.rs:138-167 vs losses.rs:99-115
+    rng = oracle.Rng(3)
+    z = (rng.normal(n * c) * 3).reshape(n, c)
+    labels = rng.below(c, n)
+    loss_ref, d_ref = oracle.softmax_xent(z, oracle.one_hot(labels, c))
+    gz, gl = gpu.upload(z), rgpu_b200.upload_labels(gpu, labels)
+    d, loss = gpu.zeros((n, c)), gpu.zeros((n,))
+    gpu.softmax_xent(gz, gl, d, loss)
+    rows = gpu.download(loss).ravel()
+    assert abs(float(np.float32(rows.sum()) / n) - loss_ref) < 1e-5 * max(1, abs(loss_ref))
+    assert erro_rel(d_ref, gpu.download(d)) < 1e-6
+
+
+def test_softmax_xent_saturated_logits(gpu):
+    # autodiff.rs:62-72: logits of 100 must stay finite.
+    z = np.array([[1, 2, 3], [100, 100, 100], [1000, -1000, 0]], np.float32)
+    labels = np.array([2, 0, 1], np.uint32)
+    loss_ref, d_ref = oracle.softmax_xent(z, oracle.one_hot(labels, 3))
+    d, loss = gpu.zeros((3, 3)), gpu.zeros((3,))
+    gpu.softmax_xent(gpu.upload(z), rgpu_b200.upload_labels(gpu, labels), d, loss)
+    got = gpu.download(d)
+    assert np.all(np.isfinite(got))
+    assert erro_rel(d_ref, got) < 1e-6
+    assert abs(gpu.download(loss).mean() - loss_ref) < 1e-4
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (32, 10), (64, 130), (65, 7), (2048, 1024), (8192, 33)])
+def test_colsum_matches_reduce_to(gpu, rows, cols):
+    # kernels.rs:182-199 vs tensor.rs:410-418
+    g = oracle.Rng(11).normal(rows * cols).reshape(rows, cols)
+    src, dst = gpu.upload(g), gpu.zeros((1, cols))
+    scratch = gpu.zeros((max(1, (rows + 63) // 64), cols))
+    gpu.colsum(src, dst, scratch)
+    assert erro_rel(oracle.reduce_rows(g), gpu.download(dst)) < 1e-5
+
+
+def test_bias_add_relu_relu_bwd(gpu):
+    rng = oracle.Rng(2)
+    z = rng.normal(50 * 9).reshape(50, 9)
+    b = rng.normal(9).reshape(1, 9)
+    gz = gpu.upload(z)
+    gpu.bias_add(gz, gpu.upload(b))
+    assert np.array_equal(gpu.download(gz), z + b)
+    y = gpu.zeros((50, 9))
+    gpu.relu(gz, y)
+    a = np.maximum(z + b, 0)
+    assert np.array_equal(gpu.download(y), a)
+    dz = rng.normal(50 * 9).reshape(50, 9)
+    gdz = gpu.upload(dz)
+    gpu.relu_bwd(y, gdz)
+    assert np.array_equal(gpu.download(gdz), dz * (a > 0))
+
+
+@pytest.mark.parametrize("n", [1, 7, 1000, 4099])
+def test_adam_is_bit_exact_with_cpu_optimiser(gpu, n):
+    # optim.rs:163-198: same rounding sequence, so equal bit for bit.
+    rng = oracle.Rng(5)
+    theta = rng.normal(n)
+    th_ref, m_ref, v_ref = theta.copy(), np.zeros(n, np.float32), np.zeros(n, np.float32)
+    gt, gm, gv = gpu.upload(theta), gpu.zeros((n,)), gpu.zeros((n,))
+    for t in range(1, 4):
+        g = rng.normal(n)
+        oracle.adam_update(th_ref, m_ref, v_ref, g, 1e-3, t)
+        gpu.adam(gt, gm, gv, gpu.upload(g), 1e-3, t)
+    assert np.array_equal(gpu.download(gt).ravel(), th_ref)
+    assert np.array_equal(gpu.download(gm).ravel(), m_ref)
+    assert np.array_equal(gpu.download(gv).ravel(), v_ref)
+
+
+def test_sgd_is_bit_exact(gpu):
+    rng = oracle.Rng(6)
+    theta = rng.normal(1027)
+    g = rng.normal(1027)
+    ref = theta.copy()
+    oracle.sgd_update(ref, g, 0.01)
+    gt = gpu.upload(theta)
+    gpu.sgd(gt, gpu.upload(g), 0.01)
+    assert np.array_equal(gpu.download(gt).ravel(), ref)
+
+
+def test_cast_rounds_to_nearest_even(gpu):
+    x = oracle.Rng(9).normal(333) * 100
+    src, dst = gpu.upload(x), gpu.zeros((333,), "bf16")
+    gpu.cast(src, dst)
+    want = rgpu_b200.bf16_to_f32(rgpu_b200.f32_to_bf16(x))
+    assert np.array_equal(gpu.download(dst).ravel(), want)
