@@ -1,0 +1,366 @@
+"""Benchmark: train samples/s of the full MLP step (forward + backward + update)
+on 1..8 B200, with the roofline of the dominant kernel and the CPU baseline.
+
+Default workload: the wide MLP
+4096 -> 8192 -> 8192 -> 8192 -> 1000, ReLU, softmax-CE, bf16 operands with f32
+accumulate and f32 master weights, Adam(lr 1e-3), batch 8192 per GPU
+(weak scaling: at 8 GPUs the global batch is 65536, configs[4]).  Synthetic
+seeded data: X ~ N(0,1), labels uniform in [0,1000), Kaiming-uniform W, zero b.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--config wide|small] [--global-batch B]
+
+Multi-GPU: launch one process per GPU with torch.distributed.run; dW/db are
+summed with NCCL inside the captured step (rt_mlp_set_comm).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # wide MLP, bf16/f32-acc, Adam 1e-3, batch 8192 per GPU
+    "wide": dict(dims=[4096, 8192, 8192, 8192, 1000], batch=8192, dtype="bf16", optimizer="adam", lr=1e-3),
+    # 512 -> 1024 -> 1024 -> 10, f32, SGD 0.01, batch 2048
+    "small": dict(dims=[512, 1024, 1024, 10], batch=2048, dtype="f32", optimizer="sgd", lr=0.01),
+}
+CPU_SAMPLE_ROWS = {"wide": 64, "small": 256}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return dict(hbm=d["hbm_gbs"], bf16=d["bf16_tflops"], bf16_sus=d.get("bf16_tflops_sustained"),
+                    source="measured")
+    return dict(hbm=6650.0, bf16=1590.0, bf16_sus=1400.0, source="fallback")
+
+
+def exact_flops(dims, n):
+    """fwd + dW for every layer, dX for every layer but the first."""
+    f = 0
+    for l in range(len(dims) - 1):
+        dm = dims[l] * dims[l + 1]
+        f += 4 * n * dm
+        if l > 0:
+            f += 2 * n * dm
+    return float(f)
+
+
+def make_inputs(cfg, rows, seed):
+    rng = np.random.default_rng(seed)
+    dims = cfg["dims"]
+    params = []
+    for l in range(len(dims) - 1):
+        lim = np.float32(np.sqrt(6.0 / dims[l]))
+        params.append(rng.uniform(-lim, lim, size=(dims[l], dims[l + 1])).astype(np.float32))
+        params.append(np.zeros((1, dims[l + 1]), np.float32))
+    x = rng.standard_normal((rows, dims[0]), dtype=np.float32)
+    labels = rng.integers(0, dims[-1], size=rows, dtype=np.uint32)
+    return params, x, labels
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.dev = device_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            return None
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 7:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline(cfg_name, cfg, warm=1, reps=1, rows=None):
+    """rtensor's CPU train step (oracle restatement) on a bounded sample."""
+    import oracle
+
+    rows = rows or CPU_SAMPLE_ROWS[cfg_name]
+    threads = os.cpu_count() or 1
+    params, x, labels = make_inputs(cfg, rows, 99)
+    m = oracle.Mlp(cfg["dims"])
+    m.set_params(params)
+    opt = oracle.OPT_ADAM if cfg["optimizer"] == "adam" else oracle.OPT_SGD
+    for _ in range(warm):
+        m.train_step(x, labels, opt, cfg["lr"], threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        m.train_step(x, labels, opt, cfg["lr"], threads=threads)
+    dt = (time.perf_counter() - t0) / reps
+    return rows / dt, threads, dt, rows
+
+
+def run_reference(args, cfg_name, cfg, rank):
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    rows = CPU_SAMPLE_ROWS[cfg_name]
+    import oracle  # noqa: F401
+
+    per_step = []
+    params, x, labels = make_inputs(cfg, rows, 99)
+    import oracle as O
+
+    m = O.Mlp(cfg["dims"])
+    m.set_params(params)
+    opt = O.OPT_ADAM if cfg["optimizer"] == "adam" else O.OPT_SGD
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        m.train_step(x, labels, opt, cfg["lr"], threads=cores)
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            per_step.append(dt)
+    sec = sum(per_step) / len(per_step)
+    value = rows / sec
+    line = {
+        "impl": "reference", "metric": "train samples/sec (fwd+bwd+update)", "value": value,
+        "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": config_dict(cfg_name, cfg, args.gpus, cfg["batch"] * args.gpus),
+        "cpu_baseline": {"value": value, "unit": "samples/s", "cores": cores, "kind": "port",
+                         "sample": f"{rows} rows of the {cfg['batch']}-row step per timed step, full model"},
+        "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(cfg_name, cfg, n, global_batch):
+    d = cfg["dims"]
+    return {"workload": ("wide MLP " if cfg_name == "wide" else "MLP ") + "->".join(map(str, d)),
+            "global_batch": global_batch, "batch_per_gpu": global_batch // n, "dtype_policy":
+            "bf16 operands, f32 accumulate, f32 master weights" if cfg["dtype"] == "bf16" else "f32",
+            "optimizer": f"{cfg['optimizer']}(lr={cfg['lr']})", "parallelism": f"dp{n}",
+            "l2": "inputs larger than L2 (each step streams several GB)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="wide", choices=sorted(CONFIGS))
+    ap.add_argument("--global-batch", type=int, default=0, help="strong scaling: fixed global batch")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference(args, args.config, cfg, rank)
+        return
+
+    import torch
+
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    import rgpu_b200
+
+    if args.global_batch:
+        batch = args.global_batch // world
+        scaling = "strong"
+    else:
+        batch = cfg["batch"]
+        scaling = "weak"
+    global_batch = batch * world
+    dims = cfg["dims"]
+
+    gpu = rgpu_b200.Gpu(local)
+    params, x, labels = make_inputs(cfg, batch, 1234 + rank)
+    mlp = rgpu_b200.GpuMlp.from_params(gpu, params, batch, cfg["lr"], dtype=cfg["dtype"],
+                                       optimizer=cfg["optimizer"], global_batch=global_batch)
+    del params
+    comm = None
+    if world > 1:
+        uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(rgpu_b200.Comm.unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        comm = rgpu_b200.Comm(gpu, rank, world, bytes(uid.cpu().numpy().tobytes()))
+        mlp.set_comm(comm)
+
+    # inputs: device copy (value) and pinned host copy (e2e)
+    x_dtype = cfg["dtype"]
+    if x_dtype == "bf16":
+        xh = rgpu_b200.f32_to_bf16(x)
+    else:
+        xh = x
+    x_dev = torch.from_numpy(xh.view(np.int16) if x_dtype == "bf16" else xh).cuda(local)
+    lab_dev = torch.from_numpy(labels.view(np.int32)).cuda(local)
+    x_pin = torch.from_numpy(xh.view(np.int16) if x_dtype == "bf16" else xh).pin_memory()
+    lab_pin = torch.from_numpy(labels.view(np.int32)).pin_memory()
+    loss_pin = torch.zeros(batch, dtype=torch.float32).pin_memory()
+    torch.cuda.synchronize()
+    stream = torch.cuda.ExternalStream(gpu.stream(), device=torch.device("cuda", local))
+
+    def step_dev():
+        mlp.step_ptr(x_dev.data_ptr(), x_dtype, lab_dev.data_ptr())
+
+    def step_host():
+        mlp.step_host_ptr(x_pin.data_ptr(), x_dtype, lab_pin.data_ptr(), loss_pin.data_ptr())
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        gpu.sync()
+        torch.cuda.synchronize()
+
+    def timed(fn, k):
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(k):
+            fn()
+        e1.record(stream)
+        gpu.sync()
+        ms = e0.elapsed_time(e1)
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        if dist:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        barrier()
+        return float(t.item())
+
+    mlp.enable_timing(True)
+    for _ in range(args.warmup):
+        step_dev()
+    gpu.sync()
+
+    # ---- timed region: device-resident inputs
+    clocks = ClockSampler(local)
+    clocks.start()
+    launches0 = gpu.launch_count()
+    ms = timed(step_dev, args.steps)
+    launches = gpu.launch_count() - launches0
+    clk = clocks.stop()
+    ops = mlp.op_times()  # the last timed step's per-kernel device times
+
+    # ---- end-to-end: host buffers, H2D + D2H inside the timed region
+    for _ in range(2):
+        step_host()
+    gpu.sync()
+    ms_e2e = timed(step_host, args.steps)
+
+    ms_step = ms / args.steps
+    value = global_batch / (ms_step / 1e3)
+    e2e_value = global_batch / (ms_e2e / args.steps / 1e3)
+    pk = peaks()
+    step_flops = exact_flops(dims, batch)
+    # dominant kernel: the GEMM label with the largest total time in the step
+    by_label = {}
+    for lab, fl, t in ops:
+        a = by_label.setdefault(lab, [0.0, 0.0, 0])
+        a[0] += fl
+        a[1] += t
+        a[2] += 1
+    dom = max(by_label.items(), key=lambda kv: kv[1][1]) if by_label else None
+    roof = None
+    if dom:
+        lab, (fl, t, cnt) = dom
+        ach = fl / (t / 1e3) / 1e12 if t > 0 else 0.0
+        peak = pk["bf16"] if cfg["dtype"] == "bf16" else 75.0
+        roof = {"bound": "tensor", "kernel": lab, "launches_per_step": cnt, "achieved": ach, "peak": peak,
+                "unit": "TFLOP/s", "frac": ach / peak, "traffic": None,
+                "peak_source": pk["source"] + (" bf16 dense (cuBLAS burst)" if cfg["dtype"] == "bf16"
+                                               else " f32 SIMT nominal")}
+    gemm_t = sum(t for lab, fl, t in ops if fl > 0)
+    gemm_f = sum(fl for lab, fl, t in ops if fl > 0)
+    step_tflops = step_flops / (ms_step / 1e3) / 1e12
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            try:
+                v, cores, dt, rows = cpu_baseline(args.config, cfg)
+                cpu = {"value": v, "unit": "samples/s", "cores": cores, "kind": "port",
+                       "sample": f"{rows} rows of the {batch}-row step, full model, {dt:.1f} s/step"}
+            except Exception as e:  # the baseline must not hide the GPU line
+                cpu = {"value": None, "unit": "samples/s", "cores": os.cpu_count(), "kind": "port",
+                       "sample": f"failed: {e}"}
+        in_bytes = xh.nbytes + labels.nbytes
+        line = {
+            "metric": "train samples/sec (fwd+bwd+update)", "value": value, "unit": "samples/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": cfg["dtype"],
+            "data": "synthetic (seeded N(0,1) inputs, uniform labels, Kaiming-uniform weights)",
+            "config": config_dict(args.config, cfg, world, global_batch),
+            "roofline": roof,
+            "step_tensor_frac": {"achieved_tflops": step_tflops, "peak": pk["bf16"], "frac": step_tflops / pk["bf16"],
+                                 "flops_per_step_per_gpu": step_flops,
+                                 "gemm_tflops": gemm_f / (gemm_t / 1e3) / 1e12 if gemm_t > 0 else None},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "samples/s", "h2d_bytes_per_step": in_bytes,
+                    "d2h_bytes_per_step": batch * 4},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+            "kernels_last_step": [{"label": lab, "ms": round(t, 4), "tflops": round(fl / (t / 1e3) / 1e12, 1) if fl and t
+                                   else None} for lab, fl, t in ops],
+        }
+        print(json.dumps(line), flush=True)
+
+    mlp.close()
+    if comm:
+        comm.close()
+    gpu.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

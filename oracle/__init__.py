@@ -66,6 +66,7 @@ def lib():
         L.or_mlp_train_step.restype = C.c_float
         L.or_mlp_train_step.argtypes = [C.c_void_p, _f32p, _u32p, C.c_size_t, C.c_int,
                                         C.c_float, C.c_int, C.c_int]
+        L.or_mlp_set_bf16_emulation.argtypes = [C.c_void_p, C.c_int]
         L.or_mlp_forward.restype = C.c_float
         L.or_mlp_forward.argtypes = [C.c_void_p, _f32p, _u32p, C.c_size_t, C.c_int]
         L.or_adam_update.argtypes = [_f32p, _f32p, _f32p, _f32p, C.c_size_t, C.c_float,
@@ -191,6 +192,11 @@ class Mlp:
         if getattr(self, "_h", None):
             lib().or_mlp_free(self._h)
             self._h = None
+
+    def set_bf16_emulation(self, on: bool = True):
+        """Round at the bf16 GPU plan's storage points (test-only option, not
+        the reference algorithm; see rtensor_cpu.h)."""
+        lib().or_mlp_set_bf16_emulation(self._h, int(bool(on)))
 
     def init_glorot(self, rng: Rng):
         lib().or_mlp_init_glorot(self._h, C.byref(rng.state))

@@ -48,6 +48,19 @@ inline float powi_f32(float a, int b) {
     return recip ? 1.0f / r : r;
 }
 
+// Round an f32 to the nearest bf16 (ties to even) and widen it back.
+inline float round_bf16(float f) {
+    uint32_t b;
+    std::memcpy(&b, &f, 4);
+    b = (b + (((b >> 16) & 1u) + 0x7FFFu)) & 0xFFFF0000u;
+    float r;
+    std::memcpy(&r, &b, 4);
+    return r;
+}
+inline void round_bf16(std::vector<float>& v) {
+    for (auto& x : v) x = round_bf16(x);
+}
+
 // ---------------------------------------------------------------- matmul
 // Rows [r0, r1) of C = A B, ikj order (tensor.rs:318-373).
 void matmul_rows(const float* a, const float* b, float* c, size_t r0, size_t r1, size_t k, size_t n) {
@@ -227,6 +240,8 @@ struct or_mlp {
     std::vector<std::vector<float>> act;  // act[0] = x, act[l+1] = output of layer l
     size_t n = 0;
     int t = 0;
+    bool bf16 = false;
+    std::vector<std::vector<float>> Wq;  // bf16-rounded weights (bf16 emulation)
 };
 
 extern "C" {
@@ -287,22 +302,36 @@ void or_mlp_init_kaiming(or_mlp* m, uint64_t* s) {
 // Sequential::forward (nn.rs:179-181) of Dense layers (nn.rs:143-149):
 // Z = x.matmul(W).add(b) (zip with b tiled over rows, tensor.rs:196-200),
 // then relu (ops.rs:190-194) on hidden layers; the last layer is Linear.
+static const float* gemm_weights(or_mlp* m, int l) { return m->bf16 ? m->Wq[l].data() : m->W[l].data(); }
+
 static void forward_impl(or_mlp* m, const float* x, size_t n, int threads) {
     m->n = n;
     m->act.resize(m->L + 1);
     m->act[0].assign(x, x + n * m->dims[0]);
+    if (m->bf16) {
+        round_bf16(m->act[0]);
+        m->Wq.resize(m->L);
+        for (int l = 0; l < m->L; ++l) {
+            m->Wq[l] = m->W[l];
+            round_bf16(m->Wq[l]);
+        }
+    }
     for (int l = 0; l < m->L; ++l) {
         size_t d = m->dims[l], u = m->dims[l + 1];
         auto& out = m->act[l + 1];
         out.resize(n * u);
-        matmul(m->act[l].data(), m->W[l].data(), out.data(), n, d, u, threads);
+        matmul(m->act[l].data(), gemm_weights(m, l), out.data(), n, d, u, threads);
         const float* bb = m->b[l].data();
         for (size_t i = 0; i < n; ++i)
             for (size_t j = 0; j < u; ++j) out[i * u + j] = out[i * u + j] + bb[j];
-        if (l + 1 < m->L)
+        if (l + 1 < m->L) {
             for (auto& v : out) v = std::fmax(v, 0.0f);
+            if (m->bf16) round_bf16(out);
+        }
     }
 }
+
+void or_mlp_set_bf16_emulation(or_mlp* m, int on) { m->bf16 = on != 0; }
 
 float or_mlp_forward(or_mlp* m, const float* x, const uint32_t* labels, size_t n, int threads) {
     forward_impl(m, x, n, threads);
@@ -330,6 +359,7 @@ float or_mlp_train_step(or_mlp* m, const float* x, const uint32_t* labels, size_
     or_one_hot(labels, n, c, y.data());
     std::vector<float> g(n * c);
     float loss = softmax_xent(m->act[L].data(), y.data(), n, c, g.data());
+    if (m->bf16) round_bf16(g);
 
     std::vector<float> wt, at, gin;
     for (int l = L - 1; l >= 0; --l) {
@@ -338,6 +368,7 @@ float or_mlp_train_step(or_mlp* m, const float* x, const uint32_t* labels, size_
             // relu node of layer l: mask from the relu input; A > 0 <=> Z > 0.
             const auto& a = m->act[l + 1];
             for (size_t i = 0; i < n * u; ++i) g[i] = g[i] * (a[i] > 0.0f ? 1.0f : 0.0f);
+            if (m->bf16) round_bf16(g);
         }
         // add node: adjoint of b.
         reduce_rows(g.data(), m->db[l].data(), n, u);
@@ -345,7 +376,7 @@ float or_mlp_train_step(or_mlp* m, const float* x, const uint32_t* labels, size_
         bool need_dx = (l > 0) || input_grad;
         if (need_dx) {
             wt.resize(u * d);
-            transpose(m->W[l].data(), wt.data(), d, u);
+            transpose(gemm_weights(m, l), wt.data(), d, u);
             gin.resize(n * d);
             matmul(g.data(), wt.data(), gin.data(), n, u, d, threads);
         }

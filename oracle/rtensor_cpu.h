@@ -86,6 +86,16 @@ enum { OR_OPT_NONE = 0, OR_OPT_SGD = 1, OR_OPT_ADAM = 2 };
  * computes the adjoint of x, which the tape always does (ops.rs:128). */
 float or_mlp_train_step(or_mlp* m, const float* x, const uint32_t* labels, size_t n,
                         int optimizer, float lr, int threads, int input_grad);
+/* bf16 emulation (NOT part of the reference algorithm; test-only): when on,
+ * the step rounds to bf16 (nearest even) exactly where the bf16 GPU plan
+ * stores bf16 -- the input x, the weights used by the GEMMs (the f32 master
+ * copy is what the optimiser updates), every hidden activation after
+ * bias+ReLU, and every adjoint delta_l before it feeds a GEMM or the bias
+ * reduction.  Arithmetic between those points stays f32, in the reference's
+ * loop order.  This isolates the bf16 kernels' arithmetic from the rounding
+ * policy itself; with it off the oracle is the plain reference. */
+void or_mlp_set_bf16_emulation(or_mlp* m, int on);
+
 /* Forward only (Sequential::predict, nn.rs:184-188); returns the loss of the
  * logits against the labels when labels != NULL. */
 float or_mlp_forward(or_mlp* m, const float* x, const uint32_t* labels, size_t n, int threads);

@@ -88,6 +88,7 @@ int launch_gemm_simt(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream);
 // its alignment rules (caller falls back to the SIMT kernel).
 int launch_gemm_tc(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream);
 bool gemm_tc_supported(const rt_ctx* ctx, const GemmDesc& g);
+int gemm_tc_init(rt_ctx* ctx);
 int launch_splitk_reduce(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream);
 
 int launch_xent(rt_ctx* ctx, const float* logits, int64_t ldz, const uint32_t* labels, int64_t n,

@@ -79,6 +79,13 @@ int rt_ctx_create(int device, rt_ctx** out) {
     }
     cudaMemset(c->dev_err, 0, 4 * sizeof(int));
     c->stream = c->own_stream;
+    int st = gemm_tc_init(c);
+    if (st != RT_OK) {
+        cudaFree(c->dev_err);
+        cudaStreamDestroy(c->own_stream);
+        delete c;
+        return st;
+    }
     *out = c;
     return RT_OK;
 }

@@ -195,7 +195,11 @@ class GpuTensor:
 
     def free(self):
         if self.handle and self.handle.value:
-            lib().rt_tensor_free(self.handle)
+            # A tensor outliving its context is released with the context's
+            # device memory; freeing it after rt_ctx_destroy would touch a
+            # destroyed context.
+            if self.gpu.alive():
+                lib().rt_tensor_free(self.handle)
             self.handle = C.c_void_p(0)
 
     def __del__(self):
@@ -214,8 +218,11 @@ class Gpu:
         self.handle = h
         self.device = device
 
+    def alive(self) -> bool:
+        return bool(self.handle and self.handle.value)
+
     def close(self):
-        if self.handle and self.handle.value:
+        if self.alive():
             lib().rt_ctx_destroy(self.handle)
             self.handle = C.c_void_p(0)
 
@@ -358,7 +365,7 @@ class Comm:
         _check(lib().rt_comm_allreduce_f32(self.handle, dev_ptr, count))
 
     def close(self):
-        if self.handle and self.handle.value:
+        if self.handle and self.handle.value and self.gpu.alive():
             lib().rt_comm_destroy(self.handle)
             self.handle = C.c_void_p(0)
 
@@ -403,7 +410,7 @@ class GpuMlp:
         return m
 
     def close(self):
-        if self.handle and self.handle.value:
+        if self.handle and self.handle.value and self.gpu.alive():
             lib().rt_mlp_destroy(self.handle)
             self.handle = C.c_void_p(0)
 

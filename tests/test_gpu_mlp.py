@@ -129,17 +129,33 @@ def test_config2_f32_batch2048(gpu):
 def test_bf16_wide_mlp_reduced_batch(gpu):
     # BASELINE config 3 architecture (4096 -> 8192 x3 -> 1000) with bf16
     # operands, f32 accumulate and f32 master weights, at a batch the oracle
-    # finishes in seconds.  Tolerance 2e-2 relative L2 per gradient.
+    # finishes in seconds.
     dims = [4096, 8192, 8192, 8192, 1000]
     model, x, labels = baseline_inputs(dims, 64, 2027)
     params = model.params()
     mlp = rgpu_b200.GpuMlp.from_params(gpu, params, 64, 0.0, dtype="bf16", optimizer="none")
     mlp.step(gpu.upload(x), rgpu_b200.upload_labels(gpu, labels))
     grads_gpu = mlp.grads()
-    del mlp
+    mlp.close()
+    # (1) The kernels' arithmetic: against the oracle rounding to bf16 at the
+    # same storage points, every gradient within 2e-2 relative L2.
+    model.set_bf16_emulation(True)
     model.train_step(x, labels, threads=8, input_grad=False)
     for i, (gc, gg) in enumerate(zip(model.grads(), grads_gpu)):
-        assert rel_l2(gg, gc) <= 2e-2, f"param {i}: {rel_l2(gg, gc):.3e}"
+        assert rel_l2(gg, gc) <= 2e-2, f"param {i} vs bf16-emulating oracle: {rel_l2(gg, gc):.3e}"
+    # (2) Against the plain f32 reference: the output layer (no ReLU mask in
+    # its path) within 2e-2; hidden layers differ by ReLU masks that flip where
+    # bf16 operand rounding moves a pre-activation across zero, so they are
+    # held to direction (cosine >= 0.99) instead.
+    model.set_bf16_emulation(False)
+    model.train_step(x, labels, threads=8, input_grad=False)
+    gref = model.grads()
+    for i in (len(gref) - 2, len(gref) - 1):
+        assert rel_l2(grads_gpu[i], gref[i]) <= 2e-2, f"output param {i}: {rel_l2(grads_gpu[i], gref[i]):.3e}"
+    for i, (gc, gg) in enumerate(zip(gref, grads_gpu)):
+        a, b = gg.ravel().astype(np.float64), gc.ravel().astype(np.float64)
+        cos = float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+        assert cos >= 0.99, f"param {i}: cosine {cos:.4f}"
 
 
 def test_bf16_adam_step_updates_master_and_shadow(gpu):
@@ -147,12 +163,15 @@ def test_bf16_adam_step_updates_master_and_shadow(gpu):
     model, x, labels = baseline_inputs(dims, 256, 2028)
     mlp = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 256, 1e-3, dtype="bf16", optimizer="adam")
     gx, gy = gpu.upload(x), rgpu_b200.upload_labels(gpu, labels)
+    model.set_bf16_emulation(True)
+    loss_cpu = None
     for _ in range(5):
-        model.train_step(x, labels, oracle.OPT_ADAM, 1e-3, threads=4)
+        loss_cpu = model.train_step(x, labels, oracle.OPT_ADAM, 1e-3, threads=4)
         mlp.step(gx, gy)
     for i, (wc, wg) in enumerate(zip(model.params(), mlp.weights())):
         assert erro_rel(wc, wg) < 2e-2, f"param {i}"
-    assert abs(model.forward(x, labels) - mlp.last_loss()) < 5e-2
+    # loss of the 5th step's forward pass (before its update) on both sides
+    assert abs(loss_cpu - mlp.last_loss()) < 2e-2
 
 
 def test_host_step_equals_device_step(gpu):
@@ -167,7 +186,10 @@ def test_host_step_equals_device_step(gpu):
     gpu.sync()
     for wa, wb in zip(a.weights(), b.weights()):
         assert np.array_equal(wa, wb)
-    assert abs(float(np.float32(rows.sum()) / 64) - b.last_loss()) < 1e-7
+    seq = np.float32(0.0)
+    for v in rows:  # mean_all's sequential f32 sum (tensor.rs:279-286)
+        seq = np.float32(seq + v)
+    assert float(seq / np.float32(64)) == b.last_loss()
 
 
 def test_forward_only_and_logits(gpu):

@@ -197,7 +197,12 @@ def test_colsum_matches_reduce_to(gpu, rows, cols):
     src, dst = gpu.upload(g), gpu.zeros((1, cols))
     scratch = gpu.zeros((max(1, (rows + 63) // 64), cols))
     gpu.colsum(src, dst, scratch)
-    assert erro_rel(oracle.reduce_rows(g), gpu.download(dst)) < 1e-5
+    # Both sums round differently (64-row chunks vs one sequential sweep); the
+    # GPU's must be at least about as close to the exact sum as the CPU's.
+    exact = g.astype(np.float64).sum(0, keepdims=True)
+    e_cpu = erro_rel(exact, oracle.reduce_rows(g))
+    e_gpu = erro_rel(exact, gpu.download(dst))
+    assert e_gpu <= 2 * e_cpu + 1e-6, (e_gpu, e_cpu)
 
 
 def test_bias_add_relu_relu_bwd(gpu):
