@@ -126,36 +126,62 @@ def test_config2_f32_batch2048(gpu):
     assert abs(loss_cpu - loss_gpu) < 1e-4
 
 
+def _wide_bf16_grads(gpu, dims, n, seed, fast):
+    model, x, labels = baseline_inputs(dims, n, seed)
+    gpu.set_fast_gemm(fast)
+    try:
+        mlp = rgpu_b200.GpuMlp.from_params(gpu, model.params(), n, 0.0, dtype="bf16", optimizer="none")
+        mlp.step(gpu.upload(x), rgpu_b200.upload_labels(gpu, labels))
+        grads = mlp.grads()
+        mlp.close()
+    finally:
+        gpu.set_fast_gemm(True)
+    return model, x, labels, grads
+
+
+def test_bf16_step_logic_matches_bf16_oracle_exactly(gpu):
+    # The bf16 plan's rounding points (x, W shadow, activations, deltas) and
+    # step logic, isolated from accumulation order: the SIMT kernels sum k in
+    # the oracle's order and bf16 x bf16 products are exact in f32, so the
+    # only differences left are the xent's lane-parallel sums.
+    dims = [512, 1024, 1024, 1024, 100]
+    model, x, labels, grads = _wide_bf16_grads(gpu, dims, 256, 2027, fast=False)
+    model.set_bf16_emulation(True)
+    model.train_step(x, labels, threads=8, input_grad=False)
+    for i, (gc, gg) in enumerate(zip(model.grads(), grads)):
+        assert rel_l2(gg, gc) <= 1e-3, f"param {i}: {rel_l2(gg, gc):.3e}"
+
+
 def test_bf16_wide_mlp_reduced_batch(gpu):
     # BASELINE config 3 architecture (4096 -> 8192 x3 -> 1000) with bf16
-    # operands, f32 accumulate and f32 master weights, at a batch the oracle
-    # finishes in seconds.
+    # operands on the tensor-core path, f32 accumulate, f32 master weights, at
+    # a batch the oracle finishes in seconds.
+    #
+    # The tensor cores sum k in another order (and truncate), so each layer's
+    # output differs from the oracle's by ~1e-5 relative; bf16 rounding of the
+    # activations turns that into independent rounding noise (~2^-9), and
+    # hidden-layer gradients pick up ReLU-mask flips from it.  Measured on
+    # B200: output layer 1.6e-3 / 5e-4, hidden layers 2.1e-2 .. 2.5e-2 against
+    # the bf16-point oracle; 4.4e-3 (output) and 4.7e-2 .. 7.9e-2 (hidden)
+    # against the plain f32 reference.
     dims = [4096, 8192, 8192, 8192, 1000]
-    model, x, labels = baseline_inputs(dims, 64, 2027)
-    params = model.params()
-    mlp = rgpu_b200.GpuMlp.from_params(gpu, params, 64, 0.0, dtype="bf16", optimizer="none")
-    mlp.step(gpu.upload(x), rgpu_b200.upload_labels(gpu, labels))
-    grads_gpu = mlp.grads()
-    mlp.close()
-    # (1) The kernels' arithmetic: against the oracle rounding to bf16 at the
-    # same storage points, every gradient within 2e-2 relative L2.
+    model, x, labels, grads_gpu = _wide_bf16_grads(gpu, dims, 64, 2027, fast=True)
+    L = len(grads_gpu)
     model.set_bf16_emulation(True)
     model.train_step(x, labels, threads=8, input_grad=False)
     for i, (gc, gg) in enumerate(zip(model.grads(), grads_gpu)):
-        assert rel_l2(gg, gc) <= 2e-2, f"param {i} vs bf16-emulating oracle: {rel_l2(gg, gc):.3e}"
-    # (2) Against the plain f32 reference: the output layer (no ReLU mask in
-    # its path) within 2e-2; hidden layers differ by ReLU masks that flip where
-    # bf16 operand rounding moves a pre-activation across zero, so they are
-    # held to direction (cosine >= 0.99) instead.
+        bound = 2e-2 if i >= L - 2 else 4e-2
+        assert rel_l2(gg, gc) <= bound, f"param {i} vs bf16-point oracle: {rel_l2(gg, gc):.3e} > {bound}"
     model.set_bf16_emulation(False)
     model.train_step(x, labels, threads=8, input_grad=False)
     gref = model.grads()
-    for i in (len(gref) - 2, len(gref) - 1):
+    for i in (L - 2, L - 1):
         assert rel_l2(grads_gpu[i], gref[i]) <= 2e-2, f"output param {i}: {rel_l2(grads_gpu[i], gref[i]):.3e}"
     for i, (gc, gg) in enumerate(zip(gref, grads_gpu)):
         a, b = gg.ravel().astype(np.float64), gc.ravel().astype(np.float64)
         cos = float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
         assert cos >= 0.99, f"param {i}: cosine {cos:.4f}"
+        assert rel_l2(gg, gc) <= 0.12, f"param {i} vs f32: {rel_l2(gg, gc):.3e}"
 
 
 def test_bf16_adam_step_updates_master_and_shadow(gpu):
