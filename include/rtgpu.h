@@ -125,6 +125,20 @@ int rt_matmul_split_k(rt_ctx* ctx, const rt_tensor* a, const rt_tensor* b, rt_te
  * 64x64 blocks, at least 4 16-deep k tiles per slice. */
 int rt_split_k_suggest(int64_t m, int64_t n, int64_t k);
 int64_t rt_split_k_workspace(int64_t m, int64_t n, int slices);
+/* No counterpart in the reference.  The same split-K GEMM as
+ * rt_matmul_split_k, for callers that cannot allocate device memory when they
+ * call (inside a CUDA graph capture, under a host runtime whose allocator
+ * owns the device memory, in loops that forbid allocation after start-up):
+ * the partial sums live in a fixed 16 MiB array built into the library
+ * (rt_split_k_static_capacity() floats per device, held until the process
+ * exits).  Calls needing slices*m*n above that capacity fail with
+ * RT_ERR_INVALID.  All calls on a device share the array, so calls whose
+ * kernels overlap on the GPU race and must be serialised; the first call on
+ * a device looks up the array's device address and should happen outside
+ * any stream capture. */
+int rt_matmul_split_k_noalloc(rt_ctx* ctx, const rt_tensor* a, const rt_tensor* b, rt_tensor* c,
+                              int slices, int transposed);
+int64_t rt_split_k_static_capacity(void);
 
 /* Full-control GEMM used by the plan (and by Rust callers that manage their
  * own buffers).  Logical A is [m,k], logical B is [k,n]:

@@ -88,6 +88,8 @@ _SIGS = [
     ("rt_matmul_a_bt", C.c_int, [C.c_void_p] * 4),
     ("rt_matmul_bias", C.c_int, [C.c_void_p] * 5 + [C.c_int]),
     ("rt_matmul_split_k", C.c_int, [C.c_void_p] * 5 + [C.c_int, C.c_int]),
+    ("rt_matmul_split_k_noalloc", C.c_int, [C.c_void_p] * 4 + [C.c_int, C.c_int]),
+    ("rt_split_k_static_capacity", C.c_int64, []),
     ("rt_split_k_suggest", C.c_int, [C.c_int64, C.c_int64, C.c_int64]),
     ("rt_split_k_workspace", C.c_int64, [C.c_int64, C.c_int64, C.c_int]),
     ("rt_gemm", C.c_int, [C.c_void_p, C.POINTER(GemmArgs)]),
@@ -299,6 +301,17 @@ class Gpu:
     def split_k(self, a, b, c, partials, slices: int, transposed: bool):
         _check(lib().rt_matmul_split_k(self.handle, a.handle, b.handle, c.handle, partials.handle, slices,
                                        int(transposed)))
+
+    def split_k_noalloc(self, a, b, c, slices: int, transposed: bool):
+        """Split-K GEMM with the partial sums in the library's built-in scratch
+        array: no device allocation, for callers that may not allocate (e.g.
+        during CUDA graph capture).  Calls overlapping on the GPU race on the
+        shared scratch; slices*m*n must fit split_k_static_capacity()."""
+        _check(lib().rt_matmul_split_k_noalloc(self.handle, a.handle, b.handle, c.handle, slices, int(transposed)))
+
+    @staticmethod
+    def split_k_static_capacity() -> int:
+        return lib().rt_split_k_static_capacity()
 
     @staticmethod
     def fatias_sugeridas(m: int, n: int, k: int) -> int:
