@@ -35,6 +35,12 @@ CONFIGS = {
     "small": dict(dims=[512, 1024, 1024, 10], batch=2048, dtype="f32", optimizer="sgd", lr=0.01),
 }
 CPU_SAMPLE_ROWS = {"wide": 64, "small": 256}
+# DRAM bytes (read + write) of one 8192 x 8192 x 8192 dW GEMM launch, from an
+# ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of
+# `bench.py --gemm TN --mnk 8192 8192 8192`; scaled to other dW launches by
+# their FLOPs.
+DW_GEMM_TRAFFIC_BYTES = 1.419e9 + 0.253e9
+DW_GEMM_TRAFFIC_FLOPS = 2.0 * 8192 ** 3
 
 
 def peaks():
@@ -172,6 +178,37 @@ def run_reference(args, cfg_name, cfg, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_gemm_only(args):
+    """One bf16 tensor-core GEMM repeated `reps` times (the small case for ncu
+    captures of the dominant kernel).  Operands are N(0,1), the output bf16."""
+    import torch
+
+    import rgpu_b200
+
+    m, n, k = args.mnk
+    gpu = rgpu_b200.Gpu(0)
+    rng = np.random.default_rng(0)
+    shape_a = (k, m) if args.gemm == "TN" else (m, k)
+    shape_b = (n, k) if args.gemm == "NT" else (k, n)
+    a = gpu.upload(rng.standard_normal(shape_a, dtype=np.float32), "bf16")
+    b = gpu.upload(rng.standard_normal(shape_b, dtype=np.float32), "bf16")
+    c = gpu.zeros((m, n), "f32" if args.gemm == "TN" else "bf16")
+    fn = {"NN": gpu.matmul, "NT": gpu.matmul_a_bt, "TN": gpu.matmul_at_b}[args.gemm]
+    fn(a, b, c)
+    gpu.sync()
+    st = torch.cuda.ExternalStream(gpu.stream())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(args.reps):
+        fn(a, b, c)
+    e1.record(st)
+    gpu.sync()
+    ms = e0.elapsed_time(e1) / args.reps
+    print(json.dumps({"gemm": args.gemm, "m": m, "n": n, "k": k, "ms": ms,
+                      "tflops": 2.0 * m * n * k / (ms / 1e3) / 1e12}), flush=True)
+    gpu.close()
+
+
 def config_dict(cfg_name, cfg, n, global_batch):
     d = cfg["dims"]
     return {"workload": ("wide MLP " if cfg_name == "wide" else "MLP ") + "->".join(map(str, d)),
@@ -190,7 +227,13 @@ def main():
     ap.add_argument("--config", default="wide", choices=sorted(CONFIGS))
     ap.add_argument("--global-batch", type=int, default=0, help="strong scaling: fixed global batch")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--gemm", choices=["NN", "NT", "TN"], help="profile one bf16 GEMM instead of the step")
+    ap.add_argument("--mnk", type=int, nargs=3, default=[8192, 8192, 8192], metavar=("M", "N", "K"))
+    ap.add_argument("--reps", type=int, default=3)
     args = ap.parse_args()
+    if args.gemm:
+        run_gemm_only(args)
+        return
     cfg = CONFIGS[args.config]
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -315,8 +358,12 @@ def main():
         lab, (fl, t, cnt) = dom
         ach = fl / (t / 1e3) / 1e12 if t > 0 else 0.0
         peak = pk["bf16"] if cfg["dtype"] == "bf16" else 75.0
+        traffic = None
+        if lab == "dw_gemm" and cfg["dtype"] == "bf16":
+            traffic = DW_GEMM_TRAFFIC_BYTES * (fl / cnt) / DW_GEMM_TRAFFIC_FLOPS
         roof = {"bound": "tensor", "kernel": lab, "launches_per_step": cnt, "achieved": ach, "peak": peak,
-                "unit": "TFLOP/s", "frac": ach / peak, "traffic": None,
+                "unit": "TFLOP/s", "frac": ach / peak, "traffic": traffic,
+                "traffic_note": "bytes per launch, ncu capture of the 8192^3 dW GEMM scaled by FLOPs",
                 "peak_source": pk["source"] + (" bf16 dense (cuBLAS burst)" if cfg["dtype"] == "bf16"
                                                else " f32 SIMT nominal")}
     gemm_t = sum(t for lab, fl, t in ops if fl > 0)
