@@ -359,7 +359,7 @@ def main():
         ach = fl / (t / 1e3) / 1e12 if t > 0 else 0.0
         peak = pk["bf16"] if cfg["dtype"] == "bf16" else 75.0
         traffic = None
-        if lab == "dw_gemm" and cfg["dtype"] == "bf16":
+        if lab == "dw_gemm" and cfg["dtype"] == "bf16":  # plain dW launch, as captured
             traffic = DW_GEMM_TRAFFIC_BYTES * (fl / cnt) / DW_GEMM_TRAFFIC_FLOPS
         roof = {"bound": "tensor", "kernel": lab, "launches_per_step": cnt, "achieved": ach, "peak": peak,
                 "unit": "TFLOP/s", "frac": ach / peak, "traffic": traffic,

@@ -158,18 +158,8 @@ __global__ void opt_step_begin_kernel(OptScalars* s, float beta1, float beta2) {
     s->inv_c2 = __fdiv_rn(1.0f, c2);
 }
 
-// One fused pass per element with the exact rounding sequence of
-// optim.rs:586-593 (no FMA contraction: __fmul_rn / __fadd_rn), 128-bit
-// vector loads where the buffers allow.
-__device__ __forceinline__ float adam_one(float th, float g, float& m, float& v, float b1, float b2, float omb1,
-                                          float omb2, float inv_c1, float inv_c2, float eps, float lr) {
-    m = __fadd_rn(__fmul_rn(m, b1), __fmul_rn(g, omb1));
-    v = __fadd_rn(__fmul_rn(v, b2), __fmul_rn(__fmul_rn(g, g), omb2));
-    float m_hat = __fmul_rn(m, inv_c1);
-    float v_hat = __fmul_rn(v, inv_c2);
-    return __fsub_rn(th, __fmul_rn(__fdiv_rn(m_hat, __fadd_rn(__fsqrt_rn(v_hat), eps)), lr));
-}
-
+// One fused pass per element (adam_one: the rounding sequence of
+// optim.rs:586-593), 128-bit vector loads where the buffers allow.
 __global__ void adam_kernel(OptBatch batch, const OptScalars* __restrict__ sc, float lr, float b1, float b2,
                             float eps) {
     const OptTensor& T = batch.t[blockIdx.y];
@@ -242,6 +232,12 @@ __global__ void sgd_kernel(OptBatch batch, float lr) {
         T.theta[i] = th;
         if (T.shadow) T.shadow[i] = __float2bfloat16_rn(th);
     }
+}
+
+template <typename T>
+__global__ void fill_column_kernel(T* p, int64_t rows, int64_t ld, int64_t col, float value) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += (int64_t)gridDim.x * blockDim.x)
+        stf<T>(p, i * ld + col, value);
 }
 
 unsigned grid_for(const rt_ctx* ctx, int64_t work, int per_thread = 1) {
@@ -363,6 +359,19 @@ int launch_cast(rt_ctx* ctx, const void* src, rt_dtype sdt, int64_t lds, void* d
                                                                      (__nv_bfloat16*)dst, ldd, rows, cols);
     else
         return fail(RT_ERR_INVALID, "cast: unsupported dtype pair");
+    count_launch(ctx);
+    RT_CUDA(cudaGetLastError());
+    return RT_OK;
+}
+
+int launch_fill_column(rt_ctx* ctx, void* p, rt_dtype dt, int64_t rows, int64_t ld, int64_t col, float value,
+                       cudaStream_t st) {
+    if (rows == 0) return RT_OK;
+    unsigned g = grid_for(ctx, rows);
+    if (dt == RT_BF16)
+        fill_column_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((__nv_bfloat16*)p, rows, ld, col, value);
+    else
+        fill_column_kernel<float><<<g, 256, 0, st>>>((float*)p, rows, ld, col, value);
     count_launch(ctx);
     RT_CUDA(cudaGetLastError());
     return RT_OK;

@@ -48,6 +48,7 @@ struct SimtParams {
     int64_t k_per_slice;
     int epi;
     int out_bf16;
+    OptFuse opt;
 };
 
 // Applies the epilogue to one accumulator and stores it.
@@ -187,6 +188,16 @@ __global__ void __launch_bounds__(THREADS) gemm_simt_kernel(SimtParams p) {
                 finish<float>(p, gi, gj, acc[i][j]);
             }
         }
+        if (!p.ws && p.opt.kind) {
+            // the gradient row segments this thread owns, updated in place
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                int64_t gj0 = n0 + half * 64 + tx * 4;
+                int64_t rem = p.n - gj0;
+                int cnt = rem < 4 ? (int)rem : 4;
+                if (cnt > 0) opt_apply_row<4>(p.opt, gi * p.ldc + gj0, &acc[i][half * 4], cnt);
+            }
+        }
     }
 }
 
@@ -203,6 +214,7 @@ __global__ void splitk_reduce_kernel(SimtParams p, int slices) {
             finish<__nv_bfloat16>(p, i, j, s);
         else
             finish<float>(p, i, j, s);
+        if (p.opt.kind) opt_apply_row<1>(p.opt, i * p.ldc + j, &s, 1);
     }
 }
 
@@ -227,6 +239,7 @@ SimtParams make_params(const GemmDesc& g) {
     p.k_per_slice = kps > 0 ? kps : BK;
     p.epi = g.epi;
     p.out_bf16 = g.out_dtype == RT_BF16;
+    p.opt = g.opt;
     return p;
 }
 

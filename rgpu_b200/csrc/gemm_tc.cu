@@ -188,6 +188,7 @@ struct TcParams {
     int epi;
     int out_bf16;
     int* err;
+    OptFuse opt;
 };
 
 // Stage geometry shared by host and device.
@@ -495,10 +496,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int j = 0; j < 32; ++j)
                             if (col0 + j < p.n) dst[j] = v[j];
-                    } else if (p.out_bf16) {
-                        epilogue_chunk<__nv_bfloat16>(p, row, col0, v);
                     } else {
-                        epilogue_chunk<float>(p, row, col0, v);
+                        if (p.opt.kind) {
+                            // optimiser step on theta[row, col0 .. col0+31] with this gradient chunk
+                            int64_t rem = p.n - col0;
+                            int cnt = rem < 32 ? (int)rem : 32;
+                            opt_apply_row<32>(p.opt, row * p.ldc + col0, v, cnt);
+                        }
+                        if (p.out_bf16)
+                            epilogue_chunk<__nv_bfloat16>(p, row, col0, v);
+                        else
+                            epilogue_chunk<float>(p, row, col0, v);
                     }
                 }
             }
@@ -614,6 +622,7 @@ int launch_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     p.epi = g.epi;
     p.out_bf16 = g.out_dtype == RT_BF16;
     p.err = ctx->dev_err;
+    p.opt = g.opt;
 
     int64_t tiles = (int64_t)p.tiles_m * p.tiles_n * p.splits;
     int grid = (int)(tiles < ctx->sm_count ? tiles : ctx->sm_count);

@@ -7,6 +7,7 @@
 #include <cstdio>
 #include <string>
 
+#include "optim_math.cuh"
 #include "rtgpu.h"
 
 namespace rt {
@@ -80,6 +81,7 @@ struct GemmDesc {
     const void* mask; int64_t ldmask;
     int split_k;       // >= 1 after planning
     float* workspace;  // split_k * m * n f32 when split_k > 1
+    OptFuse opt;       // optimiser applied to theta[i*ldc + j] with gradient C[i,j] (kind 0 = none)
 };
 
 // Kernel launchers: enqueue on `stream`, return RT_OK or an error code.
@@ -105,6 +107,10 @@ int launch_relu_bwd(rt_ctx* ctx, const void* a, void* dz, rt_dtype dt, int64_t r
                     int64_t lda, int64_t ldz, cudaStream_t stream);
 int launch_cast(rt_ctx* ctx, const void* src, rt_dtype sdt, int64_t lds, void* dst, rt_dtype ddt,
                 int64_t ldd, int64_t rows, int64_t cols, cudaStream_t stream);
+// Sets column `col` of a [rows, ld] matrix to `value` (the ones column that
+// turns the dW GEMM into a dW + db GEMM).
+int launch_fill_column(rt_ctx* ctx, void* p, rt_dtype dt, int64_t rows, int64_t ld, int64_t col, float value,
+                       cudaStream_t stream);
 
 // Multi-tensor optimiser.  Each entry updates a packed f32 buffer of n
 // elements (theta, g, m, v) and optionally writes a bf16 shadow copy.
@@ -119,11 +125,6 @@ struct OptTensor {
     int64_t n;
 };
 constexpr int kMaxOptTensors = 16;
-struct OptScalars {       // lives in device memory, written by launch_opt_step_begin
-    int t;
-    float inv_c1, inv_c2;
-    float pad;
-};
 int launch_opt_step_begin(rt_ctx* ctx, OptScalars* s, float beta1, float beta2, cudaStream_t stream);
 int launch_adam(rt_ctx* ctx, const OptTensor* ts, int count, const OptScalars* s, float lr, float beta1,
                 float beta2, float eps, cudaStream_t stream);

@@ -7,8 +7,22 @@
 //
 // Backward recurrence (gpu/mod.rs:35-46):
 //   delta_L = (P - Y) / n_global
-//   dW_l = A_{l-1}^T delta_l        db_l = 1^T delta_l
 //   delta_{l-1} = (delta_l W_l^T) * 1[A_{l-1} > 0]     (l > 0)
+//   [dW_l; db_l] = [A_{l-1}, 1]^T delta_l
+//
+// Layout choices that remove kernels from the step:
+//   - every layer input (x and each hidden A_l) carries one extra column of
+//     ones, so the dW GEMM over [A, 1] produces db as its last row and no
+//     separate column reduction runs;
+//   - W_l and b_l share one [d_l + 1, ld] block (b in the last row), and so do
+//     their gradients and Adam moments, so one GEMM epilogue can apply the
+//     optimiser to both;
+//   - with a single GPU the optimiser runs inside the dW GEMM epilogue (the
+//     update's memory traffic overlaps tensor-core work); the dX GEMM that
+//     still needs W_l runs first.  Under data parallelism the gradients are
+//     allreduced first and a multi-tensor optimiser kernel follows.
+//   - two input slots: a host step copies the next batch on a copy stream
+//     while the previous step computes.
 #include <cstring>
 #include <vector>
 
@@ -26,18 +40,31 @@ namespace {
 int64_t round8(int64_t x) { return (x + 7) / 8 * 8; }
 
 struct PlanLayer {
-    int64_t d = 0, u = 0, ld = 0;  // W_l is [d, u] with row stride ld
-    float* w32 = nullptr;
-    __nv_bfloat16* w16 = nullptr;  // bf16 shadow (bf16 plans)
-    float* b = nullptr;
-    float *mw = nullptr, *vw = nullptr, *mb = nullptr, *vb = nullptr;
-    float* dw = nullptr;
-    float* db = nullptr;
-    void* act = nullptr;    // hidden: A_l [n, u] (operand dtype); last: logits f32
-    void* delta = nullptr;  // delta_l [n, u] (operand dtype)
+    int64_t d = 0, u = 0;
+    int64_t ld = 0;      // row stride of the [d+1, ld] parameter blocks and of delta_l
+    int64_t ld_act = 0;  // row stride of A_l (u + 1 columns: activations and the ones column)
+    float* w32 = nullptr;            // [d+1, ld] f32: W rows 0..d-1, bias row d
+    float* b = nullptr;              // = w32 + d*ld
+    __nv_bfloat16* w16 = nullptr;    // bf16 shadow of w32 (bf16 plans)
+    float *m = nullptr, *v = nullptr;  // Adam moments [d+1, ld]
+    float* g = nullptr;              // gradient [d+1, ld]: dW rows 0..d-1, db row d
+    float* db = nullptr;             // = g + d*ld
+    void* act = nullptr;    // hidden: A_l [n, ld_act] (operand dtype); last: logits f32 [n, ld]
+    void* delta = nullptr;  // delta_l [n, ld] (operand dtype)
     int split_dw = 1;
-    float* ws = nullptr;    // split-K partials for dW_l
+    float* ws = nullptr;    // split-K partials for the dW GEMM
     size_t ws_bytes = 0;
+};
+
+struct Slot {
+    void* x = nullptr;          // [n, ldx] operand dtype, ones column at d0
+    uint32_t* labels = nullptr;
+    void* stage = nullptr;      // host-dtype staging when it differs from the plan's
+    size_t stage_bytes = 0;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    bool timed = false;
+    cudaEvent_t ready = nullptr, free_ = nullptr;
 };
 
 struct OpRecord {
@@ -52,24 +79,19 @@ struct rt_mlp {
     rt_mlp_config cfg{};
     std::vector<int64_t> dims;
     std::vector<PlanLayer> L;
-    rt_dtype adt = RT_F32;  // operand / activation dtype
+    rt_dtype adt = RT_F32;
     int64_t n = 0, ldx = 0;
-    void* x = nullptr;
-    uint32_t* labels = nullptr;
+    Slot slot[2];
+    int next_slot = 0;
+    int last_slot = 0;
     float* loss_rows = nullptr;
-    float* colsum_ws = nullptr;
     OptScalars* opt = nullptr;
-    void* x_stage = nullptr;  // host-path staging when the host dtype differs
-    size_t x_stage_bytes = 0;
     std::vector<void*> allocs;
+    cudaStream_t copy_stream = nullptr;
 
-    cudaGraph_t graph = nullptr;
-    cudaGraphExec_t exec = nullptr;
-    bool graph_timed = false;
     bool timing = false;
     std::vector<cudaEvent_t> events;
     std::vector<OpRecord> ops;
-    std::vector<float> op_ms;
     int kernels_per_step = 0;
 
     rt_comm* comm = nullptr;
@@ -89,27 +111,42 @@ int dalloc(rt_mlp* m, void** p, size_t bytes) {
 }
 
 template <typename T>
-int dalloc_t(rt_mlp* m, T** p, size_t count, size_t elem = sizeof(T)) {
-    return dalloc(m, reinterpret_cast<void**>(p), count * elem);
+int dalloc_t(rt_mlp* m, T** p, size_t count) {
+    return dalloc(m, reinterpret_cast<void**>(p), count * sizeof(T));
+}
+
+void drop_graphs(rt_mlp* m) {
+    for (auto& s : m->slot) {
+        if (s.exec) cudaGraphExecDestroy(s.exec);
+        if (s.graph) cudaGraphDestroy(s.graph);
+        s.exec = nullptr;
+        s.graph = nullptr;
+    }
 }
 
 void free_all(rt_mlp* m) {
-    if (m->exec) cudaGraphExecDestroy(m->exec);
-    if (m->graph) cudaGraphDestroy(m->graph);
-    m->exec = nullptr;
-    m->graph = nullptr;
+    drop_graphs(m);
+    for (auto& s : m->slot) {
+        if (s.ready) cudaEventDestroy(s.ready);
+        if (s.free_) cudaEventDestroy(s.free_);
+        if (s.stage) cudaFree(s.stage);
+    }
     for (auto e : m->events) cudaEventDestroy(e);
     for (auto e : m->comm_ready) cudaEventDestroy(e);
     for (auto e : m->comm_done) cudaEventDestroy(e);
     if (m->comm_stream) cudaStreamDestroy(m->comm_stream);
+    if (m->copy_stream) cudaStreamDestroy(m->copy_stream);
     for (void* p : m->allocs) cudaFree(p);
     m->allocs.clear();
 }
+
+bool fused_optimizer(const rt_mlp* m) { return m->cfg.optimizer != RT_OPT_NONE && m->comm == nullptr; }
 
 // ---------------------------------------------------------------- step body
 struct Enqueuer {
     rt_mlp* m;
     cudaStream_t st;
+    int s;  // input slot
     bool forward_only;
     int op_index = 0;
 
@@ -128,8 +165,8 @@ struct Enqueuer {
         return RT_OK;
     }
 
-    const void* input_of(int l) const { return l == 0 ? m->x : m->L[l - 1].act; }
-    int64_t ld_in(int l) const { return l == 0 ? m->ldx : m->L[l - 1].ld; }
+    const void* input_of(int l) const { return l == 0 ? m->slot[s].x : m->L[l - 1].act; }
+    int64_t ld_in(int l) const { return l == 0 ? m->ldx : m->L[l - 1].ld_act; }
     const void* weights(const PlanLayer& P) const {
         return m->adt == RT_BF16 ? (const void*)P.w16 : (const void*)P.w32;
     }
@@ -151,7 +188,7 @@ struct Enqueuer {
             g.b = weights(P);
             g.ldb = P.ld;
             g.c = P.act;
-            g.ldc = P.ld;
+            g.ldc = last ? P.ld : P.ld_act;
             g.epi = last ? RT_EPI_BIAS : RT_EPI_BIAS_RELU;
             g.bias = P.b;
             g.split_k = 1;
@@ -163,44 +200,21 @@ struct Enqueuer {
 
     int backward_and_update() {
         const int nl = (int)m->L.size();
+        const bool fused = fused_optimizer(m);
         PlanLayer& Last = m->L[nl - 1];
         double gb = (double)(m->cfg.global_batch > 0 ? m->cfg.global_batch : m->n);
-        RT_TRY(launch_xent(m->ctx, (const float*)Last.act, Last.ld, m->labels, m->n, Last.u, (float)(1.0 / gb),
-                           Last.delta, m->adt, Last.ld, m->loss_rows, st));
+        if (m->cfg.optimizer == RT_OPT_ADAM) {
+            RT_TRY(launch_opt_step_begin(m->ctx, m->opt, m->cfg.beta1, m->cfg.beta2, st));
+            RT_TRY(mark("adam_scalars", 0));
+        }
+        RT_TRY(launch_xent(m->ctx, (const float*)Last.act, Last.ld, m->slot[s].labels, m->n, Last.u,
+                           (float)(1.0 / gb), Last.delta, m->adt, Last.ld, m->loss_rows, st));
         RT_TRY(mark("softmax_xent", 0));
         for (int l = nl - 1; l >= 0; --l) {
             PlanLayer& P = m->L[l];
-            // dW_l = A_{l-1}^T delta_l  (TN, K = batch), f32 output for the optimiser.
-            GemmDesc g{};
-            g.layout = RT_TN;
-            g.in_dtype = m->adt;
-            g.out_dtype = RT_F32;
-            g.m = P.d;
-            g.n = P.u;
-            g.k = m->n;
-            g.a = input_of(l);
-            g.lda = ld_in(l);
-            g.b = P.delta;
-            g.ldb = P.ld;
-            g.c = P.dw;
-            g.ldc = P.ld;
-            g.epi = RT_EPI_NONE;
-            g.split_k = P.split_dw;
-            g.workspace = P.ws;
-            RT_TRY(run_gemm(m->ctx, g, st, P.ws_bytes));
-            RT_TRY(mark("dw_gemm", 2.0 * m->n * P.d * P.u));
-            // db_l = 1^T delta_l
-            RT_TRY(launch_colsum(m->ctx, P.delta, m->adt, m->n, P.u, P.ld, m->colsum_ws, P.db, st));
-            RT_TRY(mark("db_colsum", 0));
-            if (m->comm) {
-                RT_CUDA(cudaEventRecord(m->comm_ready[l], st));
-                RT_CUDA(cudaStreamWaitEvent(m->comm_stream, m->comm_ready[l], 0));
-                RT_TRY(comm_allreduce(m->comm, P.dw, P.d * P.ld, m->comm_stream));
-                RT_TRY(comm_allreduce(m->comm, P.db, round8(P.u), m->comm_stream));
-                RT_CUDA(cudaEventRecord(m->comm_done[l], m->comm_stream));
-            }
             if (l > 0) {
-                // delta_{l-1} = (delta_l W_l^T) * 1[A_{l-1} > 0]  (NT, fused mask).
+                // delta_{l-1} = (delta_l W_l^T) * 1[A_{l-1} > 0]  (NT, fused mask); reads W_l
+                // before the fused update below rewrites it.
                 PlanLayer& Q = m->L[l - 1];
                 GemmDesc h{};
                 h.layout = RT_NT;
@@ -217,23 +231,56 @@ struct Enqueuer {
                 h.ldc = Q.ld;
                 h.epi = RT_EPI_RELU_MASK;
                 h.mask = Q.act;
-                h.ldmask = Q.ld;
+                h.ldmask = Q.ld_act;
                 h.split_k = 1;
                 RT_TRY(run_gemm(m->ctx, h, st, 0));
                 RT_TRY(mark("dx_gemm_relu_mask", 2.0 * m->n * P.d * P.u));
             }
+            // [dW_l; db_l] = [A_{l-1}, 1]^T delta_l  (TN, K = batch, M = d + 1), f32 gradient out,
+            // optimiser fused into the epilogue on one GPU.
+            GemmDesc g{};
+            g.layout = RT_TN;
+            g.in_dtype = m->adt;
+            g.out_dtype = RT_F32;
+            g.m = P.d + 1;
+            g.n = P.u;
+            g.k = m->n;
+            g.a = input_of(l);
+            g.lda = ld_in(l);
+            g.b = P.delta;
+            g.ldb = P.ld;
+            g.c = P.g;
+            g.ldc = P.ld;
+            g.epi = RT_EPI_NONE;
+            g.split_k = P.split_dw;
+            g.workspace = P.ws;
+            if (fused) {
+                g.opt.kind = m->cfg.optimizer == RT_OPT_ADAM ? 2 : 1;
+                g.opt.theta = P.w32;
+                g.opt.m = P.m;
+                g.opt.v = P.v;
+                g.opt.shadow = P.w16;
+                g.opt.sc = m->opt;
+                g.opt.lr = m->cfg.lr;
+                g.opt.beta1 = m->cfg.beta1;
+                g.opt.beta2 = m->cfg.beta2;
+                g.opt.eps = m->cfg.eps;
+            }
+            RT_TRY(run_gemm(m->ctx, g, st, P.ws_bytes));
+            RT_TRY(mark(fused ? "dw_gemm_opt" : "dw_gemm", 2.0 * m->n * P.d * P.u));
+            if (m->comm) {
+                RT_CUDA(cudaEventRecord(m->comm_ready[l], st));
+                RT_CUDA(cudaStreamWaitEvent(m->comm_stream, m->comm_ready[l], 0));
+                RT_TRY(comm_allreduce(m->comm, P.g, (P.d + 1) * P.ld, m->comm_stream));
+                RT_CUDA(cudaEventRecord(m->comm_done[l], m->comm_stream));
+            }
         }
         if (m->comm)
             for (int l = 0; l < nl; ++l) RT_CUDA(cudaStreamWaitEvent(st, m->comm_done[l], 0));
-        if (m->cfg.optimizer == RT_OPT_NONE) return RT_OK;
+        if (m->cfg.optimizer == RT_OPT_NONE || fused) return RT_OK;
         std::vector<OptTensor> ts;
-        for (auto& P : m->L) {
-            ts.push_back({P.w32, P.dw, P.mw, P.vw, P.w16, P.ld, P.ld, P.d * P.ld});
-            ts.push_back({P.b, P.db, P.mb, P.vb, nullptr, 0, round8(P.u), round8(P.u)});
-        }
+        for (auto& P : m->L) ts.push_back({P.w32, P.g, P.m, P.v, P.w16, P.ld, P.ld, (P.d + 1) * P.ld});
         if (m->cfg.optimizer == RT_OPT_ADAM) {
-            RT_TRY(launch_opt_step_begin(m->ctx, m->opt, m->cfg.beta1, m->cfg.beta2, st));
-            RT_TRY(mark("adam_scalars", 0));
             RT_TRY(launch_adam(m->ctx, ts.data(), (int)ts.size(), m->opt, m->cfg.lr, m->cfg.beta1, m->cfg.beta2,
                                m->cfg.eps, st));
             RT_TRY(mark("adam", 0));
@@ -245,67 +292,74 @@ struct Enqueuer {
     }
 };
 
-int capture_step(rt_mlp* m) {
+int capture_step(rt_mlp* m, int s) {
     cudaStream_t st = m->ctx->stream;
-    if (m->exec) {
-        cudaGraphExecDestroy(m->exec);
-        m->exec = nullptr;
+    Slot& S = m->slot[s];
+    if (S.exec) {
+        cudaGraphExecDestroy(S.exec);
+        S.exec = nullptr;
     }
-    if (m->graph) {
-        cudaGraphDestroy(m->graph);
-        m->graph = nullptr;
+    if (S.graph) {
+        cudaGraphDestroy(S.graph);
+        S.graph = nullptr;
     }
     uint64_t before = m->ctx->launches;
     RT_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-    Enqueuer q{m, st, false};
-    int s = q.begin();
-    if (s == RT_OK) s = q.forward();
-    if (s == RT_OK) s = q.backward_and_update();
+    Enqueuer q{m, st, s, false};
+    int rc = q.begin();
+    if (rc == RT_OK) rc = q.forward();
+    if (rc == RT_OK) rc = q.backward_and_update();
     cudaGraph_t graph = nullptr;
     cudaError_t e = cudaStreamEndCapture(st, &graph);
-    if (s != RT_OK) {
+    if (rc != RT_OK) {
         if (graph) cudaGraphDestroy(graph);
-        return s;
+        return rc;
     }
     if (e != cudaSuccess) return fail(RT_ERR_CUDA, "step capture failed: %s", cudaGetErrorString(e));
-    m->graph = graph;
-    RT_CUDA(cudaGraphInstantiate(&m->exec, graph, 0));
+    S.graph = graph;
+    RT_CUDA(cudaGraphInstantiate(&S.exec, graph, 0));
     m->kernels_per_step = (int)(m->ctx->launches - before);
-    m->graph_timed = m->timing;
+    S.timed = m->timing;
     return RT_OK;
 }
 
-int copy_input(rt_mlp* m, const void* x, rt_dtype xdt, const uint32_t* labels, cudaMemcpyKind kind) {
-    cudaStream_t st = m->ctx->stream;
+int launch_slot(rt_mlp* m, int s) {
+    Slot& S = m->slot[s];
+    if (!S.exec || S.timed != m->timing) RT_TRY(capture_step(m, s));
+    RT_CUDA(cudaGraphLaunch(S.exec, m->ctx->stream));
+    RT_CUDA(cudaEventRecord(S.free_, m->ctx->stream));
+    m->ctx->launches += (uint64_t)m->kernels_per_step;
+    m->last_slot = s;
+    return RT_OK;
+}
+
+// Copies one batch into slot s on stream st (x columns 0..d0-1; the ones
+// column stays).
+int fill_slot(rt_mlp* m, int s, const void* x, rt_dtype xdt, const uint32_t* labels, cudaMemcpyKind kind,
+              cudaStream_t st) {
+    Slot& S = m->slot[s];
     const int64_t d0 = m->dims[0];
     RT_CHECK(xdt == RT_F32 || xdt == RT_BF16, "x dtype must be RT_F32 or RT_BF16");
     if (xdt == m->adt) {
         size_t es = dtype_size(xdt);
-        RT_CUDA(cudaMemcpy2DAsync(m->x, m->ldx * es, x, d0 * es, d0 * es, m->n, kind, st));
+        RT_CUDA(cudaMemcpy2DAsync(S.x, m->ldx * es, x, d0 * es, d0 * es, m->n, kind, st));
     } else {
         const void* src = x;
         if (kind == cudaMemcpyHostToDevice) {
             size_t bytes = (size_t)m->n * d0 * dtype_size(xdt);
-            if (m->x_stage_bytes < bytes) {
-                if (m->x_stage) cudaFree(m->x_stage);
-                m->x_stage = nullptr;
-                m->x_stage_bytes = 0;
-                RT_CUDA(cudaMalloc(&m->x_stage, bytes));
-                m->x_stage_bytes = bytes;
+            if (S.stage_bytes < bytes) {
+                if (S.stage) cudaFree(S.stage);
+                S.stage = nullptr;
+                S.stage_bytes = 0;
+                RT_CUDA(cudaMalloc(&S.stage, bytes));
+                S.stage_bytes = bytes;
             }
-            RT_CUDA(cudaMemcpyAsync(m->x_stage, x, bytes, kind, st));
-            src = m->x_stage;
+            RT_CUDA(cudaMemcpyAsync(S.stage, x, bytes, kind, st));
+            src = S.stage;
         }
-        RT_TRY(launch_cast(m->ctx, src, xdt, d0, m->x, m->adt, m->ldx, m->n, d0, st));
+        RT_TRY(launch_cast(m->ctx, src, xdt, d0, S.x, m->adt, m->ldx, m->n, d0, st));
     }
-    RT_CUDA(cudaMemcpyAsync(m->labels, labels, (size_t)m->n * 4, kind, st));
-    return RT_OK;
-}
-
-int launch_step(rt_mlp* m) {
-    if (!m->exec || m->graph_timed != m->timing) RT_TRY(capture_step(m));
-    RT_CUDA(cudaGraphLaunch(m->exec, m->ctx->stream));
-    m->ctx->launches += (uint64_t)m->kernels_per_step;
+    RT_CUDA(cudaMemcpyAsync(S.labels, labels, (size_t)m->n * 4, kind, st));
     return RT_OK;
 }
 
@@ -324,6 +378,11 @@ int read_packed(rt_mlp* m, const void* src, rt_dtype dt, int64_t rows, int64_t c
     return RT_OK;
 }
 
+int refresh_shadow(rt_mlp* m, PlanLayer& P, cudaStream_t st) {
+    if (m->adt != RT_BF16) return RT_OK;
+    return launch_cast(m->ctx, P.w32, RT_F32, P.ld, P.w16, RT_BF16, P.ld, P.d + 1, P.ld, st);
+}
+
 }  // namespace
 
 extern "C" {
@@ -336,6 +395,7 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
     RT_CHECK(cfg->dtype == RT_F32 || cfg->dtype == RT_BF16, "rt_mlp_create: dtype must be RT_F32 or RT_BF16");
     RT_CHECK(cfg->optimizer >= RT_OPT_NONE && cfg->optimizer <= RT_OPT_ADAM, "rt_mlp_create: unknown optimizer");
     for (int l = 0; l <= cfg->n_layers; ++l) RT_CHECK(cfg->dims[l] >= 1, "rt_mlp_create: dims[%d] < 1", l);
+    for (int l = 0; l < cfg->n_layers; ++l) RT_CHECK(weights[l] != nullptr, "rt_mlp_create: weights[%d] is NULL", l);
     RT_CUDA(cudaSetDevice(ctx->device));
     rt_mlp* m = new rt_mlp;
     m->ctx = ctx;
@@ -353,45 +413,49 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
         return code;
     };
 
-    m->ldx = round8(m->dims[0]);
-    if ((s = dalloc(m, &m->x, (size_t)m->n * m->ldx * es))) return bail(s);
-    if ((s = dalloc_t(m, &m->labels, (size_t)m->n))) return bail(s);
+    m->ldx = round8(m->dims[0] + 1);
+    for (auto& S : m->slot) {
+        if ((s = dalloc(m, &S.x, (size_t)m->n * m->ldx * es))) return bail(s);
+        if ((s = dalloc_t(m, &S.labels, (size_t)m->n))) return bail(s);
+        if ((s = launch_fill_column(ctx, S.x, m->adt, m->n, m->ldx, m->dims[0], 1.0f, ctx->stream)))
+            return bail(s);
+        if (cudaEventCreateWithFlags(&S.ready, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&S.free_, cudaEventDisableTiming) != cudaSuccess)
+            return bail(fail(RT_ERR_CUDA, "event creation failed"));
+    }
+    if (cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(fail(RT_ERR_CUDA, "copy stream creation failed"));
     if ((s = dalloc_t(m, &m->loss_rows, (size_t)m->n))) return bail(s);
     if ((s = dalloc_t(m, &m->opt, 1))) return bail(s);
-    int64_t max_u = 0;
     m->L.resize(nl);
     for (int l = 0; l < nl; ++l) {
         PlanLayer& P = m->L[l];
         P.d = m->dims[l];
         P.u = m->dims[l + 1];
         P.ld = round8(P.u);
-        if (P.u > max_u) max_u = P.u;
-        size_t wn = (size_t)P.d * P.ld, bn = (size_t)round8(P.u), an = (size_t)m->n * P.ld;
         bool last = l == nl - 1;
-        if ((s = dalloc_t(m, &P.w32, wn))) return bail(s);
-        if ((s = dalloc_t(m, &P.b, bn))) return bail(s);
-        if ((s = dalloc_t(m, &P.dw, wn))) return bail(s);
-        if ((s = dalloc_t(m, &P.db, bn))) return bail(s);
+        P.ld_act = last ? P.ld : round8(P.u + 1);
+        size_t pn = (size_t)(P.d + 1) * P.ld;
+        if ((s = dalloc_t(m, &P.w32, pn))) return bail(s);
+        if ((s = dalloc_t(m, &P.g, pn))) return bail(s);
+        P.b = P.w32 + P.d * P.ld;
+        P.db = P.g + P.d * P.ld;
         if (cfg->optimizer == RT_OPT_ADAM) {
-            if ((s = dalloc_t(m, &P.mw, wn))) return bail(s);
-            if ((s = dalloc_t(m, &P.vw, wn))) return bail(s);
-            if ((s = dalloc_t(m, &P.mb, bn))) return bail(s);
-            if ((s = dalloc_t(m, &P.vb, bn))) return bail(s);
+            if ((s = dalloc_t(m, &P.m, pn))) return bail(s);
+            if ((s = dalloc_t(m, &P.v, pn))) return bail(s);
         }
-        if (m->adt == RT_BF16 && (s = dalloc_t(m, &P.w16, wn))) return bail(s);
-        if ((s = dalloc(m, &P.act, an * (last ? 4 : es)))) return bail(s);
-        if ((s = dalloc(m, &P.delta, an * es))) return bail(s);
-        // weights in (host f32 packed [d,u] -> padded rows)
+        if (m->adt == RT_BF16 && (s = dalloc_t(m, &P.w16, pn))) return bail(s);
+        if ((s = dalloc(m, &P.act, (size_t)m->n * P.ld_act * (last ? 4 : es)))) return bail(s);
+        if (!last && (s = launch_fill_column(ctx, P.act, m->adt, m->n, P.ld_act, P.u, 1.0f, ctx->stream)))
+            return bail(s);
+        if ((s = dalloc(m, &P.delta, (size_t)m->n * P.ld * es))) return bail(s);
         if (cudaMemcpy2D(P.w32, P.ld * 4, weights[l], P.u * 4, P.u * 4, P.d, cudaMemcpyHostToDevice) != cudaSuccess)
             return bail(fail(RT_ERR_CUDA, "weight upload failed"));
-        if (biases && biases[l] &&
-            cudaMemcpy(P.b, biases[l], (size_t)P.u * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        if (biases && biases[l] && cudaMemcpy(P.b, biases[l], (size_t)P.u * 4, cudaMemcpyHostToDevice) != cudaSuccess)
             return bail(fail(RT_ERR_CUDA, "bias upload failed"));
-        if (m->adt == RT_BF16 &&
-            (s = launch_cast(ctx, P.w32, RT_F32, P.ld, P.w16, RT_BF16, P.ld, P.d, P.ld, ctx->stream)))
-            return bail(s);
-        // split-K for dW_l when its output tiles cannot fill the GPU.
-        int64_t tiles = ((P.d + 127) / 128) * ((P.u + 255) / 256);
+        if ((s = refresh_shadow(m, P, ctx->stream))) return bail(s);
+        // split-K for the dW GEMM when its 128x256 output tiles cannot fill the GPU.
+        int64_t tiles = ((P.d + 1 + 127) / 128) * ((P.u + 255) / 256);
         int split = 1;
         if (tiles * 4 < (int64_t)ctx->sm_count * 3) {
             int64_t sp = (int64_t)ctx->sm_count / tiles;
@@ -402,11 +466,10 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
         }
         P.split_dw = split;
         if (split > 1) {
-            P.ws_bytes = (size_t)split * P.d * P.u * 4;
+            P.ws_bytes = (size_t)split * (P.d + 1) * P.u * 4;
             if ((s = dalloc(m, (void**)&P.ws, P.ws_bytes))) return bail(s);
         }
     }
-    if ((s = dalloc_t(m, &m->colsum_ws, (size_t)colsum_scratch_rows(m->n) * max_u))) return bail(s);
     if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) return bail(fail(RT_ERR_CUDA, "plan setup sync failed"));
     *out = m;
     return RT_OK;
@@ -416,7 +479,7 @@ int rt_mlp_destroy(rt_mlp* m) {
     if (!m) return RT_OK;
     cudaSetDevice(m->ctx->device);
     cudaStreamSynchronize(m->ctx->stream);
-    if (m->x_stage) cudaFree(m->x_stage);
+    if (m->copy_stream) cudaStreamSynchronize(m->copy_stream);
     free_all(m);
     delete m;
     return RT_OK;
@@ -424,15 +487,26 @@ int rt_mlp_destroy(rt_mlp* m) {
 
 int rt_mlp_step(rt_mlp* m, const void* x_dev, rt_dtype x_dtype, const uint32_t* labels_dev) {
     RT_CHECK(m && x_dev && labels_dev, "rt_mlp_step: bad arguments");
-    RT_TRY(copy_input(m, x_dev, x_dtype, labels_dev, cudaMemcpyDeviceToDevice));
-    return launch_step(m);
+    int s = m->next_slot;
+    m->next_slot ^= 1;
+    // device inputs: copy on the compute stream (GpuMlp::carregar, gpu/mod.rs:1486-1495)
+    RT_TRY(fill_slot(m, s, x_dev, x_dtype, labels_dev, cudaMemcpyDeviceToDevice, m->ctx->stream));
+    return launch_slot(m, s);
 }
 
 int rt_mlp_step_host(rt_mlp* m, const void* x_host, rt_dtype x_dtype, const uint32_t* labels_host,
                      float* loss_rows_host) {
     RT_CHECK(m && x_host && labels_host, "rt_mlp_step_host: bad arguments");
-    RT_TRY(copy_input(m, x_host, x_dtype, labels_host, cudaMemcpyHostToDevice));
-    RT_TRY(launch_step(m));
+    int s = m->next_slot;
+    m->next_slot ^= 1;
+    Slot& S = m->slot[s];
+    // The copy stream refills slot s once the step that last read it is done,
+    // overlapping the step that is running on the other slot.
+    RT_CUDA(cudaStreamWaitEvent(m->copy_stream, S.free_, 0));
+    RT_TRY(fill_slot(m, s, x_host, x_dtype, labels_host, cudaMemcpyHostToDevice, m->copy_stream));
+    RT_CUDA(cudaEventRecord(S.ready, m->copy_stream));
+    RT_CUDA(cudaStreamWaitEvent(m->ctx->stream, S.ready, 0));
+    RT_TRY(launch_slot(m, s));
     if (loss_rows_host)
         RT_CUDA(cudaMemcpyAsync(loss_rows_host, m->loss_rows, (size_t)m->n * 4, cudaMemcpyDeviceToHost,
                                 m->ctx->stream));
@@ -443,13 +517,15 @@ int rt_mlp_forward_only(rt_mlp* m, const void* x_dev, rt_dtype x_dtype) {
     RT_CHECK(m && x_dev, "rt_mlp_forward_only: bad arguments");
     const int64_t d0 = m->dims[0];
     cudaStream_t st = m->ctx->stream;
+    int s = m->next_slot;
+    Slot& S = m->slot[s];
     if (x_dtype == m->adt) {
         size_t es = dtype_size(x_dtype);
-        RT_CUDA(cudaMemcpy2DAsync(m->x, m->ldx * es, x_dev, d0 * es, d0 * es, m->n, cudaMemcpyDeviceToDevice, st));
+        RT_CUDA(cudaMemcpy2DAsync(S.x, m->ldx * es, x_dev, d0 * es, d0 * es, m->n, cudaMemcpyDeviceToDevice, st));
     } else {
-        RT_TRY(launch_cast(m->ctx, x_dev, x_dtype, d0, m->x, m->adt, m->ldx, m->n, d0, st));
+        RT_TRY(launch_cast(m->ctx, x_dev, x_dtype, d0, S.x, m->adt, m->ldx, m->n, d0, st));
     }
-    Enqueuer q{m, st, true};
+    Enqueuer q{m, st, s, true};
     return q.forward();
 }
 
@@ -481,7 +557,7 @@ int rt_mlp_weights(rt_mlp* m, int layer, float* w, float* b) {
 int rt_mlp_grads(rt_mlp* m, int layer, float* dw, float* db) {
     RT_CHECK(m && layer >= 0 && layer < (int)m->L.size(), "bad layer index");
     PlanLayer& P = m->L[layer];
-    if (dw) RT_TRY(read_packed(m, P.dw, RT_F32, P.d, P.u, P.ld, dw));
+    if (dw) RT_TRY(read_packed(m, P.g, RT_F32, P.d, P.u, P.ld, dw));
     if (db) RT_TRY(read_packed(m, P.db, RT_F32, 1, P.u, P.u, db));
     return rt_ctx_sync(m->ctx);
 }
@@ -490,18 +566,16 @@ int rt_mlp_set_weights(rt_mlp* m, int layer, const float* w, const float* b) {
     RT_CHECK(m && layer >= 0 && layer < (int)m->L.size(), "bad layer index");
     PlanLayer& P = m->L[layer];
     cudaStream_t st = m->ctx->stream;
-    if (w) {
-        RT_CUDA(cudaMemcpy2DAsync(P.w32, P.ld * 4, w, P.u * 4, P.u * 4, P.d, cudaMemcpyHostToDevice, st));
-        if (m->adt == RT_BF16) RT_TRY(launch_cast(m->ctx, P.w32, RT_F32, P.ld, P.w16, RT_BF16, P.ld, P.d, P.ld, st));
-    }
+    if (w) RT_CUDA(cudaMemcpy2DAsync(P.w32, P.ld * 4, w, P.u * 4, P.u * 4, P.d, cudaMemcpyHostToDevice, st));
     if (b) RT_CUDA(cudaMemcpyAsync(P.b, b, (size_t)P.u * 4, cudaMemcpyHostToDevice, st));
+    RT_TRY(refresh_shadow(m, P, st));
     RT_CUDA(cudaStreamSynchronize(st));
     return RT_OK;
 }
 
 int rt_mlp_dispatches_per_step(rt_mlp* m, int* out) {
     RT_CHECK(m && out, "bad arguments");
-    if (!m->exec) RT_TRY(capture_step(m));
+    if (!m->slot[0].exec) RT_TRY(capture_step(m, 0));
     *out = m->kernels_per_step;
     return RT_OK;
 }
@@ -540,14 +614,8 @@ int rt_mlp_set_comm(rt_mlp* m, rt_comm* comm) {
         for (auto& e : m->comm_ready) RT_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         for (auto& e : m->comm_done) RT_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     }
-    if (m->exec) {
-        cudaGraphExecDestroy(m->exec);
-        m->exec = nullptr;
-    }
-    if (m->graph) {
-        cudaGraphDestroy(m->graph);
-        m->graph = nullptr;
-    }
+    m->ops.clear();
+    drop_graphs(m);
     return RT_OK;
 }
 
