@@ -15,12 +15,11 @@
 //     ones, so the dW GEMM over [A, 1] produces db as its last row and no
 //     separate column reduction runs;
 //   - W_l and b_l share one [d_l + 1, ld] block (b in the last row), and so do
-//     their gradients and Adam moments, so one GEMM epilogue can apply the
-//     optimiser to both;
-//   - with a single GPU the optimiser runs inside the dW GEMM epilogue (the
-//     update's memory traffic overlaps tensor-core work); the dX GEMM that
-//     still needs W_l runs first.  Under data parallelism the gradients are
-//     allreduced first and a multi-tensor optimiser kernel follows.
+//     their gradients and Adam moments, so one optimiser launch updates both;
+//   - each layer's optimiser update runs on a side stream as soon as its dW
+//     GEMM is done (the dX GEMM, the last reader of W_l, runs first), so the
+//     update's HBM traffic overlaps the remaining backward GEMMs; under data
+//     parallelism it follows that layer's allreduce on the comm stream.
 //   - two input slots: a host step copies the next batch on a copy stream
 //     while the previous step computes.
 #include <cstring>
@@ -38,6 +37,9 @@ using namespace rt;
 namespace {
 
 int64_t round8(int64_t x) { return (x + 7) / 8 * 8; }
+// Row strides of GEMM operands are kept at multiples of 64 elements so every
+// 128-byte TMA row segment starts on a 128-byte line.
+int64_t round64(int64_t x) { return (x + 63) / 64 * 64; }
 
 struct PlanLayer {
     int64_t d = 0, u = 0;
@@ -97,6 +99,9 @@ struct rt_mlp {
     rt_comm* comm = nullptr;
     cudaStream_t comm_stream = nullptr;
     std::vector<cudaEvent_t> comm_ready, comm_done;
+    // per-layer optimiser on a side stream, overlapping the remaining backward GEMMs
+    cudaStream_t opt_stream = nullptr;
+    std::vector<cudaEvent_t> grad_ready, opt_done;
 };
 
 namespace {
@@ -134,13 +139,23 @@ void free_all(rt_mlp* m) {
     for (auto e : m->events) cudaEventDestroy(e);
     for (auto e : m->comm_ready) cudaEventDestroy(e);
     for (auto e : m->comm_done) cudaEventDestroy(e);
+    for (auto e : m->grad_ready) cudaEventDestroy(e);
+    for (auto e : m->opt_done) cudaEventDestroy(e);
     if (m->comm_stream) cudaStreamDestroy(m->comm_stream);
+    if (m->opt_stream) cudaStreamDestroy(m->opt_stream);
     if (m->copy_stream) cudaStreamDestroy(m->copy_stream);
     for (void* p : m->allocs) cudaFree(p);
     m->allocs.clear();
 }
 
-bool fused_optimizer(const rt_mlp* m) { return m->cfg.optimizer != RT_OPT_NONE && m->comm == nullptr; }
+// Enqueues the optimiser update of layer P's [d+1, ld] parameter block on st.
+int enqueue_layer_update(rt_mlp* m, PlanLayer& P, cudaStream_t st) {
+    OptTensor t{P.w32, P.g, P.m, P.v, P.w16, P.ld, P.ld, (P.d + 1) * P.ld};
+    if (m->cfg.optimizer == RT_OPT_ADAM)
+        return launch_adam(m->ctx, &t, 1, m->opt, m->cfg.lr, m->cfg.beta1, m->cfg.beta2, m->cfg.eps, st);
+    if (m->cfg.optimizer == RT_OPT_SGD) return launch_sgd(m->ctx, &t, 1, m->cfg.lr, st);
+    return RT_OK;
+}
 
 // ---------------------------------------------------------------- step body
 struct Enqueuer {
@@ -200,7 +215,7 @@ struct Enqueuer {
 
     int backward_and_update() {
         const int nl = (int)m->L.size();
-        const bool fused = fused_optimizer(m);
+        const bool update = m->cfg.optimizer != RT_OPT_NONE;
         PlanLayer& Last = m->L[nl - 1];
         double gb = (double)(m->cfg.global_batch > 0 ? m->cfg.global_batch : m->n);
         if (m->cfg.optimizer == RT_OPT_ADAM) {
@@ -213,8 +228,8 @@ struct Enqueuer {
         for (int l = nl - 1; l >= 0; --l) {
             PlanLayer& P = m->L[l];
             if (l > 0) {
-                // delta_{l-1} = (delta_l W_l^T) * 1[A_{l-1} > 0]  (NT, fused mask); reads W_l
-                // before the fused update below rewrites it.
+                // delta_{l-1} = (delta_l W_l^T) * 1[A_{l-1} > 0]  (NT, fused mask).  It is the
+                // last reader of W_l in the step, so W_l's update may start after the dW GEMM.
                 PlanLayer& Q = m->L[l - 1];
                 GemmDesc h{};
                 h.layout = RT_NT;
@@ -236,8 +251,7 @@ struct Enqueuer {
                 RT_TRY(run_gemm(m->ctx, h, st, 0));
                 RT_TRY(mark("dx_gemm_relu_mask", 2.0 * m->n * P.d * P.u));
             }
-            // [dW_l; db_l] = [A_{l-1}, 1]^T delta_l  (TN, K = batch, M = d + 1), f32 gradient out,
-            // optimiser fused into the epilogue on one GPU.
+            // [dW_l; db_l] = [A_{l-1}, 1]^T delta_l  (TN, K = batch, M = d + 1), f32 gradient.
             GemmDesc g{};
             g.layout = RT_TN;
             g.in_dtype = m->adt;
@@ -254,40 +268,29 @@ struct Enqueuer {
             g.epi = RT_EPI_NONE;
             g.split_k = P.split_dw;
             g.workspace = P.ws;
-            if (fused) {
-                g.opt.kind = m->cfg.optimizer == RT_OPT_ADAM ? 2 : 1;
-                g.opt.theta = P.w32;
-                g.opt.m = P.m;
-                g.opt.v = P.v;
-                g.opt.shadow = P.w16;
-                g.opt.sc = m->opt;
-                g.opt.lr = m->cfg.lr;
-                g.opt.beta1 = m->cfg.beta1;
-                g.opt.beta2 = m->cfg.beta2;
-                g.opt.eps = m->cfg.eps;
-            }
             RT_TRY(run_gemm(m->ctx, g, st, P.ws_bytes));
-            RT_TRY(mark(fused ? "dw_gemm_opt" : "dw_gemm", 2.0 * m->n * P.d * P.u));
+            RT_TRY(mark("dw_gemm", 2.0 * m->n * P.d * P.u));
             if (m->comm) {
+                // allreduce, then this layer's update, on the comm stream
                 RT_CUDA(cudaEventRecord(m->comm_ready[l], st));
                 RT_CUDA(cudaStreamWaitEvent(m->comm_stream, m->comm_ready[l], 0));
                 RT_TRY(comm_allreduce(m->comm, P.g, (P.d + 1) * P.ld, m->comm_stream));
+                if (update) RT_TRY(enqueue_layer_update(m, P, m->comm_stream));
                 RT_CUDA(cudaEventRecord(m->comm_done[l], m->comm_stream));
+            } else if (update) {
+                RT_CUDA(cudaEventRecord(m->grad_ready[l], st));
+                RT_CUDA(cudaStreamWaitEvent(m->opt_stream, m->grad_ready[l], 0));
+                RT_TRY(enqueue_layer_update(m, P, m->opt_stream));
+                RT_CUDA(cudaEventRecord(m->opt_done[l], m->opt_stream));
             }
         }
-        if (m->comm)
-            for (int l = 0; l < nl; ++l) RT_CUDA(cudaStreamWaitEvent(st, m->comm_done[l], 0));
-        if (m->cfg.optimizer == RT_OPT_NONE || fused) return RT_OK;
-        std::vector<OptTensor> ts;
-        for (auto& P : m->L) ts.push_back({P.w32, P.g, P.m, P.v, P.w16, P.ld, P.ld, (P.d + 1) * P.ld});
-        if (m->cfg.optimizer == RT_OPT_ADAM) {
-            RT_TRY(launch_adam(m->ctx, ts.data(), (int)ts.size(), m->opt, m->cfg.lr, m->cfg.beta1, m->cfg.beta2,
-                               m->cfg.eps, st));
-            RT_TRY(mark("adam", 0));
-        } else {
-            RT_TRY(launch_sgd(m->ctx, ts.data(), (int)ts.size(), m->cfg.lr, st));
-            RT_TRY(mark("sgd", 0));
+        for (int l = 0; l < nl; ++l) {
+            if (m->comm)
+                RT_CUDA(cudaStreamWaitEvent(st, m->comm_done[l], 0));
+            else if (update)
+                RT_CUDA(cudaStreamWaitEvent(st, m->opt_done[l], 0));
         }
+        if (update) RT_TRY(mark(m->cfg.optimizer == RT_OPT_ADAM ? "adam_tail" : "sgd_tail", 0));
         return RT_OK;
     }
 };
@@ -413,7 +416,7 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
         return code;
     };
 
-    m->ldx = round8(m->dims[0] + 1);
+    m->ldx = round64(m->dims[0] + 1);
     for (auto& S : m->slot) {
         if ((s = dalloc(m, &S.x, (size_t)m->n * m->ldx * es))) return bail(s);
         if ((s = dalloc_t(m, &S.labels, (size_t)m->n))) return bail(s);
@@ -423,8 +426,15 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
             cudaEventCreateWithFlags(&S.free_, cudaEventDisableTiming) != cudaSuccess)
             return bail(fail(RT_ERR_CUDA, "event creation failed"));
     }
-    if (cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking) != cudaSuccess)
-        return bail(fail(RT_ERR_CUDA, "copy stream creation failed"));
+    if (cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&m->opt_stream, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(fail(RT_ERR_CUDA, "stream creation failed"));
+    m->grad_ready.resize(nl);
+    m->opt_done.resize(nl);
+    for (int l = 0; l < nl; ++l)
+        if (cudaEventCreateWithFlags(&m->grad_ready[l], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&m->opt_done[l], cudaEventDisableTiming) != cudaSuccess)
+            return bail(fail(RT_ERR_CUDA, "event creation failed"));
     if ((s = dalloc_t(m, &m->loss_rows, (size_t)m->n))) return bail(s);
     if ((s = dalloc_t(m, &m->opt, 1))) return bail(s);
     m->L.resize(nl);
@@ -432,9 +442,9 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
         PlanLayer& P = m->L[l];
         P.d = m->dims[l];
         P.u = m->dims[l + 1];
-        P.ld = round8(P.u);
+        P.ld = P.u >= 64 ? round64(P.u) : round8(P.u);
         bool last = l == nl - 1;
-        P.ld_act = last ? P.ld : round8(P.u + 1);
+        P.ld_act = last ? P.ld : round64(P.u + 1);
         size_t pn = (size_t)(P.d + 1) * P.ld;
         if ((s = dalloc_t(m, &P.w32, pn))) return bail(s);
         if ((s = dalloc_t(m, &P.g, pn))) return bail(s);

@@ -1,0 +1,83 @@
+"""One rank of the data-parallel parity check (launched by tests/test_gpu_dp.py
+with torch.distributed.run, one process per GPU).
+
+Every rank holds the full model, takes rows [r*n/p, (r+1)*n/p) of the global
+batch, scales its softmax-CE adjoint by 1/n_global, and the plan sums dW/db
+over ranks with NCCL inside the captured step.  Rank 0 also runs the whole
+global batch on its GPU without a communicator; the summed DP gradients must
+equal that single-GPU result (and the replicas must stay identical under
+Adam).  Results go to the JSON file named by argv[1].
+"""
+import datetime
+import json
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+import rgpu_b200  # noqa: E402
+
+
+def main():
+    out_path = sys.argv[1]
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    gpu = rgpu_b200.Gpu(local)
+    uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        uid.copy_(torch.frombuffer(bytearray(rgpu_b200.Comm.unique_id()), dtype=torch.uint8))
+    dist.broadcast(uid, 0)
+    comm = rgpu_b200.Comm(gpu, rank, world, bytes(uid.cpu().numpy().tobytes()))
+
+    rng = np.random.default_rng(7)
+    dims = [64, 256, 192, 10]
+    params = []
+    for l in range(len(dims) - 1):
+        lim = np.sqrt(6.0 / dims[l])
+        params += [rng.uniform(-lim, lim, (dims[l], dims[l + 1])).astype(np.float32),
+                   rng.uniform(-0.1, 0.1, (1, dims[l + 1])).astype(np.float32)]
+    n_global = 512
+    x = rng.standard_normal((n_global, dims[0])).astype(np.float32)
+    labels = rng.integers(0, dims[-1], n_global).astype(np.uint32)
+    per = n_global // world
+    xs, ls = x[rank * per:(rank + 1) * per], labels[rank * per:(rank + 1) * per]
+    result = {}
+    for dtype in ("f32", "bf16"):
+        mlp = rgpu_b200.GpuMlp.from_params(gpu, params, per, 0.0, dtype=dtype, optimizer="none",
+                                           global_batch=n_global)
+        mlp.set_comm(comm)
+        mlp.step(gpu.upload(xs), rgpu_b200.upload_labels(gpu, ls))
+        g_dp = mlp.grads()
+        mlp.close()
+        if rank == 0:
+            ref = rgpu_b200.GpuMlp.from_params(gpu, params, n_global, 0.0, dtype=dtype, optimizer="none")
+            ref.step(gpu.upload(x), rgpu_b200.upload_labels(gpu, labels))
+            g_ref = ref.grads()
+            ref.close()
+            result[dtype] = [float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)) for a, b in zip(g_dp, g_ref)]
+    # Adam: replicas stay bit-identical.
+    mlp = rgpu_b200.GpuMlp.from_params(gpu, params, per, 1e-3, dtype="bf16", optimizer="adam", global_batch=n_global)
+    mlp.set_comm(comm)
+    gx, gl = gpu.upload(xs), rgpu_b200.upload_labels(gpu, ls)
+    for _ in range(5):
+        mlp.step(gx, gl)
+    w = np.concatenate([a.ravel() for a in mlp.weights()])
+    mlp.close()
+    wt = torch.from_numpy(w).cuda()
+    gathered = [torch.zeros_like(wt) for _ in range(world)]
+    dist.all_gather(gathered, wt)
+    if rank == 0:
+        result["replicas_identical"] = all(torch.equal(gathered[0], g) for g in gathered[1:])
+        json.dump(result, open(out_path, "w"))
+    comm.close()
+    gpu.close()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,30 @@
+"""Data-parallel parity on 2 GPUs (skipped when fewer are visible): NCCL
+allreduce of dW/db inside the captured step equals the single-GPU global
+batch, and the replicas stay bit-identical under Adam."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def test_two_rank_dp_equals_single_gpu(tmp_path):
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = tmp_path / "dp.json"
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29531",
+           os.path.join(HERE, "dp_worker.py"), str(out)]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    res = json.load(open(out))
+    assert max(res["f32"]) <= 1e-5, res["f32"]
+    assert max(res["bf16"]) <= 2e-2, res["bf16"]
+    assert res["replicas_identical"]
