@@ -27,287 +27,11 @@
 // No TMA load here uses the cluster-wide broadcast form: every CTA loads its
 // own operand tiles, so the kernel is safe to run on every GPU of a
 // data-parallel job.
-#include <cuda.h>
-
-#include <mutex>
-
-#include "internal.h"
+#include "tc_common.cuh"
 
 namespace rt {
 namespace {
-
-constexpr int kThreads = 256;
-constexpr int BM = 128;
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
-
-// ------------------------------------------------------------- PTX helpers
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ uint64_t globaltimer() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return done != 0;
-}
-
-// Bounded wait.  Returns false when the limit expired or another role
-// aborted; the caller then leaves its loop.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
-    if (mbar_try_wait(bar, parity)) return true;
-    uint64_t t0 = globaltimer();
-    for (uint32_t it = 1;; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 255u) == 0) {
-            if (*abort_flag) return false;
-            if (globaltimer() - t0 > kWaitLimitNs) return false;
-        }
-    }
-}
-
-__device__ __forceinline__ void fence_barrier_init() {
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y,
-                                            uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-            "r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-        : "memory");
-}
-
-__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tc_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-                 : "memory");
-}
-
-template <bool kTF32>
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                       uint32_t accumulate) {
-    if constexpr (kTF32) {
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "setp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-            : "memory");
-    } else {
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "setp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-            : "memory");
-    }
-}
-
-// 32 lanes x 32 columns of 32-bit accumulator: thread i of the warp receives
-// row (lane base + i), columns [col, col + 32).
-__device__ __forceinline__ void tmem_ld_32x32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// Shared-memory matrix descriptor (tcgen05 "version 1" layout): start address,
-// leading/stride byte offsets (16-byte units) and the 128-byte swizzle mode.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
-    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
-    d |= (uint64_t)1 << 46;  // descriptor version for tcgen05
-    d |= (uint64_t)2 << 61;  // 128-byte swizzle
-    return d;
-}
-
-// Instruction descriptor for kind::f16 (bf16 x bf16) or kind::tf32, f32 accumulate.
-__host__ __device__ constexpr uint32_t make_idesc(bool tf32, bool a_mn, bool b_mn, int n, int m) {
-    return (1u << 4)                              // D format: f32
-           | ((tf32 ? 2u : 1u) << 7)              // A format: bf16 = 1, tf32 = 2
-           | ((tf32 ? 2u : 1u) << 10)             // B format
-           | ((a_mn ? 1u : 0u) << 15)             // A major-ness (1 = MN-major)
-           | ((b_mn ? 1u : 0u) << 16)             // B major-ness
-           | ((uint32_t)(n >> 3) << 17)           // N / 8
-           | ((uint32_t)(m >> 4) << 24);          // M / 16
-}
-
-struct TcParams {
-    int64_t m, n, k;
-    int tiles_m, tiles_n, splits, kblocks, kb_per_split, group;
-    void* c;
-    int64_t ldc;
-    float* ws;
-    const float* bias;
-    const void* mask;
-    int64_t ldmask;
-    int epi;
-    int out_bf16;
-    int* err;
-    OptFuse opt;
-};
-
-// Stage geometry shared by host and device.
-template <typename TIn, int BN>
-struct Geo {
-    static constexpr int ES = sizeof(TIn);
-    static constexpr int BK = 128 / ES;        // one 128-byte swizzle row of k
-    static constexpr int CHUNK = 128 / ES;     // MN elements per 128-byte row (MN-major boxes)
-    static constexpr int UK = 32 / ES;         // k per tcgen05.mma
-    static constexpr int A_BYTES = BM * 128;
-    static constexpr int B_BYTES = BN * 128;
-    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
-    static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-};
-
-__device__ __forceinline__ void tile_coords(const TcParams& p, int t, int& split, int& mb, int& nb) {
-    int per = p.tiles_m * p.tiles_n;
-    split = t / per;
-    int r = t % per;
-    int gsz = p.group * p.tiles_n;
-    int g = r / gsz;
-    int first = g * p.group;
-    int rows = min(p.tiles_m - first, p.group);
-    int in = r % gsz;
-    mb = first + in % rows;
-    nb = in / rows;
-}
-
-__device__ __forceinline__ void record_error(int* err, int code, int detail) {
-    if (atomicCAS(err, 0, code) == 0) err[1] = detail;
-}
-
-template <typename TOut>
-__device__ __forceinline__ float load_mask_elem(const void* mask, int64_t idx);
-template <>
-__device__ __forceinline__ float load_mask_elem<float>(const void* mask, int64_t idx) {
-    return static_cast<const float*>(mask)[idx];
-}
-template <>
-__device__ __forceinline__ float load_mask_elem<__nv_bfloat16>(const void* mask, int64_t idx) {
-    return __bfloat162float(static_cast<const __nv_bfloat16*>(mask)[idx]);
-}
-
-// Epilogue for 32 consecutive columns of one row.
-template <typename TOut>
-__device__ __forceinline__ void epilogue_chunk(const TcParams& p, int64_t row, int64_t col0, float (&v)[32]) {
-    const int64_t n = p.n;
-    const bool full = col0 + 32 <= n;
-    if (p.epi == RT_EPI_BIAS || p.epi == RT_EPI_BIAS_RELU) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = v[j] + (col0 + j < n ? __ldg(p.bias + col0 + j) : 0.0f);
-        if (p.epi == RT_EPI_BIAS_RELU) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
-        }
-    } else if (p.epi == RT_EPI_RELU_MASK) {
-        const int64_t base = row * p.ldmask + col0;
-        if (full && sizeof(TOut) == 2) {
-            const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.mask) + base);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                uint4 u = src[q];
-                const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) v[q * 8 + j] = v[q * 8 + j] * (__bfloat162float(h[j]) > 0.0f ? 1.0f : 0.0f);
-            }
-        } else if (full) {
-            const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.mask) + base);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                float4 u = src[q];
-                v[q * 4 + 0] = v[q * 4 + 0] * (u.x > 0.0f ? 1.0f : 0.0f);
-                v[q * 4 + 1] = v[q * 4 + 1] * (u.y > 0.0f ? 1.0f : 0.0f);
-                v[q * 4 + 2] = v[q * 4 + 2] * (u.z > 0.0f ? 1.0f : 0.0f);
-                v[q * 4 + 3] = v[q * 4 + 3] * (u.w > 0.0f ? 1.0f : 0.0f);
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (col0 + j < n) v[j] = v[j] * (load_mask_elem<TOut>(p.mask, base + j) > 0.0f ? 1.0f : 0.0f);
-        }
-    }
-    if constexpr (sizeof(TOut) == 2) {
-        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.c) + row * p.ldc + col0;
-        if (full) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                uint4 u;
-                __nv_bfloat162 h0 = __floats2bfloat162_rn(v[q * 8 + 0], v[q * 8 + 1]);
-                __nv_bfloat162 h1 = __floats2bfloat162_rn(v[q * 8 + 2], v[q * 8 + 3]);
-                __nv_bfloat162 h2 = __floats2bfloat162_rn(v[q * 8 + 4], v[q * 8 + 5]);
-                __nv_bfloat162 h3 = __floats2bfloat162_rn(v[q * 8 + 6], v[q * 8 + 7]);
-                u.x = *reinterpret_cast<uint32_t*>(&h0);
-                u.y = *reinterpret_cast<uint32_t*>(&h1);
-                u.z = *reinterpret_cast<uint32_t*>(&h2);
-                u.w = *reinterpret_cast<uint32_t*>(&h3);
-                reinterpret_cast<uint4*>(dst)[q] = u;
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (col0 + j < n) dst[j] = __float2bfloat16_rn(v[j]);
-        }
-    } else {
-        float* dst = static_cast<float*>(p.c) + row * p.ldc + col0;
-        if (full) {
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-                reinterpret_cast<float4*>(dst)[q] = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
-        } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (col0 + j < n) dst[j] = v[j];
-        }
-    }
-}
-
+using namespace tc;
 template <typename TIn, bool A_MN, bool B_MN, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -543,45 +267,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-// ------------------------------------------------------------------ host
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    });
-    return fn;
-}
-
-// 2-D row-major tensor: `inner` contiguous elements per row, `outer` rows,
-// row stride `ld` elements; box (box_inner x box_outer), 128-byte swizzle.
-int make_tmap(CUtensorMap* map, const void* base, bool bf16, int64_t inner, int64_t outer, int64_t ld,
-              int box_inner, int box_outer) {
-    EncodeTiledFn enc = encode_fn();
-    if (!enc) return fail(RT_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled is not available from the driver");
-    const int es = bf16 ? 2 : 4;
-    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
-    cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
-    cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
-                     const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS)
-        return fail(RT_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d): inner %lld outer %lld ld %lld box %dx%d",
-                    (int)r, (long long)inner, (long long)outer, (long long)ld, box_inner, box_outer);
-    return RT_OK;
-}
-
 template <typename TIn, bool A_MN, bool B_MN, int BN>
 int launch_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     using G = Geo<TIn, BN>;
@@ -686,6 +371,7 @@ bool gemm_tc_supported(const rt_ctx* ctx, const GemmDesc& g) {
 
 int launch_gemm_tc(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     if (!gemm_tc_supported(ctx, g)) return fail(RT_ERR_UNSUPPORTED, "operands not eligible for the tensor-core GEMM");
+    if (gemm_tc2_wanted(ctx, g)) return launch_gemm_tc2(ctx, g, st);
     if (g.n <= 64) return launch_layout<__nv_bfloat16, 64>(ctx, g, st);
     if (g.n <= 128) return launch_layout<__nv_bfloat16, 128>(ctx, g, st);
     return launch_layout<__nv_bfloat16, 256>(ctx, g, st);

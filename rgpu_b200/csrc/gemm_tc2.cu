@@ -1,0 +1,442 @@
+// Two-CTA tensor-core GEMM (tcgen05 cta_group::2): a cluster of two CTAs on a
+// pair of SMs computes a 256 x BN tile with one MMA stream.
+//
+// Same operands, layouts, epilogues and bounded-wait rules as the one-CTA
+// kernel in gemm_tc.cu; what changes is how a tile's operands are split:
+//   - CTA rank r of the pair loads A rows [128 r, 128 r + 128) of the tile and
+//     B columns [BN/2 r, BN/2 (r + 1)), each into its own shared memory at the
+//     same offsets; per 64-deep k block that is 32 KB per CTA instead of the
+//     48 KB a one-CTA 128 x 256 tile needs, which leaves room for 6 stages;
+//   - the leader (rank 0) issues tcgen05.mma.cta_group::2 (M = 256); the
+//     tensor cores read both CTAs' halves and each CTA's TMEM receives its own
+//     128 accumulator rows;
+//   - both CTAs' TMA loads complete on the leader's full barrier (the
+//     .cta_group::2 form of the load names the leader's barrier), and only the
+//     leader posts the expected byte count of the pair;
+//   - the leader's MMA thread releases stages and publishes finished
+//     accumulators with one tcgen05.commit per CTA (its own barrier and the
+//     peer's, addressed through mapa); the peer's epilogue warps arrive
+//     remotely on the leader's TMEM-empty barrier.
+// Every CTA loads its own tiles: no load is shared between CTAs.
+#include "tc_common.cuh"
+
+namespace rt {
+namespace {
+using namespace tc;
+
+constexpr int BM2 = 256;  // rows per CTA pair
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// TMA load whose completion is counted on the pair leader's barrier.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y,
+                                                 uint32_t leader_bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(leader_bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit_pair(uint32_t cluster_bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+template <typename TIn, int BN>
+struct Geo2 {
+    static constexpr int ES = sizeof(TIn);
+    static constexpr int BK = 128 / ES;
+    static constexpr int CHUNK = 128 / ES;
+    static constexpr int UK = 32 / ES;
+    static constexpr int BNH = BN / 2;  // B rows (n) held by each CTA
+    static constexpr int A_BYTES = 128 * 128;
+    static constexpr int B_BYTES = BNH * 128;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+template <typename TIn, bool A_MN, bool B_MN, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                    TcParams p) {
+    using G = Geo2<TIn, BN>;
+    constexpr int STAGES = G::STAGES;
+    constexpr uint32_t IDESC = make_idesc(false, A_MN, B_MN, BN, BM2);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem_a = smem;
+    uint8_t* smem_b = smem + STAGES * G::A_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * G::STAGE_BYTES);
+    uint64_t* full = bars;                     // leader: both CTAs' bytes of a stage
+    uint64_t* empty = bars + STAGES;           // each CTA: stage released by the MMAs
+    uint64_t* tfull = bars + 2 * STAGES;       // each CTA: accumulator ready
+    uint64_t* tempty = bars + 2 * STAGES + 2;  // leader: accumulator drained by both epilogues
+    uint64_t* drain = bars + 2 * STAGES + 4;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    uint32_t* last_phase = tmem_slot + 2;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const uint32_t peer = rank ^ 1u;
+    const int cluster_id = blockIdx.x >> 1;
+    const int num_clusters = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+            last_phase[s] = 0;
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(smem_u32(&tfull[s]), 1);
+            mbar_init(smem_u32(&tempty[s]), 8);  // 4 epilogue warps x 2 CTAs
+        }
+        mbar_init(smem_u32(drain), 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tmap(&tmap_a);
+        prefetch_tmap(&tmap_b);
+    }
+    if (warp == 2) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(G::TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // barrier initialisation and the TMEM address are now visible to the pair
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t peer_abort = mapa_shared(smem_u32((const void*)abort_flag), peer);
+    auto raise_abort = [&]() {
+        *abort_flag = 1;
+        st_cluster_u32(peer_abort, 1u);
+    };
+
+    const int total_tiles = p.tiles_m * p.tiles_n * p.splits;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------ TMA producer (both CTAs)
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
+            int split, mb, nb;
+            tile_coords(p, t, split, mb, nb);
+            int kb0 = split * p.kb_per_split;
+            int kb1 = min(p.kblocks, kb0 + p.kb_per_split);
+            const int m0 = mb * BM2 + (int)rank * 128;
+            const int n0 = nb * BN + (int)rank * G::BNH;
+            for (int kb = kb0; kb < kb1; ++kb) {
+                if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t leader_full = mapa_shared(smem_u32(&full[stage]), 0);
+                if (rank == 0) mbar_expect_tx(smem_u32(&full[stage]), 2 * G::STAGE_BYTES);
+                last_phase[stage] = phase + 1;
+                const int k0 = kb * G::BK;
+                const uint32_t sa = smem_u32(smem_a + stage * G::A_BYTES);
+                const uint32_t sb = smem_u32(smem_b + stage * G::B_BYTES);
+                if (A_MN) {
+#pragma unroll
+                    for (int c = 0; c < 128 / G::CHUNK; ++c)
+                        tma_load_2d_pair(sa + c * (G::BK * 128), &tmap_a, m0 + c * G::CHUNK, k0, leader_full);
+                } else {
+                    tma_load_2d_pair(sa, &tmap_a, k0, m0, leader_full);
+                }
+                if (B_MN) {
+#pragma unroll
+                    for (int c = 0; c < G::BNH / G::CHUNK; ++c)
+                        tma_load_2d_pair(sb + c * (G::BK * 128), &tmap_b, n0 + c * G::CHUNK, k0, leader_full);
+                } else {
+                    tma_load_2d_pair(sb, &tmap_b, k0, n0, leader_full);
+                }
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+        }
+        if (!ok) {
+            record_error(p.err, DEV_TIMEOUT_PRODUCER, blockIdx.x);
+            raise_abort();
+        }
+    } else if (warp == 1 && lane == 0 && rank == 0) {
+        // ------------------------------------------------ MMA issuer (pair leader)
+        int stage = 0;
+        uint32_t phase = 0;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        bool ok = true;
+        constexpr uint32_t A_KSTEP = A_MN ? G::UK * 128 : 32;
+        constexpr uint32_t B_KSTEP = B_MN ? G::UK * 128 : 32;
+        constexpr uint32_t A_LBO = A_MN ? G::BK * 128 : 16;
+        constexpr uint32_t B_LBO = B_MN ? G::BK * 128 : 16;
+        for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
+            int split, mb, nb;
+            tile_coords(p, t, split, mb, nb);
+            int kb0 = split * p.kb_per_split;
+            int kb1 = min(p.kblocks, kb0 + p.kb_per_split);
+            if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+            for (int kb = kb0; kb < kb1; ++kb) {
+                if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t sa = smem_u32(smem_a + stage * G::A_BYTES);
+                const uint32_t sb = smem_u32(smem_b + stage * G::B_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < G::BK / G::UK; ++kk) {
+                    uint64_t ad = smem_desc(sa + kk * A_KSTEP, A_LBO, 1024);
+                    uint64_t bd = smem_desc(sb + kk * B_KSTEP, B_LBO, 1024);
+                    tc_mma_pair(d_tmem, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+                }
+                // release the stage in both CTAs once these MMAs have read it
+                tc_commit_pair(smem_u32(&empty[stage]));
+                tc_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+            if (!ok) break;
+            tc_commit_pair(smem_u32(&tfull[acc]));
+            tc_commit_pair(mapa_shared(smem_u32(&tfull[acc]), 1));
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+        if (!ok) {
+            record_error(p.err, DEV_TIMEOUT_MMA, blockIdx.x);
+            raise_abort();
+        }
+        tc_commit_pair(smem_u32(drain));
+        mbar_wait(smem_u32(drain), 0, abort_flag);
+    } else if (warp >= 4) {
+        // ------------------------------------------------ epilogue (both CTAs)
+        const int ew = warp - 4;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        bool ok = true;
+        for (int t = cluster_id; t < total_tiles; t += num_clusters) {
+            int split, mb, nb;
+            tile_coords(p, t, split, mb, nb);
+            bool got = mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag);
+            if (!__all_sync(0xffffffffu, got)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int64_t row = (int64_t)mb * BM2 + (int64_t)rank * 128 + ew * 32 + lane;
+            const uint32_t tbase = tmem_base + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                const int64_t col0 = (int64_t)nb * BN + c;
+                if (col0 >= p.n) break;
+                float v[32];
+                tmem_ld_32x32(tbase + (uint32_t)c, v);
+                if (row < p.m) {
+                    if (p.ws) {
+                        float* dst = p.ws + (int64_t)split * p.m * p.n + row * p.n + col0;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < p.n) dst[j] = v[j];
+                    } else {
+                        if (p.opt.kind) {
+                            int64_t rem = p.n - col0;
+                            int cnt = rem < 32 ? (int)rem : 32;
+                            opt_apply_row<32>(p.opt, row * p.ldc + col0, v, cnt);
+                        }
+                        if (p.out_bf16)
+                            epilogue_chunk<__nv_bfloat16>(p, row, col0, v);
+                        else
+                            epilogue_chunk<float>(p, row, col0, v);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+        if (!ok && lane == 0) {
+            record_error(p.err, DEV_TIMEOUT_EPILOGUE, blockIdx.x);
+            raise_abort();
+        }
+    }
+
+    __syncwarp();
+    __syncthreads();
+    if (*abort_flag && rank == 0 && threadIdx.x == 0) {
+        // Both CTAs' TMA loads complete on the leader's barriers: wait for the
+        // last phase issued into each stage before either CTA can exit.
+        for (int s = 0; s < STAGES; ++s)
+            if (last_phase[s]) {
+                volatile int never = 0;
+                mbar_wait(smem_u32(&full[s]), last_phase[s] - 1, &never);
+            }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // no remote arrive or load is outstanding past this point
+    if (warp == 2) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(G::TMEM_COLS)
+                     : "memory");
+    }
+}
+
+template <typename TIn, bool A_MN, bool B_MN, int BN>
+int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
+    using G = Geo2<TIn, BN>;
+    const bool bf16 = sizeof(TIn) == 2;
+    CUtensorMap ta, tb;
+    if (A_MN)
+        RT_TRY(make_tmap(&ta, g.a, bf16, g.m, g.k, g.lda, G::CHUNK, G::BK));
+    else
+        RT_TRY(make_tmap(&ta, g.a, bf16, g.k, g.m, g.lda, G::BK, 128));
+    if (B_MN)
+        RT_TRY(make_tmap(&tb, g.b, bf16, g.n, g.k, g.ldb, G::CHUNK, G::BK));
+    else
+        RT_TRY(make_tmap(&tb, g.b, bf16, g.k, g.n, g.ldb, G::BK, G::BNH));
+
+    TcParams p{};
+    GemmDesc gr = g;
+    p.m = g.m;
+    p.n = g.n;
+    p.k = g.k;
+    p.tiles_m = (int)((g.m + BM2 - 1) / BM2);
+    p.tiles_n = (int)((g.n + BN - 1) / BN);
+    p.kblocks = (int)((g.k + G::BK - 1) / G::BK);
+    int splits = g.split_k > 1 ? g.split_k : 1;
+    if (splits > p.kblocks) splits = p.kblocks;
+    p.kb_per_split = (p.kblocks + splits - 1) / splits;
+    splits = (p.kblocks + p.kb_per_split - 1) / p.kb_per_split;
+    p.splits = splits;
+    gr.split_k = splits;
+    p.group = ctx->l2_group;
+    p.c = g.c;
+    p.ldc = g.ldc;
+    p.ws = splits > 1 ? g.workspace : nullptr;
+    p.bias = g.bias;
+    p.mask = g.mask;
+    p.ldmask = g.ldmask;
+    p.epi = g.epi;
+    p.out_bf16 = g.out_dtype == RT_BF16;
+    p.err = ctx->dev_err;
+    p.opt = g.opt;
+
+    int64_t tiles = (int64_t)p.tiles_m * p.tiles_n * p.splits;
+    int64_t clusters = ctx->sm_count / 2;
+    if (tiles < clusters) clusters = tiles;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = G::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    RT_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<TIn, A_MN, B_MN, BN>, ta, tb, p));
+    count_launch(ctx);
+    if (splits > 1) return launch_splitk_reduce(ctx, gr, st);
+    return RT_OK;
+}
+
+template <int BN>
+int launch_pair_layout(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
+    switch (g.layout) {
+        case RT_NN: return launch_pair_variant<__nv_bfloat16, false, true, BN>(ctx, g, st);
+        case RT_NT: return launch_pair_variant<__nv_bfloat16, false, false, BN>(ctx, g, st);
+        case RT_TN: return launch_pair_variant<__nv_bfloat16, true, true, BN>(ctx, g, st);
+    }
+    return fail(RT_ERR_INVALID, "unknown layout");
+}
+
+template <bool A_MN, bool B_MN, int BN>
+int set_attr_pair() {
+    RT_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<__nv_bfloat16, A_MN, B_MN, BN>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Geo2<__nv_bfloat16, BN>::SMEM));
+    return RT_OK;
+}
+
+}  // namespace
+
+int gemm_tc2_init(rt_ctx* ctx) {
+    (void)ctx;
+    RT_TRY((set_attr_pair<false, true, 128>()));
+    RT_TRY((set_attr_pair<false, false, 128>()));
+    RT_TRY((set_attr_pair<true, true, 128>()));
+    RT_TRY((set_attr_pair<false, true, 256>()));
+    RT_TRY((set_attr_pair<false, false, 256>()));
+    RT_TRY((set_attr_pair<true, true, 256>()));
+    return RT_OK;
+}
+
+// Pair tiles pay off when the output has at least one full 256-row tile and
+// a 128-wide column tile; smaller problems keep the one-CTA kernel.
+bool gemm_tc2_wanted(const rt_ctx* ctx, const GemmDesc& g) {
+    return ctx->pair_gemm && g.in_dtype == RT_BF16 && g.m >= 256 && g.n > 64;
+}
+
+int launch_gemm_tc2(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
+    if (g.n <= 128) return launch_pair_layout<128>(ctx, g, st);
+    return launch_pair_layout<256>(ctx, g, st);
+}
+
+}  // namespace rt

@@ -51,6 +51,7 @@ struct rt_ctx {
     cudaStream_t stream = nullptr;
     int* dev_err = nullptr;  // [4] ints: first device error code, detail
     bool fast_gemm = true;
+    bool pair_gemm = true;  // two-CTA tcgen05 tiles where the problem is large enough
     int l2_group = 8;
     uint64_t launches = 0;
     char name[256] = {0};
@@ -91,6 +92,9 @@ int launch_gemm_simt(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream);
 int launch_gemm_tc(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream);
 bool gemm_tc_supported(const rt_ctx* ctx, const GemmDesc& g);
 int gemm_tc_init(rt_ctx* ctx);
+int gemm_tc2_init(rt_ctx* ctx);
+bool gemm_tc2_wanted(const rt_ctx* ctx, const GemmDesc& g);
+int launch_gemm_tc2(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream);
 int launch_splitk_reduce(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream);
 
 int launch_xent(rt_ctx* ctx, const float* logits, int64_t ldz, const uint32_t* labels, int64_t n,

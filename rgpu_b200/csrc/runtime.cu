@@ -2,6 +2,7 @@
 // (crates/rtensor/src/gpu/mod.rs:180-566) that owns the device, its stream
 // and buffers.
 #include <cstdarg>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -79,7 +80,10 @@ int rt_ctx_create(int device, rt_ctx** out) {
     }
     cudaMemset(c->dev_err, 0, 4 * sizeof(int));
     c->stream = c->own_stream;
+    const char* pair_env = getenv("RTGPU_PAIR_GEMM");
+    c->pair_gemm = !(pair_env && pair_env[0] == '0');
     int st = gemm_tc_init(c);
+    if (st == RT_OK) st = gemm_tc2_init(c);
     if (st != RT_OK) {
         cudaFree(c->dev_err);
         cudaStreamDestroy(c->own_stream);
