@@ -187,6 +187,8 @@ def run_gemm_only(args):
 
     m, n, k = args.mnk
     gpu = rgpu_b200.Gpu(0)
+    if args.l2_group:
+        gpu.set_grupo_l2(args.l2_group)
     rng = np.random.default_rng(0)
     shape_a = (k, m) if args.gemm == "TN" else (m, k)
     shape_b = (n, k) if args.gemm == "NT" else (k, n)
@@ -230,6 +232,7 @@ def main():
     ap.add_argument("--gemm", choices=["NN", "NT", "TN"], help="profile one bf16 GEMM instead of the step")
     ap.add_argument("--mnk", type=int, nargs=3, default=[8192, 8192, 8192], metavar=("M", "N", "K"))
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--l2-group", type=int, default=0, help="GEMM raster group (tile rows), 0 = library default")
     args = ap.parse_args()
     if args.gemm:
         run_gemm_only(args)
