@@ -160,7 +160,12 @@ __global__ void opt_step_begin_kernel(OptScalars* s, float beta1, float beta2) {
 
 // One fused pass per element (adam_one: the rounding sequence of
 // optim.rs:586-593), 128-bit vector loads where the buffers allow.
-__global__ void adam_kernel(OptBatch batch, const OptScalars* __restrict__ sc, float lr, float b1, float b2,
+// 128-thread blocks of <= 48 registers per thread: small enough to co-reside
+// with a running tensor-core GEMM CTA on the same SM, so a layer's update
+// overlaps the next layer's GEMMs.
+constexpr int kOptThreads = 128;
+
+__global__ void __launch_bounds__(kOptThreads) adam_kernel(OptBatch batch, const OptScalars* __restrict__ sc, float lr, float b1, float b2,
                             float eps) {
     const OptTensor& T = batch.t[blockIdx.y];
     const float inv_c1 = sc->inv_c1, inv_c2 = sc->inv_c2;
@@ -203,7 +208,7 @@ __global__ void adam_kernel(OptBatch batch, const OptScalars* __restrict__ sc, f
 }
 
 // optim.rs:486-493: theta -= g * lr.
-__global__ void sgd_kernel(OptBatch batch, float lr) {
+__global__ void __launch_bounds__(kOptThreads) sgd_kernel(OptBatch batch, float lr) {
     const OptTensor& T = batch.t[blockIdx.y];
     const int64_t n = T.n;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -402,8 +407,8 @@ int launch_adam(rt_ctx* ctx, const OptTensor* ts, int count, const OptScalars* s
     int64_t max_n;
     RT_TRY(fill_batch(b, ts, count, max_n));
     if (max_n == 0) return RT_OK;
-    dim3 grid(grid_for(ctx, max_n, 4), (unsigned)count);
-    adam_kernel<<<grid, 256, 0, st>>>(b, s, lr, beta1, beta2, eps);
+    dim3 grid(2 * grid_for(ctx, max_n, 4), (unsigned)count);
+    adam_kernel<<<grid, kOptThreads, 0, st>>>(b, s, lr, beta1, beta2, eps);
     count_launch(ctx);
     RT_CUDA(cudaGetLastError());
     return RT_OK;
@@ -414,8 +419,8 @@ int launch_sgd(rt_ctx* ctx, const OptTensor* ts, int count, float lr, cudaStream
     int64_t max_n;
     RT_TRY(fill_batch(b, ts, count, max_n));
     if (max_n == 0) return RT_OK;
-    dim3 grid(grid_for(ctx, max_n, 4), (unsigned)count);
-    sgd_kernel<<<grid, 256, 0, st>>>(b, lr);
+    dim3 grid(2 * grid_for(ctx, max_n, 4), (unsigned)count);
+    sgd_kernel<<<grid, kOptThreads, 0, st>>>(b, lr);
     count_launch(ctx);
     RT_CUDA(cudaGetLastError());
     return RT_OK;

@@ -310,7 +310,8 @@ int launch_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     p.opt = g.opt;
 
     int64_t tiles = (int64_t)p.tiles_m * p.tiles_n * p.splits;
-    int grid = (int)(tiles < ctx->sm_count ? tiles : ctx->sm_count);
+    int sms = g.max_sms > 0 && g.max_sms < ctx->sm_count ? g.max_sms : ctx->sm_count;
+    int grid = (int)(tiles < sms ? tiles : sms);
     gemm_tc_kernel<TIn, A_MN, B_MN, BN><<<grid, kThreads, G::SMEM, st>>>(ta, tb, p);
     count_launch(ctx);
     RT_CUDA(cudaGetLastError());

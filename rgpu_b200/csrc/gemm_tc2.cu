@@ -25,6 +25,11 @@ namespace {
 using namespace tc;
 
 constexpr int BM2 = 256;  // rows per CTA pair
+// 12 warps: 0 TMA producer, 1 MMA issuer (leader), 2 TMEM allocator, 3 idle,
+// 4..11 epilogue (two warps per TMEM lane quadrant, each taking half of the
+// tile's columns, so short-k tiles do not wait on the epilogue).
+constexpr int kThreads2 = 384;
+constexpr int kEpiWarps = 8;
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;
@@ -92,7 +97,7 @@ struct Geo2 {
 };
 
 template <typename TIn, bool A_MN, bool B_MN, int BN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads2, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     TcParams p) {
     using G = Geo2<TIn, BN>;
@@ -128,7 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(smem_u32(&tfull[s]), 1);
-            mbar_init(smem_u32(&tempty[s]), 8);  // 4 epilogue warps x 2 CTAs
+            mbar_init(smem_u32(&tempty[s]), 2 * kEpiWarps);  // epilogue warps of both CTAs
         }
         mbar_init(smem_u32(drain), 1);
         *abort_flag = 0;
@@ -262,7 +267,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(smem_u32(drain), 0, abort_flag);
     } else if (warp >= 4) {
         // ------------------------------------------------ epilogue (both CTAs)
-        const int ew = warp - 4;
+        const int ew = (warp - 4) & 3;        // TMEM lane quadrant
+        const int half = (warp - 4) >> 2;     // column half of the tile
         int acc = 0;
         uint32_t acc_phase = 0;
         bool ok = true;
@@ -278,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int64_t row = (int64_t)mb * BM2 + (int64_t)rank * 128 + ew * 32 + lane;
             const uint32_t tbase = tmem_base + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
+            for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
                 const int64_t col0 = (int64_t)nb * BN + c;
                 if (col0 >= p.n) break;
                 float v[32];
@@ -378,11 +384,12 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     p.opt = g.opt;
 
     int64_t tiles = (int64_t)p.tiles_m * p.tiles_n * p.splits;
-    int64_t clusters = ctx->sm_count / 2;
+    int sms = g.max_sms > 0 && g.max_sms < ctx->sm_count ? g.max_sms : ctx->sm_count;
+    int64_t clusters = sms / 2;
     if (tiles < clusters) clusters = tiles;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(kThreads2, 1, 1);
     cfg.dynamicSmemBytes = G::SMEM;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];

@@ -83,6 +83,7 @@ struct GemmDesc {
     int split_k;       // >= 1 after planning
     float* workspace;  // split_k * m * n f32 when split_k > 1
     OptFuse opt;       // optimiser applied to theta[i*ldc + j] with gradient C[i,j] (kind 0 = none)
+    int max_sms;       // persistent-grid cap (0 = every SM); leaves SMs to concurrent collectives
 };
 
 // Kernel launchers: enqueue on `stream`, return RT_OK or an error code.

@@ -22,6 +22,7 @@
 //     parallelism it follows that layer's allreduce on the comm stream.
 //   - two input slots: a host step copies the next batch on a copy stream
 //     while the previous step computes.
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -97,6 +98,7 @@ struct rt_mlp {
     int kernels_per_step = 0;
 
     rt_comm* comm = nullptr;
+    int comm_sm_reserve = 0;  // SMs the backward GEMMs leave to NCCL while gradients are reduced
     cudaStream_t comm_stream = nullptr;
     std::vector<cudaEvent_t> comm_ready, comm_done;
     // per-layer optimiser on a side stream, overlapping the remaining backward GEMMs
@@ -182,6 +184,9 @@ struct Enqueuer {
 
     const void* input_of(int l) const { return l == 0 ? m->slot[s].x : m->L[l - 1].act; }
     int64_t ld_in(int l) const { return l == 0 ? m->ldx : m->L[l - 1].ld_act; }
+    int backward_sms() const {
+        return m->comm && m->comm_sm_reserve > 0 ? m->ctx->sm_count - m->comm_sm_reserve : 0;
+    }
     const void* weights(const PlanLayer& P) const {
         return m->adt == RT_BF16 ? (const void*)P.w16 : (const void*)P.w32;
     }
@@ -248,6 +253,7 @@ struct Enqueuer {
                 h.mask = Q.act;
                 h.ldmask = Q.ld_act;
                 h.split_k = 1;
+                h.max_sms = backward_sms();
                 RT_TRY(run_gemm(m->ctx, h, st, 0));
                 RT_TRY(mark("dx_gemm_relu_mask", 2.0 * m->n * P.d * P.u));
             }
@@ -268,6 +274,7 @@ struct Enqueuer {
             g.epi = RT_EPI_NONE;
             g.split_k = P.split_dw;
             g.workspace = P.ws;
+            g.max_sms = backward_sms();
             RT_TRY(run_gemm(m->ctx, g, st, P.ws_bytes));
             RT_TRY(mark("dw_gemm", 2.0 * m->n * P.d * P.u));
             if (m->comm) {
@@ -617,6 +624,11 @@ int rt_mlp_op_time(rt_mlp* m, int i, const char** label, double* flops, float* m
 int rt_mlp_set_comm(rt_mlp* m, rt_comm* comm) {
     RT_CHECK(m, "bad arguments");
     m->comm = comm;
+    // RTGPU_COMM_SM_RESERVE=<n>: backward GEMMs run on sm_count - n SMs so the
+    // gradient allreduce has SMs of its own (an even count keeps CTA pairs whole).
+    const char* r = getenv("RTGPU_COMM_SM_RESERVE");
+    m->comm_sm_reserve = r ? (atoi(r) + 1) / 2 * 2 : 0;
+    if (m->comm_sm_reserve < 0 || m->comm_sm_reserve >= m->ctx->sm_count) m->comm_sm_reserve = 0;
     if (comm && !m->comm_stream) {
         RT_CUDA(cudaStreamCreateWithFlags(&m->comm_stream, cudaStreamNonBlocking));
         m->comm_ready.resize(m->L.size());
