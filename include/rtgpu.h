@@ -252,6 +252,56 @@ int rt_mlp_op_time(rt_mlp* mlp, int i, const char** label, double* flops, float*
  * second stream, layer by layer as backward produces them. */
 int rt_mlp_set_comm(rt_mlp* mlp, rt_comm* comm);
 
+/* ------------------------------------------------------ autodiff tape */
+/* Reverse-mode tape on the GPU for the ops a Dense network is made of.  All
+ * values and adjoints are f32 device buffers owned by the tape; every op and
+ * the backward sweep only enqueue kernels on the context stream. */
+typedef struct rt_tape rt_tape;   /* tape::Tape  (tape.rs:43-67) */
+typedef struct rt_var rt_var;     /* tape::Var   (tape.rs:136-184); owned by its tape */
+typedef struct rt_param rt_param; /* tape::Param (tape.rs:76-132) */
+typedef struct rt_adam_state rt_adam_state; /* optim::Adam (optim.rs:540-558) */
+
+/* Param::new (tape.rs:86-92): rows x cols f32 from host (NULL = zeros). */
+int rt_param_create(rt_ctx* ctx, const float* host, int64_t rows, int64_t cols, rt_param** out);
+int rt_param_destroy(rt_param* p);
+/* Param::value (tape.rs:102-104), blocking copy to host. */
+int rt_param_read(rt_param* p, float* host);
+/* Param::set (tape.rs:119-121). */
+int rt_param_write(rt_param* p, const float* host);
+/* Device view of the parameter's value (non-owning rt_tensor). */
+int rt_param_value(rt_param* p, rt_tensor** view);
+/* Tape::new (tape.rs:50-52) / drop. */
+int rt_tape_create(rt_ctx* ctx, rt_tape** out);
+int rt_tape_destroy(rt_tape* t);
+int rt_tape_len(rt_tape* t, int* out);
+/* constant (tape.rs:70-73): copies value (f32) into a leaf. */
+int rt_tape_constant(rt_tape* t, const rt_tensor* value, rt_var** out);
+/* Param::watch (tape.rs:124-131): the leaf of p, reused if already watched. */
+int rt_param_watch(rt_param* p, rt_tape* t, rt_var** out);
+/* Var::matmul (ops.rs:125-129), Var::add with [1,n] row broadcast
+ * (ops.rs:49-53), Var::relu (ops.rs:190-194). */
+int rt_var_matmul(rt_var* a, rt_var* b, rt_var** out);
+int rt_var_add(rt_var* a, rt_var* b, rt_var** out);
+int rt_var_relu(rt_var* a, rt_var** out);
+/* losses::softmax_cross_entropy (losses.rs:99-115) with integer labels
+ * (u32 [rows]) in place of the one-hot rows; the scalar loss must be the root
+ * of the backward sweep. */
+int rt_softmax_cross_entropy(rt_var* logits, const rt_tensor* labels, rt_var** out);
+/* Var::value (tape.rs:143-145) as a device view; Tensor::item (blocking). */
+int rt_var_value(rt_var* v, rt_tensor** view);
+int rt_var_item(rt_var* v, float* out);
+/* Var::backward (tape.rs:187-229): enqueue the reverse sweep from a scalar. */
+int rt_var_backward(rt_var* root);
+/* Grads::of (tape.rs:238-243): device view of the parameter's gradient, or
+ * *view = NULL when the parameter took no part in the graph. */
+int rt_grads_of(rt_tape* t, rt_param* p, rt_tensor** view);
+/* Sgd::step without momentum (optim.rs:479-493). */
+int rt_sgd_step(rt_ctx* ctx, int n, rt_param* const* params, rt_tape* grads, float lr);
+/* Adam::with_betas (optim.rs:555-557) and Adam::step (optim.rs:561-597). */
+int rt_adam_create(rt_ctx* ctx, float lr, float beta1, float beta2, float eps, rt_adam_state** out);
+int rt_adam_destroy(rt_adam_state* a);
+int rt_adam_step(rt_adam_state* a, int n, rt_param* const* params, rt_tape* grads);
+
 /* ------------------------------------------------------------------ NCCL */
 /* 128-byte ncclUniqueId, created on one rank and shared out of band. */
 int rt_comm_unique_id(unsigned char id[128]);

@@ -239,6 +239,29 @@ __global__ void __launch_bounds__(kOptThreads) sgd_kernel(OptBatch batch, float 
     }
 }
 
+__global__ void axpy_kernel(float* dst, int64_t ldd, const float* src, int64_t lds, int64_t rows, int64_t cols) {
+    int64_t total = rows * cols;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        int64_t i = idx / cols, j = idx % cols;
+        dst[i * ldd + j] = dst[i * ldd + j] + src[i * lds + j];
+    }
+}
+
+// out[0] = (sum of rows[0..n)) / n, in a fixed order (one block).
+__global__ void mean_rows_kernel(const float* rows, int64_t n, float* out) {
+    __shared__ float part[256];
+    float s = 0.0f;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += rows[i];
+    part[threadIdx.x] = s;
+    __syncthreads();
+    for (int w = 128; w > 0; w >>= 1) {
+        if ((int)threadIdx.x < w) part[threadIdx.x] += part[threadIdx.x + w];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) out[0] = n > 0 ? part[0] / (float)n : 0.0f;
+}
+
 template <typename T>
 __global__ void fill_column_kernel(T* p, int64_t rows, int64_t ld, int64_t col, float value) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += (int64_t)gridDim.x * blockDim.x)
@@ -364,6 +387,22 @@ int launch_cast(rt_ctx* ctx, const void* src, rt_dtype sdt, int64_t lds, void* d
                                                                      (__nv_bfloat16*)dst, ldd, rows, cols);
     else
         return fail(RT_ERR_INVALID, "cast: unsupported dtype pair");
+    count_launch(ctx);
+    RT_CUDA(cudaGetLastError());
+    return RT_OK;
+}
+
+int launch_axpy_inplace(rt_ctx* ctx, float* dst, int64_t ldd, const float* src, int64_t lds, int64_t rows,
+                        int64_t cols, cudaStream_t st) {
+    if (rows * cols == 0) return RT_OK;
+    axpy_kernel<<<grid_for(ctx, rows * cols), 256, 0, st>>>(dst, ldd, src, lds, rows, cols);
+    count_launch(ctx);
+    RT_CUDA(cudaGetLastError());
+    return RT_OK;
+}
+
+int launch_mean_rows(rt_ctx* ctx, const float* rows, int64_t n, float* out, cudaStream_t st) {
+    mean_rows_kernel<<<1, 256, 0, st>>>(rows, n, out);
     count_launch(ctx);
     RT_CUDA(cudaGetLastError());
     return RT_OK;

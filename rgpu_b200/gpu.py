@@ -119,6 +119,28 @@ _SIGS = [
     ("rt_mlp_op_time", C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_double),
                                  C.POINTER(C.c_float)]),
     ("rt_mlp_set_comm", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("rt_param_create", C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.POINTER(C.c_void_p)]),
+    ("rt_param_destroy", C.c_int, [C.c_void_p]),
+    ("rt_param_read", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("rt_param_write", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("rt_param_value", C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("rt_tape_create", C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("rt_tape_destroy", C.c_int, [C.c_void_p]),
+    ("rt_tape_len", C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
+    ("rt_tape_constant", C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("rt_param_watch", C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("rt_var_matmul", C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("rt_var_add", C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("rt_var_relu", C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("rt_softmax_cross_entropy", C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("rt_var_value", C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("rt_var_item", C.c_int, [C.c_void_p, C.POINTER(C.c_float)]),
+    ("rt_var_backward", C.c_int, [C.c_void_p]),
+    ("rt_grads_of", C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("rt_sgd_step", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_float]),
+    ("rt_adam_create", C.c_int, [C.c_void_p, C.c_float, C.c_float, C.c_float, C.c_float, C.POINTER(C.c_void_p)]),
+    ("rt_adam_destroy", C.c_int, [C.c_void_p]),
+    ("rt_adam_step", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     ("rt_comm_unique_id", C.c_int, [C.c_void_p]),
     ("rt_comm_init", C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.POINTER(C.c_void_p)]),
     ("rt_comm_destroy", C.c_int, [C.c_void_p]),
