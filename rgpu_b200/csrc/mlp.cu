@@ -109,12 +109,15 @@ struct rt_mlp {
 
 namespace {
 
+// Every plan buffer is zeroed on the context stream, and every later set-up
+// copy and kernel goes to that stream too, so they are ordered (the context
+// stream does not synchronise with the legacy default stream).
 int dalloc(rt_mlp* m, void** p, size_t bytes) {
     cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
     if (e != cudaSuccess) return fail(RT_ERR_OOM, "plan allocation of %zu bytes failed: %s", bytes, cudaGetErrorString(e));
     m->allocs.push_back(*p);
-    e = cudaMemset(*p, 0, bytes ? bytes : 16);
-    if (e != cudaSuccess) return fail(RT_ERR_CUDA, "cudaMemset failed: %s", cudaGetErrorString(e));
+    e = cudaMemsetAsync(*p, 0, bytes ? bytes : 16, m->ctx->stream);
+    if (e != cudaSuccess) return fail(RT_ERR_CUDA, "cudaMemsetAsync failed: %s", cudaGetErrorString(e));
     return RT_OK;
 }
 
@@ -472,9 +475,11 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
         if (!last && (s = launch_fill_column(ctx, P.act, m->adt, m->n, P.ld_act, P.u, 1.0f, ctx->stream)))
             return bail(s);
         if ((s = dalloc(m, &P.delta, (size_t)m->n * P.ld * es))) return bail(s);
-        if (cudaMemcpy2D(P.w32, P.ld * 4, weights[l], P.u * 4, P.u * 4, P.d, cudaMemcpyHostToDevice) != cudaSuccess)
+        if (cudaMemcpy2DAsync(P.w32, P.ld * 4, weights[l], P.u * 4, P.u * 4, P.d, cudaMemcpyHostToDevice,
+                              ctx->stream) != cudaSuccess)
             return bail(fail(RT_ERR_CUDA, "weight upload failed"));
-        if (biases && biases[l] && cudaMemcpy(P.b, biases[l], (size_t)P.u * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        if (biases && biases[l] &&
+            cudaMemcpyAsync(P.b, biases[l], (size_t)P.u * 4, cudaMemcpyHostToDevice, ctx->stream) != cudaSuccess)
             return bail(fail(RT_ERR_CUDA, "bias upload failed"));
         if ((s = refresh_shadow(m, P, ctx->stream))) return bail(s);
         // split-K for the dW GEMM when its 128x256 output tiles cannot fill the GPU.

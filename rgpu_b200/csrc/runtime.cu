@@ -78,8 +78,9 @@ int rt_ctx_create(int device, rt_ctx** out) {
         delete c;
         return fail(RT_ERR_CUDA, "context setup failed: %s", cudaGetErrorString(e1 != cudaSuccess ? e1 : e2));
     }
-    cudaMemset(c->dev_err, 0, 4 * sizeof(int));
     c->stream = c->own_stream;
+    cudaMemsetAsync(c->dev_err, 0, 4 * sizeof(int), c->stream);
+    cudaStreamSynchronize(c->stream);
     const char* pair_env = getenv("RTGPU_PAIR_GEMM");
     c->pair_gemm = !(pair_env && pair_env[0] == '0');
     int st = gemm_tc_init(c);

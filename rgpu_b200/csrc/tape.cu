@@ -157,9 +157,11 @@ int rt_param_create(rt_ctx* ctx, const float* host, int64_t rows, int64_t cols, 
     p->value.ld = ld_for(cols);
     size_t bytes = (size_t)(rows > 0 ? rows : 1) * (size_t)p->value.ld * 4;
     cudaError_t e = cudaMalloc((void**)&p->value.p, bytes);
-    if (e == cudaSuccess) e = cudaMemset(p->value.p, 0, bytes);
+    if (e == cudaSuccess) e = cudaMemsetAsync(p->value.p, 0, bytes, ctx->stream);
     if (e == cudaSuccess && host && rows * cols > 0)
-        e = cudaMemcpy2D(p->value.p, p->value.ld * 4, host, cols * 4, cols * 4, rows, cudaMemcpyHostToDevice);
+        e = cudaMemcpy2DAsync(p->value.p, p->value.ld * 4, host, cols * 4, cols * 4, rows, cudaMemcpyHostToDevice,
+                              ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     if (e != cudaSuccess) {
         if (p->value.p) cudaFree(p->value.p);
         delete p;
@@ -486,7 +488,7 @@ int rt_adam_create(rt_ctx* ctx, float lr, float beta1, float beta2, float eps, r
     a->beta2 = beta2;
     a->eps = eps;
     cudaError_t e = cudaMalloc((void**)&a->sc, sizeof(OptScalars));
-    if (e == cudaSuccess) e = cudaMemset(a->sc, 0, sizeof(OptScalars));
+    if (e == cudaSuccess) e = cudaMemsetAsync(a->sc, 0, sizeof(OptScalars), ctx->stream);
     if (e != cudaSuccess) {
         delete a;
         return fail(RT_ERR_CUDA, "rt_adam_create: %s", cudaGetErrorString(e));
