@@ -16,11 +16,12 @@
 //     separate column reduction runs;
 //   - W_l and b_l share one [d_l + 1, ld] block (b in the last row), and so do
 //     their gradients and Adam moments, so one optimiser launch updates both;
-//   - each layer's optimiser update runs on a side stream as soon as its dW
-//     GEMM is done (the dX GEMM, the last reader of W_l, runs first), so the
-//     update's HBM traffic overlaps the remaining backward GEMMs; under data
-//     parallelism it waits for that layer's allreduce, and the comm stream
-//     carries nothing but the allreduces.
+//   - per layer the dW GEMM runs first (under data parallelism its allreduce
+//     then starts while the dX GEMM computes), the dX GEMM second; the layer's
+//     optimiser update runs on a side stream once the dX GEMM, the last reader
+//     of W_l, is done (and, under data parallelism, the allreduce), so the
+//     update's HBM traffic overlaps the remaining backward GEMMs; the comm
+//     stream carries nothing but the allreduces.
 //   - two input slots: a host step copies the next batch on a copy stream
 //     while the previous step computes.
 #include <cstdlib>
@@ -236,9 +237,37 @@ struct Enqueuer {
         RT_TRY(mark("softmax_xent", 0));
         for (int l = nl - 1; l >= 0; --l) {
             PlanLayer& P = m->L[l];
+            // [dW_l; db_l] = [A_{l-1}, 1]^T delta_l  (TN, K = batch, M = d + 1), f32 gradient.
+            // It runs before the dX GEMM so that the layer's allreduce starts as early as possible.
+            GemmDesc g{};
+            g.layout = RT_TN;
+            g.in_dtype = m->adt;
+            g.out_dtype = RT_F32;
+            g.m = P.d + 1;
+            g.n = P.u;
+            g.k = m->n;
+            g.a = input_of(l);
+            g.lda = ld_in(l);
+            g.b = P.delta;
+            g.ldb = P.ld;
+            g.c = P.g;
+            g.ldc = P.ld;
+            g.epi = RT_EPI_NONE;
+            g.split_k = P.split_dw;
+            g.workspace = P.ws;
+            g.max_sms = backward_sms();
+            RT_TRY(run_gemm(m->ctx, g, st, P.ws_bytes));
+            RT_TRY(mark("dw_gemm", 2.0 * m->n * P.d * P.u));
+            if (m->comm) {
+                // the comm stream carries only the allreduces, back to back
+                RT_CUDA(cudaEventRecord(m->comm_ready[l], st));
+                RT_CUDA(cudaStreamWaitEvent(m->comm_stream, m->comm_ready[l], 0));
+                RT_TRY(comm_allreduce(m->comm, P.g, (P.d + 1) * P.ld, m->comm_stream));
+                RT_CUDA(cudaEventRecord(m->comm_done[l], m->comm_stream));
+            }
             if (l > 0) {
-                // delta_{l-1} = (delta_l W_l^T) * 1[A_{l-1} > 0]  (NT, fused mask).  It is the
-                // last reader of W_l in the step, so W_l's update may start after the dW GEMM.
+                // delta_{l-1} = (delta_l W_l^T) * 1[A_{l-1} > 0]  (NT, fused mask): the last
+                // reader of W_l in the step.
                 PlanLayer& Q = m->L[l - 1];
                 GemmDesc h{};
                 h.layout = RT_NT;
@@ -261,41 +290,12 @@ struct Enqueuer {
                 RT_TRY(run_gemm(m->ctx, h, st, 0));
                 RT_TRY(mark("dx_gemm_relu_mask", 2.0 * m->n * P.d * P.u));
             }
-            // [dW_l; db_l] = [A_{l-1}, 1]^T delta_l  (TN, K = batch, M = d + 1), f32 gradient.
-            GemmDesc g{};
-            g.layout = RT_TN;
-            g.in_dtype = m->adt;
-            g.out_dtype = RT_F32;
-            g.m = P.d + 1;
-            g.n = P.u;
-            g.k = m->n;
-            g.a = input_of(l);
-            g.lda = ld_in(l);
-            g.b = P.delta;
-            g.ldb = P.ld;
-            g.c = P.g;
-            g.ldc = P.ld;
-            g.epi = RT_EPI_NONE;
-            g.split_k = P.split_dw;
-            g.workspace = P.ws;
-            g.max_sms = backward_sms();
-            RT_TRY(run_gemm(m->ctx, g, st, P.ws_bytes));
-            RT_TRY(mark("dw_gemm", 2.0 * m->n * P.d * P.u));
-            if (m->comm) {
-                // the comm stream carries only the allreduces, back to back; each
-                // layer's update follows its allreduce on the optimiser stream
-                RT_CUDA(cudaEventRecord(m->comm_ready[l], st));
-                RT_CUDA(cudaStreamWaitEvent(m->comm_stream, m->comm_ready[l], 0));
-                RT_TRY(comm_allreduce(m->comm, P.g, (P.d + 1) * P.ld, m->comm_stream));
-                RT_CUDA(cudaEventRecord(m->comm_done[l], m->comm_stream));
-                if (update) {
-                    RT_CUDA(cudaStreamWaitEvent(m->opt_stream, m->comm_done[l], 0));
-                    RT_TRY(enqueue_layer_update(m, P, m->opt_stream));
-                    RT_CUDA(cudaEventRecord(m->opt_done[l], m->opt_stream));
-                }
-            } else if (update) {
+            if (update) {
+                // W_l's update waits for its last reader (this dX GEMM) and, under data
+                // parallelism, for its allreduce
                 RT_CUDA(cudaEventRecord(m->grad_ready[l], st));
                 RT_CUDA(cudaStreamWaitEvent(m->opt_stream, m->grad_ready[l], 0));
+                if (m->comm) RT_CUDA(cudaStreamWaitEvent(m->opt_stream, m->comm_done[l], 0));
                 RT_TRY(enqueue_layer_update(m, P, m->opt_stream));
                 RT_CUDA(cudaEventRecord(m->opt_done[l], m->opt_stream));
             }
