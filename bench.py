@@ -179,8 +179,10 @@ def run_reference(args, cfg_name, cfg, rank):
 
 
 def run_gemm_only(args):
-    """One bf16 tensor-core GEMM repeated `reps` times (the small case for ncu
-    captures of the dominant kernel).  Operands are N(0,1), the output bf16."""
+    """One tensor-core GEMM repeated `reps` times (the small case for ncu
+    captures of the dominant kernel).  Operands are N(0,1) bf16 (or f32 on the
+    3xTF32 path with --gemm-dtype f32); the output is bf16 except for TN and
+    f32 operands."""
     import torch
 
     import rgpu_b200
@@ -192,9 +194,9 @@ def run_gemm_only(args):
     rng = np.random.default_rng(0)
     shape_a = (k, m) if args.gemm == "TN" else (m, k)
     shape_b = (n, k) if args.gemm == "NT" else (k, n)
-    a = gpu.upload(rng.standard_normal(shape_a, dtype=np.float32), "bf16")
-    b = gpu.upload(rng.standard_normal(shape_b, dtype=np.float32), "bf16")
-    c = gpu.zeros((m, n), "f32" if args.gemm == "TN" else "bf16")
+    a = gpu.upload(rng.standard_normal(shape_a, dtype=np.float32), args.gemm_dtype)
+    b = gpu.upload(rng.standard_normal(shape_b, dtype=np.float32), args.gemm_dtype)
+    c = gpu.zeros((m, n), "f32" if args.gemm == "TN" or args.gemm_dtype == "f32" else "bf16")
     fn = {"NN": gpu.matmul, "NT": gpu.matmul_a_bt, "TN": gpu.matmul_at_b}[args.gemm]
     fn(a, b, c)
     gpu.sync()
@@ -206,8 +208,91 @@ def run_gemm_only(args):
     e1.record(st)
     gpu.sync()
     ms = e0.elapsed_time(e1) / args.reps
-    print(json.dumps({"gemm": args.gemm, "m": m, "n": n, "k": k, "ms": ms,
+    print(json.dumps({"gemm": args.gemm, "dtype": args.gemm_dtype, "m": m, "n": n, "k": k, "ms": ms,
                       "tflops": 2.0 * m * n * k / (ms / 1e3) / 1e12}), flush=True)
+    gpu.close()
+
+
+SWEEP_M = (1024, 4096, 8192)
+SWEEP_N = (512, 4096, 8192)
+SWEEP_K = (1, 8, 32, 128, 512, 2048, 16384)
+
+
+def run_dw_sweep(args):
+    """dW = X^T dY in isolation (rt_gemm, layout TN) over
+    M in {1024,4096,8192} x N in {512,4096,8192} x K (the batch) in
+    {1,...,16384}, f32 (3xTF32 tensor cores) and bf16 operands, f32 output,
+    split-K chosen by the library.  Entries N(0,1).  Each point is timed with
+    CUDA events around the GEMM alone, with L2 flushed (a 256 MB write)
+    before every repetition.  Roofline time = max(2MNK / peak,
+    ((M+N) K s_in + 4 M N) / HBM); the f32 peak is the bf16 figure / 2 (tf32
+    rate) / 3 (three products)."""
+    import torch
+
+    import rgpu_b200
+    from rgpu_b200 import gpu as G
+
+    pk = peaks()
+    gpu = rgpu_b200.Gpu(0)
+    dev = torch.device("cuda", 0)
+    st = torch.cuda.ExternalStream(gpu.stream(), device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4)
+    dtypes = args.sweep_dtypes.split(",")
+    ks = [int(k) for k in args.sweep_k.split(",")] if args.sweep_k else SWEEP_K
+    points = []
+    for dt in dtypes:
+        tdt = torch.bfloat16 if dt == "bf16" else torch.float32
+        s_in = 2 if dt == "bf16" else 4
+        peak = pk["bf16"] if dt == "bf16" else pk["bf16"] / 6.0
+        for m in SWEEP_M:
+            for n in SWEEP_N:
+                for k in ks:
+                    x = torch.randn((k, m), generator=gen, device=dev, dtype=torch.float32).to(tdt)
+                    dy = torch.randn((k, n), generator=gen, device=dev, dtype=torch.float32).to(tdt)
+                    c = torch.empty((m, n), device=dev, dtype=torch.float32)
+                    a = G.GemmArgs()
+                    a.layout, a.in_dtype, a.out_dtype = G.RT_TN, G.RT_BF16 if dt == "bf16" else G.RT_F32, G.RT_F32
+                    a.m, a.n, a.k = m, n, k
+                    a.a, a.lda, a.b, a.ldb, a.c, a.ldc = x.data_ptr(), m, dy.data_ptr(), n, c.data_ptr(), n
+                    a.split_k = 0
+                    wsb = gpu.gemm_workspace_size(a)
+                    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
+                    a.workspace, a.workspace_bytes = ws.data_ptr(), wsb
+                    torch.cuda.synchronize()
+                    for _ in range(2):
+                        gpu.gemm(a)
+                    gpu.sync()
+                    flops = 2.0 * m * n * k
+                    reps = max(3, min(20, int(2e12 / max(flops, 1.0))))
+                    times = []
+                    for _ in range(reps):
+                        flush.fill_(1)
+                        torch.cuda.synchronize()
+                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        e0.record(st)
+                        gpu.gemm(a)
+                        e1.record(st)
+                        gpu.sync()
+                        times.append(e0.elapsed_time(e1))
+                    ms = statistics.median(times)
+                    byts = (m + n) * k * s_in + 4.0 * m * n
+                    roof_ms = max(flops / (peak * 1e12), byts / (pk["hbm"] * 1e9)) * 1e3
+                    pt = {"dtype": dt, "M": m, "N": n, "K": k, "ms": round(ms, 5),
+                          "tflops": round(flops / (ms / 1e3) / 1e12, 2),
+                          "gbs": round(byts / (ms / 1e3) / 1e9, 1), "roofline_ms": round(roof_ms, 5),
+                          "frac": round(roof_ms / ms, 3),
+                          "bound": "tensor" if flops / (peak * 1e12) > byts / (pk["hbm"] * 1e9) else "hbm",
+                          "workspace_bytes": wsb}
+                    points.append(pt)
+                    print(json.dumps(pt), flush=True)
+                    del x, dy, c, ws
+    for dt in dtypes:
+        fr = [p["frac"] for p in points if p["dtype"] == dt]
+        if fr:
+            print(json.dumps({"summary": dt, "points": len(fr), "frac_median": statistics.median(fr),
+                              "frac_min": min(fr), "peak_source": pk["source"]}), flush=True)
     gpu.close()
 
 
@@ -233,7 +318,14 @@ def main():
     ap.add_argument("--mnk", type=int, nargs=3, default=[8192, 8192, 8192], metavar=("M", "N", "K"))
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--l2-group", type=int, default=0, help="GEMM raster group (tile rows), 0 = library default")
+    ap.add_argument("--gemm-dtype", default="bf16", choices=["bf16", "f32"], help="operand dtype of --gemm")
+    ap.add_argument("--sweep", action="store_true", help="dW = X^T dY sweep (BASELINE configs[3])")
+    ap.add_argument("--sweep-dtypes", default="f32,bf16")
+    ap.add_argument("--sweep-k", default="", help="comma-separated K values (default: the full sweep)")
     args = ap.parse_args()
+    if args.sweep:
+        run_dw_sweep(args)
+        return
     if args.gemm:
         run_gemm_only(args)
         return

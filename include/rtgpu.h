@@ -71,6 +71,11 @@ int rt_ctx_set_stream(rt_ctx* ctx, void* stream);
 /* Gpu::set_fast_gemm (gpu/mod.rs:442-448): 1 = tcgen05/TMA tensor-core GEMM
  * where the operands allow it (default), 0 = tiled SIMT GEMM everywhere. */
 int rt_ctx_set_fast_gemm(rt_ctx* ctx, int on);
+/* f32 GEMMs under set_fast_gemm(1): 1 = tensor cores as three tf32 products
+ * (3xTF32, about f32 accuracy; default), 0 = the SIMT f32 kernel.  Same
+ * switch family as Gpu::set_fast_gemm (gpu/mod.rs:442-448); the reference's
+ * f32 GEMMs have no tensor-core form.  RTGPU_F32_TENSOR=0 sets the default. */
+int rt_ctx_set_f32_tensor(rt_ctx* ctx, int on);
 /* Gpu::set_grupo_l2 (gpu/mod.rs:452-458): tile rows per L2 raster group. */
 int rt_ctx_set_l2_group(rt_ctx* ctx, int group);
 /* Number of kernels this context has launched so far (evidence counter). */

@@ -32,10 +32,15 @@
 namespace rt {
 namespace {
 using namespace tc;
-template <typename TIn, bool A_MN, bool B_MN, int BN>
+// X3 (f32 only, both operands K-major): the operands are [2][mn][k] hi/lo
+// planes read through 3-D maps, and the k loop runs three product segments
+// over the same k range: lo(A) hi(B), hi(A) lo(B), then hi(A) hi(B) (the
+// small terms first).
+template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    TcParams p) {
+    static_assert(!X3 || (sizeof(TIn) == 4 && !A_MN && !B_MN), "3xTF32 planes are f32 and K-major");
     using G = Geo<TIn, BN>;
     constexpr bool kTF32 = sizeof(TIn) == 4;
     constexpr int STAGES = G::STAGES;
@@ -107,22 +112,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t fb = smem_u32(&full[stage]);
                 mbar_expect_tx(fb, G::STAGE_BYTES);
                 last_phase[stage] = phase + 1;
-                const int k0 = kb * G::BK;
+                int k0 = kb * G::BK;
+                int plane_a = 0, plane_b = 0;
+                if constexpr (X3) {
+                    const int seg = kb / p.kb_seg;
+                    k0 = (kb - seg * p.kb_seg) * G::BK;
+                    plane_a = seg == 0;
+                    plane_b = seg == 1;
+                }
                 const uint32_t sa = smem_u32(smem_a + stage * G::A_BYTES);
                 const uint32_t sb = smem_u32(smem_b + stage * G::B_BYTES);
-                if (A_MN) {
-#pragma unroll
-                    for (int c = 0; c < BM / G::CHUNK; ++c)
-                        tma_load_2d(sa + c * (G::BK * 128), &tmap_a, m0 + c * G::CHUNK, k0, fb);
+                if constexpr (X3) {
+                    tma_load_3d(sa, &tmap_a, k0, m0, plane_a, fb);
+                    tma_load_3d(sb, &tmap_b, k0, n0, plane_b, fb);
                 } else {
-                    tma_load_2d(sa, &tmap_a, k0, m0, fb);
-                }
-                if (B_MN) {
+                    if (A_MN) {
 #pragma unroll
-                    for (int c = 0; c < BN / G::CHUNK; ++c)
-                        tma_load_2d(sb + c * (G::BK * 128), &tmap_b, n0 + c * G::CHUNK, k0, fb);
-                } else {
-                    tma_load_2d(sb, &tmap_b, k0, n0, fb);
+                        for (int c = 0; c < BM / G::CHUNK; ++c)
+                            tma_load_2d(sa + c * (G::BK * 128), &tmap_a, m0 + c * G::CHUNK, k0, fb);
+                    } else {
+                        tma_load_2d(sa, &tmap_a, k0, m0, fb);
+                    }
+                    if (B_MN) {
+#pragma unroll
+                        for (int c = 0; c < BN / G::CHUNK; ++c)
+                            tma_load_2d(sb + c * (G::BK * 128), &tmap_b, n0 + c * G::CHUNK, k0, fb);
+                    } else {
+                        tma_load_2d(sb, &tmap_b, k0, n0, fb);
+                    }
                 }
                 if (++stage == STAGES) {
                     stage = 0;
@@ -267,21 +284,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <typename TIn, bool A_MN, bool B_MN, int BN>
-int launch_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
+template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3>
+int launch_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X3Planes* x3) {
     using G = Geo<TIn, BN>;
     const bool bf16 = sizeof(TIn) == 2;
     CUtensorMap ta, tb;
-    // A: logical [m,k].  K-major storage [m][lda]; MN-major storage [k][lda].
-    if (A_MN)
-        RT_TRY(make_tmap(&ta, g.a, bf16, g.m, g.k, g.lda, G::CHUNK, G::BK));
-    else
-        RT_TRY(make_tmap(&ta, g.a, bf16, g.k, g.m, g.lda, G::BK, BM));
-    // B: logical [k,n].  K-major storage [n][ldb]; MN-major storage [k][ldb].
-    if (B_MN)
-        RT_TRY(make_tmap(&tb, g.b, bf16, g.n, g.k, g.ldb, G::CHUNK, G::BK));
-    else
-        RT_TRY(make_tmap(&tb, g.b, bf16, g.k, g.n, g.ldb, G::BK, BN));
+    if constexpr (X3) {
+        // hi/lo planes of the operands, both K-major: A [2][m][k], B [2][n][k]
+        RT_TRY(make_tmap_planes(&ta, x3->a, g.k, g.m, x3->lda, x3->a_plane, 2, G::BK, BM));
+        RT_TRY(make_tmap_planes(&tb, x3->b, g.k, g.n, x3->ldb, x3->b_plane, 2, G::BK, BN));
+    } else {
+        // A: logical [m,k].  K-major storage [m][lda]; MN-major storage [k][lda].
+        if (A_MN)
+            RT_TRY(make_tmap(&ta, g.a, bf16, g.m, g.k, g.lda, G::CHUNK, G::BK));
+        else
+            RT_TRY(make_tmap(&ta, g.a, bf16, g.k, g.m, g.lda, G::BK, BM));
+        // B: logical [k,n].  K-major storage [n][ldb]; MN-major storage [k][ldb].
+        if (B_MN)
+            RT_TRY(make_tmap(&tb, g.b, bf16, g.n, g.k, g.ldb, G::CHUNK, G::BK));
+        else
+            RT_TRY(make_tmap(&tb, g.b, bf16, g.k, g.n, g.ldb, G::BK, BN));
+    }
 
     TcParams p{};
     GemmDesc gr = g;  // descriptor for the split-K reduction (effective split count)
@@ -291,6 +314,11 @@ int launch_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     p.tiles_m = (int)((g.m + BM - 1) / BM);
     p.tiles_n = (int)((g.n + BN - 1) / BN);
     p.kblocks = (int)((g.k + G::BK - 1) / G::BK);
+    p.kb_seg = 0;
+    if constexpr (X3) {
+        p.kb_seg = p.kblocks;
+        p.kblocks *= 3;
+    }
     int splits = g.split_k > 1 ? g.split_k : 1;
     if (splits > p.kblocks) splits = p.kblocks;
     p.kb_per_split = (p.kblocks + splits - 1) / splits;
@@ -312,34 +340,34 @@ int launch_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     int64_t tiles = (int64_t)p.tiles_m * p.tiles_n * p.splits;
     int sms = g.max_sms > 0 && g.max_sms < ctx->sm_count ? g.max_sms : ctx->sm_count;
     int grid = (int)(tiles < sms ? tiles : sms);
-    gemm_tc_kernel<TIn, A_MN, B_MN, BN><<<grid, kThreads, G::SMEM, st>>>(ta, tb, p);
+    gemm_tc_kernel<TIn, A_MN, B_MN, BN, X3><<<grid, kThreads, G::SMEM, st>>>(ta, tb, p);
     count_launch(ctx);
     RT_CUDA(cudaGetLastError());
     if (splits > 1) return launch_splitk_reduce(ctx, gr, st);
     return RT_OK;
 }
 
-template <typename TIn, bool A_MN, bool B_MN, int BN>
+template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3>
 int set_smem_attr() {
-    RT_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<TIn, A_MN, B_MN, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 Geo<TIn, BN>::SMEM));
+    RT_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<TIn, A_MN, B_MN, BN, X3>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<TIn, BN>::SMEM));
     return RT_OK;
 }
 
-template <typename TIn, int BN>
+template <typename TIn, int BN, bool X3 = false>
 int set_smem_attrs_bn() {
-    RT_TRY((set_smem_attr<TIn, false, true, BN>()));
-    RT_TRY((set_smem_attr<TIn, false, false, BN>()));
-    RT_TRY((set_smem_attr<TIn, true, true, BN>()));
+    RT_TRY((set_smem_attr<TIn, false, true, BN, X3>()));
+    RT_TRY((set_smem_attr<TIn, false, false, BN, X3>()));
+    RT_TRY((set_smem_attr<TIn, true, true, BN, X3>()));
     return RT_OK;
 }
 
-template <typename TIn, int BN>
-int launch_layout(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
+template <typename TIn, int BN, bool X3 = false>
+int launch_layout(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X3Planes* x3 = nullptr) {
     switch (g.layout) {
-        case RT_NN: return launch_variant<TIn, false, true, BN>(ctx, g, st);
-        case RT_NT: return launch_variant<TIn, false, false, BN>(ctx, g, st);
-        case RT_TN: return launch_variant<TIn, true, true, BN>(ctx, g, st);
+        case RT_NN: return launch_variant<TIn, false, true, BN, X3>(ctx, g, st, x3);
+        case RT_NT: return launch_variant<TIn, false, false, BN, X3>(ctx, g, st, x3);
+        case RT_TN: return launch_variant<TIn, true, true, BN, X3>(ctx, g, st, x3);
     }
     return fail(RT_ERR_INVALID, "unknown layout");
 }
@@ -368,6 +396,22 @@ bool gemm_tc_supported(const rt_ctx* ctx, const GemmDesc& g) {
     if ((g.lda * es) % 16 || (g.ldb * es) % 16 || (g.ldc * os) % 16) return false;
     if (g.epi == RT_EPI_RELU_MASK && (!aligned16(g.mask) || (g.ldmask * os) % 16)) return false;
     return true;
+}
+
+// f32 GEMM from split operand planes (gemm_x3.cu prepares them).
+// Both planes are K-major whatever g.layout is (tcgen05 takes MN-major tf32
+// operands only in the 32-byte-atom swizzle, so the split transposes instead).
+int gemm_tc_x3_init() {
+    RT_TRY((set_smem_attr<float, false, false, 64, true>()));
+    RT_TRY((set_smem_attr<float, false, false, 128, true>()));
+    RT_TRY((set_smem_attr<float, false, false, 256, true>()));
+    return RT_OK;
+}
+
+int launch_gemm_tc_x3(rt_ctx* ctx, const GemmDesc& g, const X3Planes& x3, cudaStream_t st) {
+    if (g.n <= 64) return launch_variant<float, false, false, 64, true>(ctx, g, st, &x3);
+    if (g.n <= 128) return launch_variant<float, false, false, 128, true>(ctx, g, st, &x3);
+    return launch_variant<float, false, false, 256, true>(ctx, g, st, &x3);
 }
 
 int launch_gemm_tc(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {

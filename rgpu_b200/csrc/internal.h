@@ -6,6 +6,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <string>
+#include <vector>
 
 #include "optim_math.cuh"
 #include "rtgpu.h"
@@ -52,6 +53,13 @@ struct rt_ctx {
     int* dev_err = nullptr;  // [4] ints: first device error code, detail
     bool fast_gemm = true;
     bool pair_gemm = true;  // two-CTA tcgen05 tiles where the problem is large enough
+    bool f32_tensor = true;  // f32 GEMMs on the tensor cores (3xTF32) when fast_gemm is on
+    // Grow-only workspace for the hi/lo operand copies of 3xTF32 GEMMs that
+    // bring none of their own.  A replaced buffer is kept until the context
+    // is destroyed: graphs captured earlier may still reference it.
+    float* x3_scratch = nullptr;
+    size_t x3_scratch_bytes = 0;
+    std::vector<void*> x3_retired;
     int l2_group = 8;
     uint64_t launches = 0;
     char name[256] = {0};
@@ -84,6 +92,9 @@ struct GemmDesc {
     float* workspace;  // split_k * m * n f32 when split_k > 1
     OptFuse opt;       // optimiser applied to theta[i*ldc + j] with gradient C[i,j] (kind 0 = none)
     int max_sms;       // persistent-grid cap (0 = every SM); leaves SMs to concurrent collectives
+    float* x3_ws;      // hi/lo operand copies for the 3xTF32 GEMM (null = context scratch)
+    size_t x3_ws_bytes;
+    bool no_alloc;     // the call may not allocate device memory (3xTF32 then needs a ready workspace)
 };
 
 // Kernel launchers: enqueue on `stream`, return RT_OK or an error code.
@@ -96,6 +107,22 @@ int gemm_tc_init(rt_ctx* ctx);
 int gemm_tc2_init(rt_ctx* ctx);
 bool gemm_tc2_wanted(const rt_ctx* ctx, const GemmDesc& g);
 int launch_gemm_tc2(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream);
+// f32 GEMM as three tf32 tcgen05 products (lo*hi + hi*lo + hi*hi); `ws`
+// holds the split operand copies (gemm_x3_workspace_bytes).
+bool gemm_x3_supported(const rt_ctx* ctx, const GemmDesc& g);
+size_t gemm_x3_workspace_bytes(const GemmDesc& g);
+int launch_gemm_x3(rt_ctx* ctx, const GemmDesc& g, float* ws, size_t ws_bytes, cudaStream_t stream);
+int gemm_x3_init(rt_ctx* ctx);
+// Operand planes of a 3xTF32 GEMM: A as [2][m][lda] and B as [2][n][ldb]
+// f32, both K-major (plane 0 = hi, plane 1 = lo).
+struct X3Planes {
+    const float* a;
+    int64_t lda, a_plane;
+    const float* b;
+    int64_t ldb, b_plane;
+};
+int gemm_tc_x3_init();
+int launch_gemm_tc_x3(rt_ctx* ctx, const GemmDesc& g, const X3Planes& x3, cudaStream_t stream);
 int launch_splitk_reduce(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream);
 
 int launch_xent(rt_ctx* ctx, const float* logits, int64_t ldz, const uint32_t* labels, int64_t n,

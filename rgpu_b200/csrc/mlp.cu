@@ -91,6 +91,10 @@ struct rt_mlp {
     int last_slot = 0;
     float* loss_rows = nullptr;
     OptScalars* opt = nullptr;
+    // f32 plans: hi/lo operand planes of the 3xTF32 GEMMs, sized for the
+    // largest GEMM of the step (the GEMMs run one after another on one stream)
+    float* x3_ws = nullptr;
+    size_t x3_ws_bytes = 0;
     std::vector<void*> allocs;
     cudaStream_t copy_stream = nullptr;
 
@@ -217,6 +221,8 @@ struct Enqueuer {
             g.epi = last ? RT_EPI_BIAS : RT_EPI_BIAS_RELU;
             g.bias = P.b;
             g.split_k = 1;
+            g.x3_ws = m->x3_ws;
+            g.x3_ws_bytes = m->x3_ws_bytes;
             RT_TRY(run_gemm(m->ctx, g, st, 0));
             RT_TRY(mark(last ? "fwd_gemm_bias" : "fwd_gemm_bias_relu", 2.0 * m->n * P.d * P.u));
         }
@@ -256,6 +262,8 @@ struct Enqueuer {
             g.split_k = P.split_dw;
             g.workspace = P.ws;
             g.max_sms = backward_sms();
+            g.x3_ws = m->x3_ws;
+            g.x3_ws_bytes = m->x3_ws_bytes;
             RT_TRY(run_gemm(m->ctx, g, st, P.ws_bytes));
             RT_TRY(mark("dw_gemm", 2.0 * m->n * P.d * P.u));
             if (m->comm) {
@@ -287,6 +295,8 @@ struct Enqueuer {
                 h.ldmask = Q.ld_act;
                 h.split_k = 1;
                 h.max_sms = backward_sms();
+                h.x3_ws = m->x3_ws;
+                h.x3_ws_bytes = m->x3_ws_bytes;
                 RT_TRY(run_gemm(m->ctx, h, st, 0));
                 RT_TRY(mark("dx_gemm_relu_mask", 2.0 * m->n * P.d * P.u));
             }
@@ -487,7 +497,8 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
         int split = 1;
         if (tiles * 4 < (int64_t)ctx->sm_count * 3) {
             int64_t sp = (int64_t)ctx->sm_count / tiles;
-            int64_t kb = (m->n + 63) / 64;
+            // k blocks of the tensor-core loop (f32: three 32-deep 3xTF32 segments)
+            int64_t kb = m->adt == RT_F32 ? 3 * ((m->n + 31) / 32) : (m->n + 63) / 64;
             if (sp > kb / 4) sp = kb / 4;
             if (sp > 16) sp = 16;
             split = sp < 1 ? 1 : (int)sp;
@@ -497,6 +508,22 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
             P.ws_bytes = (size_t)split * (P.d + 1) * P.u * 4;
             if ((s = dalloc(m, (void**)&P.ws, P.ws_bytes))) return bail(s);
         }
+    }
+    if (m->adt == RT_F32 && ctx->fast_gemm && ctx->f32_tensor) {
+        size_t need = 0;
+        for (int l = 0; l < nl; ++l) {
+            const PlanLayer& P = m->L[l];
+            GemmDesc f{}, w{}, x{};
+            f.layout = RT_NN, f.m = m->n, f.n = P.u, f.k = P.d;      // forward
+            w.layout = RT_TN, w.m = P.d + 1, w.n = P.u, w.k = m->n;  // [dW; db]
+            x.layout = RT_NT, x.m = m->n, x.n = P.d, x.k = P.u;      // dX
+            for (const GemmDesc* g : {&f, &w, &x}) {
+                size_t b = gemm_x3_workspace_bytes(*g);
+                if (b > need) need = b;
+            }
+        }
+        if ((s = dalloc(m, (void**)&m->x3_ws, need))) return bail(s);
+        m->x3_ws_bytes = need;
     }
     if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) return bail(fail(RT_ERR_CUDA, "plan setup sync failed"));
     *out = m;

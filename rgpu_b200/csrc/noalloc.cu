@@ -99,6 +99,7 @@ int rt_matmul_split_k_noalloc(rt_ctx* ctx, const rt_tensor* a, const rt_tensor* 
     g.epi = RT_EPI_NONE;
     g.split_k = slices;
     g.workspace = scratch;
+    g.no_alloc = true;  // f32 operands stay on the SIMT kernel (the 3xTF32 path needs an operand workspace)
     return run_gemm(ctx, g, ctx->stream, kScratchFloats * sizeof(float));
 }
 

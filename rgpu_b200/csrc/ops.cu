@@ -37,11 +37,35 @@ static int choose_split(const rt_ctx* ctx, const GemmDesc& g) {
     int64_t tiles = ((g.m + 127) / 128) * ((g.n + 255) / 256);
     if (tiles <= 0) return 1;
     if (tiles * 4 >= (int64_t)ctx->sm_count * 3) return 1;
-    int64_t kblocks = (g.k + 63) / 64;
+    // k blocks of the tensor-core loop: 64 deep for bf16, three 32-deep
+    // segments for the 3xTF32 f32 path
+    int64_t kblocks = g.in_dtype == RT_F32 ? 3 * ((g.k + 31) / 32) : (g.k + 63) / 64;
     int64_t s = (int64_t)ctx->sm_count / tiles;
     if (s > kblocks / 4) s = kblocks / 4;
     if (s > 16) s = 16;
     return s < 1 ? 1 : (int)s;
+}
+
+// The context's 3xTF32 operand workspace, grown to `need` bytes unless
+// `stream` is being captured (cudaMalloc is not allowed there); the caller
+// takes the SIMT kernel when what exists is too small.
+static int x3_context_scratch(rt_ctx* ctx, cudaStream_t stream, size_t need, float** ws, size_t* have) {
+    if (ctx->x3_scratch_bytes < need) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        RT_CUDA(cudaStreamIsCapturing(stream, &cs));
+        if (cs == cudaStreamCaptureStatusNone) {
+            const size_t unit = size_t(64) << 20;
+            const size_t bytes = (need + unit - 1) / unit * unit;
+            void* p = nullptr;
+            RT_CUDA(cudaMalloc(&p, bytes));
+            if (ctx->x3_scratch) ctx->x3_retired.push_back(ctx->x3_scratch);
+            ctx->x3_scratch = static_cast<float*>(p);
+            ctx->x3_scratch_bytes = bytes;
+        }
+    }
+    *ws = ctx->x3_scratch;
+    *have = ctx->x3_scratch_bytes;
+    return RT_OK;
 }
 
 int run_gemm(rt_ctx* ctx, GemmDesc g, cudaStream_t stream, size_t ws_bytes) {
@@ -58,6 +82,14 @@ int run_gemm(rt_ctx* ctx, GemmDesc g, cudaStream_t stream, size_t ws_bytes) {
                  ws_bytes, (size_t)g.split_k * g.m * g.n * 4);
     }
     if (ctx->fast_gemm && gemm_tc_supported(ctx, g)) return launch_gemm_tc(ctx, g, stream);
+    if (ctx->fast_gemm && !g.no_alloc && gemm_x3_supported(ctx, g)) {
+        const size_t need = gemm_x3_workspace_bytes(g);
+        float* ws = g.x3_ws;
+        size_t have = g.x3_ws_bytes;
+        if (!ws) RT_TRY(x3_context_scratch(ctx, stream, need, &ws, &have));
+        if (ws && have >= need) return launch_gemm_x3(ctx, g, ws, have, stream);
+        // no workspace could be had (a capture in progress): the SIMT kernel
+    }
     return launch_gemm_simt(ctx, g, stream);
 }
 
@@ -122,6 +154,7 @@ int rt_gemm(rt_ctx* ctx, const rt_gemm_args* a) {
 size_t rt_gemm_workspace_size(rt_ctx* ctx, const rt_gemm_args* a) {
     if (!ctx || !a) return 0;
     GemmDesc g{};
+    g.in_dtype = a->in_dtype;
     g.m = a->m;
     g.n = a->n;
     g.k = a->k;

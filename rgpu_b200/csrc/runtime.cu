@@ -83,8 +83,11 @@ int rt_ctx_create(int device, rt_ctx** out) {
     cudaStreamSynchronize(c->stream);
     const char* pair_env = getenv("RTGPU_PAIR_GEMM");
     c->pair_gemm = !(pair_env && pair_env[0] == '0');
+    const char* f32_env = getenv("RTGPU_F32_TENSOR");
+    c->f32_tensor = !(f32_env && f32_env[0] == '0');
     int st = gemm_tc_init(c);
     if (st == RT_OK) st = gemm_tc2_init(c);
+    if (st == RT_OK) st = gemm_x3_init(c);
     if (st != RT_OK) {
         cudaFree(c->dev_err);
         cudaStreamDestroy(c->own_stream);
@@ -100,6 +103,8 @@ int rt_ctx_destroy(rt_ctx* ctx) {
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
     if (ctx->dev_err) cudaFree(ctx->dev_err);
+    if (ctx->x3_scratch) cudaFree(ctx->x3_scratch);
+    for (void* p : ctx->x3_retired) cudaFree(p);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return RT_OK;
@@ -129,6 +134,12 @@ int rt_ctx_set_stream(rt_ctx* ctx, void* stream) {
 int rt_ctx_set_fast_gemm(rt_ctx* ctx, int on) {
     RT_CHECK(ctx, "ctx is NULL");
     ctx->fast_gemm = on != 0;
+    return RT_OK;
+}
+
+int rt_ctx_set_f32_tensor(rt_ctx* ctx, int on) {
+    RT_CHECK(ctx, "ctx is NULL");
+    ctx->f32_tensor = on != 0;
     return RT_OK;
 }
 

@@ -80,6 +80,17 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// 3-D box load (x, y, plane): the 3xTF32 GEMM reads its hi and lo operand
+// planes through one map whose third dimension selects the plane.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -166,6 +177,7 @@ struct TcParams {
     int out_bf16;
     int* err;
     OptFuse opt;
+    int kb_seg;  // 3xTF32: k blocks per product segment (the k loop runs 3 * kb_seg blocks); 0 otherwise
 };
 
 // Stage geometry shared by host and device.
@@ -321,6 +333,26 @@ inline int make_tmap(CUtensorMap* map, const void* base, bool bf16, int64_t inne
     if (r != CUDA_SUCCESS)
         return fail(RT_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d): inner %lld outer %lld ld %lld box %dx%d",
                     (int)r, (long long)inner, (long long)outer, (long long)ld, box_inner, box_outer);
+    return RT_OK;
+}
+
+// 3-D f32 tensor of `planes` [outer, inner] planes, row stride `ld`, plane
+// stride `plane` elements; box (box_inner x box_outer x 1), 128-byte swizzle.
+inline int make_tmap_planes(CUtensorMap* map, const float* base, int64_t inner, int64_t outer, int64_t ld,
+                            int64_t plane, int planes, int box_inner, int box_outer) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(RT_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled is not available from the driver");
+    cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)planes};
+    cuuint64_t strides[2] = {(cuuint64_t)(ld * 4), (cuuint64_t)(plane * 4)};
+    cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(RT_ERR_INVALID,
+                    "cuTensorMapEncodeTiled (planes) failed (%d): inner %lld outer %lld ld %lld plane %lld box %dx%d",
+                    (int)r, (long long)inner, (long long)outer, (long long)ld, (long long)plane, box_inner, box_outer);
     return RT_OK;
 }
 

@@ -69,6 +69,7 @@ _SIGS = [
     ("rt_ctx_stream", C.c_void_p, [C.c_void_p]),
     ("rt_ctx_set_stream", C.c_int, [C.c_void_p, C.c_void_p]),
     ("rt_ctx_set_fast_gemm", C.c_int, [C.c_void_p, C.c_int]),
+    ("rt_ctx_set_f32_tensor", C.c_int, [C.c_void_p, C.c_int]),
     ("rt_ctx_set_l2_group", C.c_int, [C.c_void_p, C.c_int]),
     ("rt_ctx_launch_count", C.c_int, [C.c_void_p, C.POINTER(C.c_uint64)]),
     ("rt_host_alloc", C.c_int, [C.c_size_t, C.POINTER(C.c_void_p)]),
@@ -273,6 +274,10 @@ class Gpu:
 
     def set_fast_gemm(self, on: bool):
         _check(lib().rt_ctx_set_fast_gemm(self.handle, int(bool(on))))
+
+    def set_f32_tensor(self, on: bool):
+        """f32 GEMMs as 3xTF32 on the tensor cores (True) or on the SIMT kernel."""
+        _check(lib().rt_ctx_set_f32_tensor(self.handle, int(bool(on))))
 
     def set_grupo_l2(self, group: int):
         _check(lib().rt_ctx_set_l2_group(self.handle, int(group)))

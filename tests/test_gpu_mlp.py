@@ -107,8 +107,12 @@ def test_config1_f32_batch32_sgd(gpu):
     mlp = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 32, 0.01, optimizer="sgd")
     mlp.step(gpu.upload(x), rgpu_b200.upload_labels(gpu, labels))
     model.train_step(x, labels, oracle.OPT_SGD, 0.01, threads=4)
-    for wc, wg in zip(model.params(), mlp.weights()):
-        assert rel_l2(wg, wc) < 1e-6
+    for i, (wc, wg) in enumerate(zip(model.params(), mlp.weights())):
+        # W = W0 - lr g agrees far inside the gradient bar; b starts at zero,
+        # so b = -lr db carries the db gradient's own error (<= 1e-4; the
+        # column sum of delta cancels, which magnifies the 3xTF32 error).
+        bound = 1e-6 if i % 2 == 0 else 1e-4
+        assert rel_l2(wg, wc) < bound, f"param {i}: {rel_l2(wg, wc):.3e}"
 
 
 def test_config2_f32_batch2048(gpu):

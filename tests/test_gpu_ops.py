@@ -110,6 +110,71 @@ def test_tensor_core_gemm_accuracy_deep_k(gpu, m, n, k):
         assert e <= bound, f"{name} {m}x{n}x{k}: {e:.2e} > {bound:.2e}"
 
 
+@pytest.mark.parametrize("m,n,k", [(64, 1000, 8192), (128, 256, 4096), (300, 200, 2048), (513, 1024, 2048),
+                                   (2048, 10, 1024), (37, 23, 19)])
+def test_f32_tensor_core_gemm_tracks_the_exact_product(gpu, m, n, k):
+    # f32 operands on the tensor cores as three tf32 products (3xTF32),
+    # against the exact f64 product.  The split itself loses < 2^-20 per
+    # product; the rest is the tensor cores' truncating f32 accumulation,
+    # which grows linearly with the number of 8-deep MMA steps (k / 8 per
+    # segment, twice the bf16 path's k / 16): measured 1.95e-5 at k = 8192,
+    # inside the 1e-4 f32 gradient bar up to k ~ 40000.  The SIMT f32 kernel
+    # (round-to-nearest FMA) is held to the bf16 test's tighter bound.
+    rng = np.random.default_rng(k + m)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    ref = a.astype(np.float64) @ b.astype(np.float64)
+    ga, gb = gpu.upload(a), gpu.upload(b)
+    gat, gbt = gpu.upload(np.ascontiguousarray(a.T)), gpu.upload(np.ascontiguousarray(b.T))
+    try:
+        for tensor in (True, False):
+            gpu.set_f32_tensor(tensor)
+            bound = 1e-6 + (3e-9 if tensor else 1.6e-9) * k
+            for name, fn, x, y in (("NN", gpu.matmul, ga, gb), ("TN", gpu.matmul_at_b, gat, gb),
+                                   ("NT", gpu.matmul_a_bt, ga, gbt)):
+                c = gpu.zeros((m, n))
+                fn(x, y, c)
+                e = rel_l2(gpu.download(c), ref)
+                assert e <= bound, f"{name} {m}x{n}x{k} tensor={tensor}: {e:.2e} > {bound:.2e}"
+    finally:
+        gpu.set_f32_tensor(True)
+
+
+def test_f32_gemm_runs_on_the_tensor_cores(gpu):
+    # An aligned f32 GEMM is two launches on the tensor-core path (operand
+    # split + tcgen05 GEMM) and one on the SIMT path.
+    a, b = _ab(256, 512, 128)
+    ga, gb, c = gpu.upload(a), gpu.upload(b), gpu.zeros((256, 512))
+    try:
+        counts = {}
+        for tensor in (True, False):
+            gpu.set_f32_tensor(tensor)
+            before = gpu.launch_count()
+            gpu.matmul(ga, gb, c)
+            gpu.sync()
+            counts[tensor] = gpu.launch_count() - before
+            assert erro_rel(oracle.matmul(a, b), gpu.download(c)) < 1e-5
+        assert counts == {True: 2, False: 1}, counts
+    finally:
+        gpu.set_f32_tensor(True)
+
+
+def test_f32_tensor_core_gemm_non_finite_inputs(gpu):
+    # A non-finite operand makes its output row non-finite, as in an f32 GEMM
+    # (inf may come out as NaN: the split's hi(A) lo(B) product is inf * 0),
+    # and leaves every other row exact.
+    a = np.ones((128, 64), np.float32)
+    b = np.ones((64, 128), np.float32)
+    a[3, 5] = np.inf
+    a[7, 9] = np.nan
+    c = gpu.zeros((128, 128))
+    gpu.matmul(gpu.upload(a), gpu.upload(b), c)
+    got = gpu.download(c)
+    assert not np.isfinite(got[3]).any() and np.isnan(got[7]).all()
+    rest = np.delete(got, [3, 7], axis=0)
+    assert np.array_equal(rest, np.full_like(rest, 64.0))
+
+
 def test_bf16_output_store(gpu):
     a, b = _ab(96, 80, 48)
     ga, gb = gpu.upload(a, "bf16"), gpu.upload(b, "bf16")
