@@ -409,6 +409,7 @@ int gemm_tc_x3_init() {
 }
 
 int launch_gemm_tc_x3(rt_ctx* ctx, const GemmDesc& g, const X3Planes& x3, cudaStream_t st) {
+    if (gemm_tc2_x3_wanted(ctx, g)) return launch_gemm_tc2_x3(ctx, g, x3, st);
     if (g.n <= 64) return launch_variant<float, false, false, 64, true>(ctx, g, st, &x3);
     if (g.n <= 128) return launch_variant<float, false, false, 128, true>(ctx, g, st, &x3);
     return launch_variant<float, false, false, 256, true>(ctx, g, st, &x3);

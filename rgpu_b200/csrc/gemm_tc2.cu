@@ -18,6 +18,11 @@
 //     peer's, addressed through mapa); the peer's epilogue warps arrive
 //     remotely on the leader's TMEM-empty barrier.
 // Every CTA loads its own tiles: no load is shared between CTAs.
+//
+// X3 form (f32 operands, both K-major hi/lo planes from gemm_x3.cu): tf32
+// MMAs over three k segments, as in the one-CTA kernel; per 32-deep k block a
+// CTA loads 16 KB of A and 16 KB of B for 2 x 128 x 256 x 32 MMA work, half
+// the L2-to-SM bytes per FLOP of the one-CTA 128 x 256 tile.
 #include "tc_common.cuh"
 
 namespace rt {
@@ -66,19 +71,38 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y,
+                                                 int32_t z, uint32_t leader_bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(leader_bar)
+        : "memory");
+}
+
 __device__ __forceinline__ void tc_commit_pair(uint32_t cluster_bar) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
                  : "memory");
 }
 
+template <bool kTF32>
 __device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                             uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
+    if constexpr (kTF32) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    }
 }
 
 template <typename TIn, int BN>
@@ -96,13 +120,15 @@ struct Geo2 {
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
 };
 
-template <typename TIn, bool A_MN, bool B_MN, int BN>
+template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false>
 __global__ void __launch_bounds__(kThreads2, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     TcParams p) {
+    static_assert(!X3 || (sizeof(TIn) == 4 && !A_MN && !B_MN), "3xTF32 planes are f32 and K-major");
     using G = Geo2<TIn, BN>;
+    constexpr bool kTF32 = sizeof(TIn) == 4;
     constexpr int STAGES = G::STAGES;
-    constexpr uint32_t IDESC = make_idesc(false, A_MN, B_MN, BN, BM2);
+    constexpr uint32_t IDESC = make_idesc(kTF32, A_MN, B_MN, BN, BM2);
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -180,22 +206,30 @@ __global__ void __launch_bounds__(kThreads2, 1)
                 const uint32_t leader_full = mapa_shared(smem_u32(&full[stage]), 0);
                 if (rank == 0) mbar_expect_tx(smem_u32(&full[stage]), 2 * G::STAGE_BYTES);
                 last_phase[stage] = phase + 1;
-                const int k0 = kb * G::BK;
                 const uint32_t sa = smem_u32(smem_a + stage * G::A_BYTES);
                 const uint32_t sb = smem_u32(smem_b + stage * G::B_BYTES);
-                if (A_MN) {
-#pragma unroll
-                    for (int c = 0; c < 128 / G::CHUNK; ++c)
-                        tma_load_2d_pair(sa + c * (G::BK * 128), &tmap_a, m0 + c * G::CHUNK, k0, leader_full);
+                if constexpr (X3) {
+                    // segments: lo(A) hi(B), hi(A) lo(B), hi(A) hi(B)
+                    const int seg = kb / p.kb_seg;
+                    const int k0 = (kb - seg * p.kb_seg) * G::BK;
+                    tma_load_3d_pair(sa, &tmap_a, k0, m0, seg == 0 ? 1 : 0, leader_full);
+                    tma_load_3d_pair(sb, &tmap_b, k0, n0, seg == 1 ? 1 : 0, leader_full);
                 } else {
-                    tma_load_2d_pair(sa, &tmap_a, k0, m0, leader_full);
-                }
-                if (B_MN) {
+                    const int k0 = kb * G::BK;
+                    if (A_MN) {
 #pragma unroll
-                    for (int c = 0; c < G::BNH / G::CHUNK; ++c)
-                        tma_load_2d_pair(sb + c * (G::BK * 128), &tmap_b, n0 + c * G::CHUNK, k0, leader_full);
-                } else {
-                    tma_load_2d_pair(sb, &tmap_b, k0, n0, leader_full);
+                        for (int c = 0; c < 128 / G::CHUNK; ++c)
+                            tma_load_2d_pair(sa + c * (G::BK * 128), &tmap_a, m0 + c * G::CHUNK, k0, leader_full);
+                    } else {
+                        tma_load_2d_pair(sa, &tmap_a, k0, m0, leader_full);
+                    }
+                    if (B_MN) {
+#pragma unroll
+                        for (int c = 0; c < G::BNH / G::CHUNK; ++c)
+                            tma_load_2d_pair(sb + c * (G::BK * 128), &tmap_b, n0 + c * G::CHUNK, k0, leader_full);
+                    } else {
+                        tma_load_2d_pair(sb, &tmap_b, k0, n0, leader_full);
+                    }
                 }
                 if (++stage == STAGES) {
                     stage = 0;
@@ -241,7 +275,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
                 for (int kk = 0; kk < G::BK / G::UK; ++kk) {
                     uint64_t ad = smem_desc(sa + kk * A_KSTEP, A_LBO, 1024);
                     uint64_t bd = smem_desc(sb + kk * B_KSTEP, B_LBO, 1024);
-                    tc_mma_pair(d_tmem, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+                    tc_mma_pair<kTF32>(d_tmem, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
                 }
                 // release the stage in both CTAs once these MMAs have read it
                 tc_commit_pair(smem_u32(&empty[stage]));
@@ -343,19 +377,24 @@ __global__ void __launch_bounds__(kThreads2, 1)
     }
 }
 
-template <typename TIn, bool A_MN, bool B_MN, int BN>
-int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
+template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false>
+int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X3Planes* x3 = nullptr) {
     using G = Geo2<TIn, BN>;
     const bool bf16 = sizeof(TIn) == 2;
     CUtensorMap ta, tb;
-    if (A_MN)
-        RT_TRY(make_tmap(&ta, g.a, bf16, g.m, g.k, g.lda, G::CHUNK, G::BK));
-    else
-        RT_TRY(make_tmap(&ta, g.a, bf16, g.k, g.m, g.lda, G::BK, 128));
-    if (B_MN)
-        RT_TRY(make_tmap(&tb, g.b, bf16, g.n, g.k, g.ldb, G::CHUNK, G::BK));
-    else
-        RT_TRY(make_tmap(&tb, g.b, bf16, g.k, g.n, g.ldb, G::BK, G::BNH));
+    if constexpr (X3) {
+        RT_TRY(make_tmap_planes(&ta, x3->a, g.k, g.m, x3->lda, x3->a_plane, 2, G::BK, 128));
+        RT_TRY(make_tmap_planes(&tb, x3->b, g.k, g.n, x3->ldb, x3->b_plane, 2, G::BK, G::BNH));
+    } else {
+        if (A_MN)
+            RT_TRY(make_tmap(&ta, g.a, bf16, g.m, g.k, g.lda, G::CHUNK, G::BK));
+        else
+            RT_TRY(make_tmap(&ta, g.a, bf16, g.k, g.m, g.lda, G::BK, 128));
+        if (B_MN)
+            RT_TRY(make_tmap(&tb, g.b, bf16, g.n, g.k, g.ldb, G::CHUNK, G::BK));
+        else
+            RT_TRY(make_tmap(&tb, g.b, bf16, g.k, g.n, g.ldb, G::BK, G::BNH));
+    }
 
     TcParams p{};
     GemmDesc gr = g;
@@ -365,6 +404,11 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     p.tiles_m = (int)((g.m + BM2 - 1) / BM2);
     p.tiles_n = (int)((g.n + BN - 1) / BN);
     p.kblocks = (int)((g.k + G::BK - 1) / G::BK);
+    p.kb_seg = 0;
+    if constexpr (X3) {
+        p.kb_seg = p.kblocks;
+        p.kblocks *= 3;
+    }
     int splits = g.split_k > 1 ? g.split_k : 1;
     if (splits > p.kblocks) splits = p.kblocks;
     p.kb_per_split = (p.kblocks + splits - 1) / splits;
@@ -399,7 +443,7 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    RT_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<TIn, A_MN, B_MN, BN>, ta, tb, p));
+    RT_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3>, ta, tb, p));
     count_launch(ctx);
     if (splits > 1) return launch_splitk_reduce(ctx, gr, st);
     return RT_OK;
@@ -415,10 +459,10 @@ int launch_pair_layout(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     return fail(RT_ERR_INVALID, "unknown layout");
 }
 
-template <bool A_MN, bool B_MN, int BN>
+template <bool A_MN, bool B_MN, int BN, typename TIn = __nv_bfloat16, bool X3 = false>
 int set_attr_pair() {
-    RT_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<__nv_bfloat16, A_MN, B_MN, BN>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Geo2<__nv_bfloat16, BN>::SMEM));
+    RT_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Geo2<TIn, BN>::SMEM));
     return RT_OK;
 }
 
@@ -432,6 +476,8 @@ int gemm_tc2_init(rt_ctx* ctx) {
     RT_TRY((set_attr_pair<false, true, 256>()));
     RT_TRY((set_attr_pair<false, false, 256>()));
     RT_TRY((set_attr_pair<true, true, 256>()));
+    RT_TRY((set_attr_pair<false, false, 128, float, true>()));
+    RT_TRY((set_attr_pair<false, false, 256, float, true>()));
     return RT_OK;
 }
 
@@ -444,6 +490,19 @@ bool gemm_tc2_wanted(const rt_ctx* ctx, const GemmDesc& g) {
 int launch_gemm_tc2(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     if (g.n <= 128) return launch_pair_layout<128>(ctx, g, st);
     return launch_pair_layout<256>(ctx, g, st);
+}
+
+bool gemm_tc2_x3_wanted(const rt_ctx* ctx, const GemmDesc& g) {
+    return ctx->pair_gemm && g.m >= 256 && g.n > 64;
+}
+
+// 3xTF32 from K-major hi/lo planes.  256-wide column tiles unless they leave
+// more than half of the SM pairs idle, then 128-wide ones.
+int launch_gemm_tc2_x3(rt_ctx* ctx, const GemmDesc& g, const X3Planes& x3, cudaStream_t st) {
+    const int64_t tiles256 = ((g.m + BM2 - 1) / BM2) * ((g.n + 255) / 256) * (g.split_k > 1 ? g.split_k : 1);
+    if (g.n <= 128 || tiles256 * 4 < ctx->sm_count)
+        return launch_pair_variant<float, false, false, 128, true>(ctx, g, st, &x3);
+    return launch_pair_variant<float, false, false, 256, true>(ctx, g, st, &x3);
 }
 
 }  // namespace rt

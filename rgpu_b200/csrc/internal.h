@@ -123,7 +123,14 @@ struct X3Planes {
 };
 int gemm_tc_x3_init();
 int launch_gemm_tc_x3(rt_ctx* ctx, const GemmDesc& g, const X3Planes& x3, cudaStream_t stream);
+bool gemm_tc2_x3_wanted(const rt_ctx* ctx, const GemmDesc& g);
+int launch_gemm_tc2_x3(rt_ctx* ctx, const GemmDesc& g, const X3Planes& x3, cudaStream_t stream);
 int launch_splitk_reduce(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream);
+// GEMMs with n <= kSkinnyMax or k <= kSkinnyMax (the classes dimension of an
+// output layer) on CUDA cores: one pass over the large operand.
+constexpr int kSkinnyMax = 16;
+bool gemm_skinny_wanted(const GemmDesc& g);
+int launch_gemm_skinny(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream);
 
 int launch_xent(rt_ctx* ctx, const float* logits, int64_t ldz, const uint32_t* labels, int64_t n,
                 int64_t classes, float scale, void* delta, rt_dtype delta_dtype, int64_t ldd,

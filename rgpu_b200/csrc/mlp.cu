@@ -21,7 +21,9 @@
 //     optimiser update runs on a side stream once the dX GEMM, the last reader
 //     of W_l, is done (and, under data parallelism, the allreduce), so the
 //     update's HBM traffic overlaps the remaining backward GEMMs; the comm
-//     stream carries nothing but the allreduces.
+//     stream carries nothing but the allreduces.  The first layer's dW GEMM,
+//     the last GEMM of the step, runs in row chunks so that its allreduce and
+//     update trail it by one chunk only.
 //   - two input slots: a host step copies the next batch on a copy stream
 //     while the previous step computes.
 #include <cstdlib>
@@ -43,6 +45,12 @@ int64_t round8(int64_t x) { return (x + 7) / 8 * 8; }
 // Row strides of GEMM operands are kept at multiples of 64 elements so every
 // 128-byte TMA row segment starts on a 128-byte line.
 int64_t round64(int64_t x) { return (x + 63) / 64 * 64; }
+// Start row of chunk c of `rows` rows cut into the plan's first-layer chunks
+// (boundaries on 256-row tile edges; the last chunk takes the remainder).
+int64_t chunk_row_of(int64_t rows, int chunks, int c) {
+    if (c >= chunks) return rows;
+    return rows * c / chunks / 256 * 256;
+}
 
 struct PlanLayer {
     int64_t d = 0, u = 0;
@@ -110,6 +118,9 @@ struct rt_mlp {
     // per-layer optimiser on a side stream, overlapping the remaining backward GEMMs
     cudaStream_t opt_stream = nullptr;
     std::vector<cudaEvent_t> grad_ready, opt_done;
+    // the first layer's dW GEMM in row chunks (1 = whole), with their events
+    int chunks0 = 1;
+    std::vector<cudaEvent_t> chunk_ready, chunk_comm_done, chunk_opt_done;
 };
 
 namespace {
@@ -152,6 +163,9 @@ void free_all(rt_mlp* m) {
     for (auto e : m->comm_done) cudaEventDestroy(e);
     for (auto e : m->grad_ready) cudaEventDestroy(e);
     for (auto e : m->opt_done) cudaEventDestroy(e);
+    for (auto e : m->chunk_ready) cudaEventDestroy(e);
+    for (auto e : m->chunk_comm_done) cudaEventDestroy(e);
+    for (auto e : m->chunk_opt_done) cudaEventDestroy(e);
     if (m->comm_stream) cudaStreamDestroy(m->comm_stream);
     if (m->opt_stream) cudaStreamDestroy(m->opt_stream);
     if (m->copy_stream) cudaStreamDestroy(m->copy_stream);
@@ -159,9 +173,12 @@ void free_all(rt_mlp* m) {
     m->allocs.clear();
 }
 
-// Enqueues the optimiser update of layer P's [d+1, ld] parameter block on st.
-int enqueue_layer_update(rt_mlp* m, PlanLayer& P, cudaStream_t st) {
-    OptTensor t{P.w32, P.g, P.m, P.v, P.w16, P.ld, P.ld, (P.d + 1) * P.ld};
+// Enqueues the optimiser update of rows [r0, r1) of layer P's [d+1, ld]
+// parameter block on st.
+int enqueue_update_rows(rt_mlp* m, PlanLayer& P, int64_t r0, int64_t r1, cudaStream_t st) {
+    const int64_t o = r0 * P.ld;
+    OptTensor t{P.w32 + o, P.g + o, P.m ? P.m + o : nullptr, P.v ? P.v + o : nullptr, P.w16 ? P.w16 + o : nullptr,
+                P.ld, P.ld, (r1 - r0) * P.ld};
     if (m->cfg.optimizer == RT_OPT_ADAM)
         return launch_adam(m->ctx, &t, 1, m->opt, m->cfg.lr, m->cfg.beta1, m->cfg.beta2, m->cfg.eps, st);
     if (m->cfg.optimizer == RT_OPT_SGD) return launch_sgd(m->ctx, &t, 1, m->cfg.lr, st);
@@ -192,6 +209,7 @@ struct Enqueuer {
     }
 
     const void* input_of(int l) const { return l == 0 ? m->slot[s].x : m->L[l - 1].act; }
+    int64_t chunk_row(int64_t rows, int c) const { return chunk_row_of(rows, m->chunks0, c); }
     int64_t ld_in(int l) const { return l == 0 ? m->ldx : m->L[l - 1].ld_act; }
     int backward_sms() const {
         return m->comm && m->comm_sm_reserve > 0 ? m->ctx->sm_count - m->comm_sm_reserve : 0;
@@ -229,6 +247,55 @@ struct Enqueuer {
         return RT_OK;
     }
 
+    // The first layer has no dX GEMM, so nothing reads W_0 after its dW GEMM,
+    // and that GEMM is the last of the step: its update (and, under data
+    // parallelism, its allreduce) would trail every GEMM.  The GEMM is cut
+    // into row chunks of [dW_0; db_0] instead (contiguous rows of the
+    // parameter block); each chunk's allreduce and update start on the side
+    // streams while the next chunk computes, so only the last chunk's trail.
+    int first_layer_chunked(PlanLayer& P) {
+        const bool update = m->cfg.optimizer != RT_OPT_NONE;
+        const int64_t rows = P.d + 1;
+        for (int c = 0; c < m->chunks0; ++c) {
+            const int64_t r0 = chunk_row(rows, c), r1 = chunk_row(rows, c + 1);
+            GemmDesc g{};
+            g.layout = RT_TN;
+            g.in_dtype = m->adt;
+            g.out_dtype = RT_F32;
+            g.m = r1 - r0;
+            g.n = P.u;
+            g.k = m->n;
+            g.a = static_cast<const uint8_t*>(input_of(0)) + r0 * dtype_size(m->adt);  // A columns r0..r1
+            g.lda = ld_in(0);
+            g.b = P.delta;
+            g.ldb = P.ld;
+            g.c = P.g + r0 * P.ld;
+            g.ldc = P.ld;
+            g.epi = RT_EPI_NONE;
+            g.split_k = P.split_dw;
+            g.workspace = P.ws;
+            g.max_sms = backward_sms();
+            g.x3_ws = m->x3_ws;
+            g.x3_ws_bytes = m->x3_ws_bytes;
+            RT_TRY(run_gemm(m->ctx, g, st, P.ws_bytes));
+            // FLOPs of the weight rows (the bias row is not counted, as everywhere)
+            RT_TRY(mark("dw_gemm", 2.0 * m->n * (double)(r1 - r0 - (r1 == rows ? 1 : 0)) * P.u));
+            RT_CUDA(cudaEventRecord(m->chunk_ready[c], st));
+            if (m->comm) {
+                RT_CUDA(cudaStreamWaitEvent(m->comm_stream, m->chunk_ready[c], 0));
+                RT_TRY(comm_allreduce(m->comm, P.g + r0 * P.ld, (r1 - r0) * P.ld, m->comm_stream));
+                RT_CUDA(cudaEventRecord(m->chunk_comm_done[c], m->comm_stream));
+            }
+            if (update) {
+                RT_CUDA(cudaStreamWaitEvent(m->opt_stream, m->chunk_ready[c], 0));
+                if (m->comm) RT_CUDA(cudaStreamWaitEvent(m->opt_stream, m->chunk_comm_done[c], 0));
+                RT_TRY(enqueue_update_rows(m, P, r0, r1, m->opt_stream));
+                RT_CUDA(cudaEventRecord(m->chunk_opt_done[c], m->opt_stream));
+            }
+        }
+        return RT_OK;
+    }
+
     int backward_and_update() {
         const int nl = (int)m->L.size();
         const bool update = m->cfg.optimizer != RT_OPT_NONE;
@@ -243,6 +310,10 @@ struct Enqueuer {
         RT_TRY(mark("softmax_xent", 0));
         for (int l = nl - 1; l >= 0; --l) {
             PlanLayer& P = m->L[l];
+            if (l == 0 && m->chunks0 > 1) {
+                RT_TRY(first_layer_chunked(P));
+                continue;
+            }
             // [dW_l; db_l] = [A_{l-1}, 1]^T delta_l  (TN, K = batch, M = d + 1), f32 gradient.
             // It runs before the dX GEMM so that the layer's allreduce starts as early as possible.
             GemmDesc g{};
@@ -306,15 +377,23 @@ struct Enqueuer {
                 RT_CUDA(cudaEventRecord(m->grad_ready[l], st));
                 RT_CUDA(cudaStreamWaitEvent(m->opt_stream, m->grad_ready[l], 0));
                 if (m->comm) RT_CUDA(cudaStreamWaitEvent(m->opt_stream, m->comm_done[l], 0));
-                RT_TRY(enqueue_layer_update(m, P, m->opt_stream));
+                RT_TRY(enqueue_update_rows(m, P, 0, P.d + 1, m->opt_stream));
                 RT_CUDA(cudaEventRecord(m->opt_done[l], m->opt_stream));
             }
         }
         for (int l = 0; l < nl; ++l) {
-            if (update)
+            if (l == 0 && m->chunks0 > 1) {
+                for (int c = 0; c < m->chunks0; ++c) {
+                    if (update)
+                        RT_CUDA(cudaStreamWaitEvent(st, m->chunk_opt_done[c], 0));
+                    else if (m->comm)
+                        RT_CUDA(cudaStreamWaitEvent(st, m->chunk_comm_done[c], 0));
+                }
+            } else if (update) {
                 RT_CUDA(cudaStreamWaitEvent(st, m->opt_done[l], 0));
-            else if (m->comm)
+            } else if (m->comm) {
                 RT_CUDA(cudaStreamWaitEvent(st, m->comm_done[l], 0));
+            }
         }
         if (update) RT_TRY(mark(m->cfg.optimizer == RT_OPT_ADAM ? "adam_tail" : "sgd_tail", 0));
         return RT_OK;
@@ -461,6 +540,25 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
         if (cudaEventCreateWithFlags(&m->grad_ready[l], cudaEventDisableTiming) != cudaSuccess ||
             cudaEventCreateWithFlags(&m->opt_done[l], cudaEventDisableTiming) != cudaSuccess)
             return bail(fail(RT_ERR_CUDA, "event creation failed"));
+    {
+        // first-layer dW chunks: 4 for >= 4096 rows, 2 for >= 2048 (see first_layer_chunked)
+        const int64_t rows0 = m->dims[0] + 1;
+        const char* env = getenv("RTGPU_FIRST_LAYER_CHUNKS");
+        int ch = rows0 >= 4096 ? 4 : rows0 >= 2048 ? 2 : 1;
+        if (env && env[0]) ch = atoi(env);
+        if (ch < 1) ch = 1;
+        if (ch > 8) ch = 8;
+        while (ch > 1 && chunk_row_of(rows0, ch, 1) == 0) --ch;  // every chunk non-empty
+        m->chunks0 = ch;
+        m->chunk_ready.resize(ch);
+        m->chunk_comm_done.resize(ch);
+        m->chunk_opt_done.resize(ch);
+        for (int c = 0; c < ch; ++c)
+            if (cudaEventCreateWithFlags(&m->chunk_ready[c], cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&m->chunk_comm_done[c], cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&m->chunk_opt_done[c], cudaEventDisableTiming) != cudaSuccess)
+                return bail(fail(RT_ERR_CUDA, "event creation failed"));
+    }
     if ((s = dalloc_t(m, &m->loss_rows, (size_t)m->n))) return bail(s);
     if ((s = dalloc_t(m, &m->opt, 1))) return bail(s);
     m->L.resize(nl);

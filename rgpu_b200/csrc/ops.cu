@@ -81,6 +81,7 @@ int run_gemm(rt_ctx* ctx, GemmDesc g, cudaStream_t stream, size_t ws_bytes) {
         RT_CHECK((size_t)g.split_k * g.m * g.n * 4 <= ws_bytes, "split-K workspace too small: %zu < %zu bytes",
                  ws_bytes, (size_t)g.split_k * g.m * g.n * 4);
     }
+    if (ctx->fast_gemm && gemm_skinny_wanted(g)) return launch_gemm_skinny(ctx, g, stream);
     if (ctx->fast_gemm && gemm_tc_supported(ctx, g)) return launch_gemm_tc(ctx, g, stream);
     if (ctx->fast_gemm && !g.no_alloc && gemm_x3_supported(ctx, g)) {
         const size_t need = gemm_x3_workspace_bytes(g);

@@ -215,6 +215,63 @@ def test_relu_mask_epilogue_via_rt_gemm(gpu):
     assert erro_rel(want, gpu.download(c)) < 1e-5
 
 
+SKINNY = [(2048, 10, 1024), (1025, 10, 2048), (2048, 1024, 10), (37, 16, 300), (300, 200, 16), (5, 3, 7),
+          (129, 1, 4096), (64, 2000, 1)]
+
+
+def _skinny_ref(a, b, epi, bias, mask):
+    want = a.astype(np.float64) @ b.astype(np.float64)
+    if epi in (G.RT_EPI_BIAS, G.RT_EPI_BIAS_RELU):
+        want = want + bias
+    if epi == G.RT_EPI_BIAS_RELU:
+        want = np.maximum(want, 0)
+    if epi == G.RT_EPI_RELU_MASK:
+        want = want * (mask > 0)
+    return want
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("m,n,k", SKINNY)
+def test_skinny_gemms_every_layout_and_epilogue(gpu, m, n, k, dtype):
+    # n <= 16 or k <= 16 (an output layer's classes) runs on the skinny CUDA-core
+    # kernels: narrow N over A K-major (NN, NT), narrow N over A MN-major (TN,
+    # with and without k slices), narrow K.  Every layout and epilogue against
+    # the exact (f64) result, bf16 on the bf16-rounded operands; the kernels
+    # sum k in lane-strided order, so the bound is the SIMT f32 one used for
+    # the 3xTF32 test above.
+    a, b = _ab(m, n, k)
+    if dtype == "bf16":
+        a = rgpu_b200.bf16_to_f32(rgpu_b200.f32_to_bf16(a))
+        b = rgpu_b200.bf16_to_f32(rgpu_b200.f32_to_bf16(b))
+    bias = np.linspace(-1, 1, n, dtype=np.float32).reshape(1, n)
+    mask = np.sin(np.arange(m * n, dtype=np.float32) * 0.5).reshape(m, n).astype(np.float32)
+    ops = {G.RT_NN: (a, b), G.RT_NT: (a, np.ascontiguousarray(b.T)), G.RT_TN: (np.ascontiguousarray(a.T), b)}
+    gbias, gmask = gpu.upload(bias), gpu.upload(mask)
+    for layout, (x, y) in ops.items():
+        gx, gy = gpu.upload(x, dtype), gpu.upload(y, dtype)
+        for epi in (G.RT_EPI_NONE, G.RT_EPI_BIAS, G.RT_EPI_BIAS_RELU, G.RT_EPI_RELU_MASK):
+            for split in ((1, 4) if layout == G.RT_TN else (1,)):
+                c = gpu.zeros((m, n))
+                ws = gpu.zeros((split * m, n)) if split > 1 else None
+                args = G.GemmArgs(layout, G.RT_BF16 if dtype == "bf16" else G.RT_F32, G.RT_F32, m, n, k,
+                                  gx.ptr, gx.ld, gy.ptr, gy.ld, c.ptr, c.ld, epi, gbias.ptr, gmask.ptr, gmask.ld,
+                                  split, ws.ptr if ws is not None else None,
+                                  split * m * n * 4 if ws is not None else 0)
+                gpu.gemm(args)
+                e = rel_l2(gpu.download(c), _skinny_ref(a, b, epi, bias, mask))
+                assert e <= 1e-6 + 1.6e-9 * k, f"layout {layout} epi {epi} split {split} {m}x{n}x{k} {dtype}: {e:.2e}"
+
+
+def test_skinny_gemm_is_one_launch(gpu):
+    a, b = _ab(2048, 10, 1024)
+    ga, gb, c = gpu.upload(a), gpu.upload(b), gpu.zeros((2048, 10))
+    before = gpu.launch_count()
+    gpu.matmul(ga, gb, c)
+    gpu.sync()
+    assert gpu.launch_count() - before == 1
+    assert rel_l2(gpu.download(c), a.astype(np.float64) @ b.astype(np.float64)) < 3e-6
+
+
 @pytest.mark.parametrize("m,n,k", [(64, 64, 4096), (32, 96, 2048), (128, 64, 1024)])
 def test_split_k_matches_unsplit(gpu, m, n, k):
     # gpu.rs:383-430: 1/2/4/8/16 slices, NN and TN, error <= 3x the unsplit GEMM.
