@@ -39,7 +39,7 @@ using namespace tc;
 template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                   TcParams p) {
+                   const __grid_constant__ CUtensorMap tmap_c, TcParams p) {
     static_assert(!X3 || (sizeof(TIn) == 4 && !A_MN && !B_MN), "3xTF32 planes are f32 and K-major");
     using G = Geo<TIn, BN>;
     constexpr bool kTF32 = sizeof(TIn) == 4;
@@ -50,7 +50,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* smem_a = smem;
     uint8_t* smem_b = smem + STAGES * G::A_BYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * G::STAGE_BYTES);
+    uint8_t* smem_epi = smem + STAGES * G::STAGE_BYTES;  // [4 epilogue warps][32 x 32] output staging
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_epi + G::EPI_BYTES);
     // bars: full[STAGES], empty[STAGES], tmem_full[2], tmem_empty[2], drain
     uint64_t* full = bars;
     uint64_t* empty = bars + STAGES;
@@ -79,6 +80,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_barrier_init();
         prefetch_tmap(&tmap_a);
         prefetch_tmap(&tmap_b);
+        if (p.tma_store) prefetch_tmap(&tmap_c);
     }
     if (warp == 2) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -223,7 +225,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             tc_fence_after();
-            const int64_t row = (int64_t)mb * BM + ew * 32 + lane;
+            const int64_t row0 = (int64_t)mb * BM + ew * 32;
+            const int64_t row = row0 + lane;
             const uint32_t tbase = tmem_base + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
@@ -231,7 +234,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (col0 >= p.n) break;  // uniform across the warp
                 float v[32];
                 tmem_ld_32x32(tbase + (uint32_t)c, v);
-                if (row < p.m) {
+                if (p.tma_store == 2) {
+                    // staged split-K partials: slice `split` of the [splits][m][n] workspace
+                    stage_and_store<float>(&tmap_c, smem_epi + ew * kStageBytes, lane, row0, col0, v, split);
+                } else if (p.tma_store == 1) {
+                    // staged: coalesced TMA stores of the warp's 32 x 32 chunk
+                    uint8_t* box = smem_epi + ew * kStageBytes;
+                    if (p.out_bf16) {
+                        if (row < p.m) epilogue_math<__nv_bfloat16>(p, row, col0, v);
+                        stage_and_store<__nv_bfloat16>(&tmap_c, box, lane, row0, col0, v);
+                    } else {
+                        if (row < p.m) epilogue_math<float>(p, row, col0, v);
+                        stage_and_store<float>(&tmap_c, box, lane, row0, col0, v);
+                    }
+                } else if (row < p.m) {
                     if (p.ws) {
                         float* dst = p.ws + (int64_t)split * p.m * p.n + row * p.n + col0;
 #pragma unroll
@@ -263,6 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             record_error(p.err, DEV_TIMEOUT_EPILOGUE, blockIdx.x);
             *abort_flag = 1;
         }
+        if (p.tma_store && lane == 0) bulk_wait_all();  // this warp's output stores are complete
     }
 
     __syncwarp();  // reconverge the role warps before the block-wide barrier
@@ -288,7 +305,7 @@ template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3>
 int launch_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X3Planes* x3) {
     using G = Geo<TIn, BN>;
     const bool bf16 = sizeof(TIn) == 2;
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, tc;
     if constexpr (X3) {
         // hi/lo planes of the operands, both K-major: A [2][m][k], B [2][n][k]
         RT_TRY(make_tmap_planes(&ta, x3->a, g.k, g.m, x3->lda, x3->a_plane, 2, G::BK, BM));
@@ -336,11 +353,20 @@ int launch_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X3Plan
     p.out_bf16 = g.out_dtype == RT_BF16;
     p.err = ctx->dev_err;
     p.opt = g.opt;
+    p.tma_store = 0;
+    tc = ta;  // unused unless a staged store is chosen
+    if (ctx->tma_store && splits == 1 && !g.opt.kind) {
+        p.tma_store = 1;
+        RT_TRY(make_tmap_out(&tc, g.c, p.out_bf16 != 0, g.m, g.n, g.ldc));
+    } else if (ctx->tma_store && splits > 1 && g.n % 4 == 0 && (reinterpret_cast<uintptr_t>(g.workspace) & 15) == 0) {
+        p.tma_store = 2;
+        RT_TRY(make_tmap_ws(&tc, g.workspace, g.m, g.n, splits));
+    }
 
     int64_t tiles = (int64_t)p.tiles_m * p.tiles_n * p.splits;
     int sms = g.max_sms > 0 && g.max_sms < ctx->sm_count ? g.max_sms : ctx->sm_count;
     int grid = (int)(tiles < sms ? tiles : sms);
-    gemm_tc_kernel<TIn, A_MN, B_MN, BN, X3><<<grid, kThreads, G::SMEM, st>>>(ta, tb, p);
+    gemm_tc_kernel<TIn, A_MN, B_MN, BN, X3><<<grid, kThreads, G::SMEM, st>>>(ta, tb, tc, p);
     count_launch(ctx);
     RT_CUDA(cudaGetLastError());
     if (splits > 1) return launch_splitk_reduce(ctx, gr, st);

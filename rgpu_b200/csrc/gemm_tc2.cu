@@ -117,13 +117,14 @@ struct Geo2 {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+    static constexpr int EPI_BYTES = kEpiWarps * kStageBytes;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
 };
 
 template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false>
 __global__ void __launch_bounds__(kThreads2, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                    TcParams p) {
+                    const __grid_constant__ CUtensorMap tmap_c, TcParams p) {
     static_assert(!X3 || (sizeof(TIn) == 4 && !A_MN && !B_MN), "3xTF32 planes are f32 and K-major");
     using G = Geo2<TIn, BN>;
     constexpr bool kTF32 = sizeof(TIn) == 4;
@@ -134,7 +135,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* smem_a = smem;
     uint8_t* smem_b = smem + STAGES * G::A_BYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * G::STAGE_BYTES);
+    uint8_t* smem_epi = smem + STAGES * G::STAGE_BYTES;  // [8 epilogue warps][32 x 32] output staging
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_epi + G::EPI_BYTES);
     uint64_t* full = bars;                     // leader: both CTAs' bytes of a stage
     uint64_t* empty = bars + STAGES;           // each CTA: stage released by the MMAs
     uint64_t* tfull = bars + 2 * STAGES;       // each CTA: accumulator ready
@@ -166,6 +168,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
         fence_barrier_init();
         prefetch_tmap(&tmap_a);
         prefetch_tmap(&tmap_b);
+        if (p.tma_store) prefetch_tmap(&tmap_c);
     }
     if (warp == 2) {
         asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -315,7 +318,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
                 break;
             }
             tc_fence_after();
-            const int64_t row = (int64_t)mb * BM2 + (int64_t)rank * 128 + ew * 32 + lane;
+            const int64_t row0 = (int64_t)mb * BM2 + (int64_t)rank * 128 + ew * 32;
+            const int64_t row = row0 + lane;
             const uint32_t tbase = tmem_base + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
             for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
@@ -323,7 +327,20 @@ __global__ void __launch_bounds__(kThreads2, 1)
                 if (col0 >= p.n) break;
                 float v[32];
                 tmem_ld_32x32(tbase + (uint32_t)c, v);
-                if (row < p.m) {
+                if (p.tma_store == 2) {
+                    // staged split-K partials: slice `split` of the [splits][m][n] workspace
+                    stage_and_store<float>(&tmap_c, smem_epi + (warp - 4) * kStageBytes, lane, row0, col0, v, split);
+                } else if (p.tma_store == 1) {
+                    // staged: coalesced TMA stores of the warp's 32 x 32 chunk
+                    uint8_t* box = smem_epi + (warp - 4) * kStageBytes;
+                    if (p.out_bf16) {
+                        if (row < p.m) epilogue_math<__nv_bfloat16>(p, row, col0, v);
+                        stage_and_store<__nv_bfloat16>(&tmap_c, box, lane, row0, col0, v);
+                    } else {
+                        if (row < p.m) epilogue_math<float>(p, row, col0, v);
+                        stage_and_store<float>(&tmap_c, box, lane, row0, col0, v);
+                    }
+                } else if (row < p.m) {
                     if (p.ws) {
                         float* dst = p.ws + (int64_t)split * p.m * p.n + row * p.n + col0;
 #pragma unroll
@@ -354,6 +371,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
             record_error(p.err, DEV_TIMEOUT_EPILOGUE, blockIdx.x);
             raise_abort();
         }
+        if (p.tma_store && lane == 0) bulk_wait_all();  // this warp's output stores are complete
     }
 
     __syncwarp();
@@ -381,7 +399,7 @@ template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false>
 int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X3Planes* x3 = nullptr) {
     using G = Geo2<TIn, BN>;
     const bool bf16 = sizeof(TIn) == 2;
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, tc;
     if constexpr (X3) {
         RT_TRY(make_tmap_planes(&ta, x3->a, g.k, g.m, x3->lda, x3->a_plane, 2, G::BK, 128));
         RT_TRY(make_tmap_planes(&tb, x3->b, g.k, g.n, x3->ldb, x3->b_plane, 2, G::BK, G::BNH));
@@ -426,6 +444,15 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X
     p.out_bf16 = g.out_dtype == RT_BF16;
     p.err = ctx->dev_err;
     p.opt = g.opt;
+    p.tma_store = 0;
+    tc = ta;  // unused unless a staged store is chosen
+    if (ctx->tma_store && splits == 1 && !g.opt.kind) {
+        p.tma_store = 1;
+        RT_TRY(make_tmap_out(&tc, g.c, p.out_bf16 != 0, g.m, g.n, g.ldc));
+    } else if (ctx->tma_store && splits > 1 && g.n % 4 == 0 && (reinterpret_cast<uintptr_t>(g.workspace) & 15) == 0) {
+        p.tma_store = 2;
+        RT_TRY(make_tmap_ws(&tc, g.workspace, g.m, g.n, splits));
+    }
 
     int64_t tiles = (int64_t)p.tiles_m * p.tiles_n * p.splits;
     int sms = g.max_sms > 0 && g.max_sms < ctx->sm_count ? g.max_sms : ctx->sm_count;
@@ -443,7 +470,7 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    RT_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3>, ta, tb, p));
+    RT_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3>, ta, tb, tc, p));
     count_launch(ctx);
     if (splits > 1) return launch_splitk_reduce(ctx, gr, st);
     return RT_OK;

@@ -54,6 +54,7 @@ struct rt_ctx {
     bool fast_gemm = true;
     bool pair_gemm = true;  // two-CTA tcgen05 tiles where the problem is large enough
     bool f32_tensor = true;  // f32 GEMMs on the tensor cores (3xTF32) when fast_gemm is on
+    bool tma_store = true;   // tensor-core GEMM epilogues store C through shared memory and TMA
     // Grow-only workspace for the hi/lo operand copies of 3xTF32 GEMMs that
     // bring none of their own.  A replaced buffer is kept until the context
     // is destroyed: graphs captured earlier may still reference it.
@@ -126,6 +127,8 @@ int launch_gemm_tc_x3(rt_ctx* ctx, const GemmDesc& g, const X3Planes& x3, cudaSt
 bool gemm_tc2_x3_wanted(const rt_ctx* ctx, const GemmDesc& g);
 int launch_gemm_tc2_x3(rt_ctx* ctx, const GemmDesc& g, const X3Planes& x3, cudaStream_t stream);
 int launch_splitk_reduce(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream);
+// Split-K slice count for a tensor-core GEMM (1 = no split).
+int choose_split_k(const rt_ctx* ctx, int64_t m, int64_t n, int64_t k, rt_dtype in_dtype);
 // GEMMs with n <= kSkinnyMax or k <= kSkinnyMax (the classes dimension of an
 // output layer) on CUDA cores: one pass over the large operand.
 constexpr int kSkinnyMax = 16;

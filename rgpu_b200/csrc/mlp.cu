@@ -590,16 +590,13 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
             cudaMemcpyAsync(P.b, biases[l], (size_t)P.u * 4, cudaMemcpyHostToDevice, ctx->stream) != cudaSuccess)
             return bail(fail(RT_ERR_CUDA, "bias upload failed"));
         if ((s = refresh_shadow(m, P, ctx->stream))) return bail(s);
-        // split-K for the dW GEMM when its 128x256 output tiles cannot fill the GPU.
-        int64_t tiles = ((P.d + 1 + 127) / 128) * ((P.u + 255) / 256);
-        int split = 1;
-        if (tiles * 4 < (int64_t)ctx->sm_count * 3) {
-            int64_t sp = (int64_t)ctx->sm_count / tiles;
-            // k blocks of the tensor-core loop (f32: three 32-deep 3xTF32 segments)
-            int64_t kb = m->adt == RT_F32 ? 3 * ((m->n + 31) / 32) : (m->n + 63) / 64;
-            if (sp > kb / 4) sp = kb / 4;
-            if (sp > 16) sp = 16;
-            split = sp < 1 ? 1 : (int)sp;
+        // split-K for the dW GEMM when its output tiles cannot fill the GPU
+        // (the library's rule; the output layer's narrow-N dW slices the same way)
+        int split = choose_split_k(ctx, P.d + 1, P.u, m->n, m->adt);
+        if (P.u <= kSkinnyMax) {
+            // the skinny dW kernel slices k in 64-row steps: up to 16 slices, >= 128 rows each
+            int64_t sp = m->n / 128;
+            split = (int)(sp < 1 ? 1 : sp > 16 ? 16 : sp);
         }
         P.split_dw = split;
         if (split > 1) {

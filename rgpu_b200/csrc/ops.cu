@@ -32,18 +32,26 @@ static int check_gemm(const GemmDesc& g) {
 
 // Slices for the tensor-core kernel: split only when the output tiles cannot
 // fill the GPU and the reduction is deep (the dW = X^T dY case at large
-// batch, gpu/mod.rs:1351-1358).
-static int choose_split(const rt_ctx* ctx, const GemmDesc& g) {
-    int64_t tiles = ((g.m + 127) / 128) * ((g.n + 255) / 256);
+// batch, gpu/mod.rs:1351-1358).  Each slice keeps at least 8 k blocks (512
+// deep for bf16) and nothing splits below 24 k blocks: a shallower split
+// saves less MMA time than the partial-sum round trip and the reduction
+// launch cost.
+int choose_split_k(const rt_ctx* ctx, int64_t m, int64_t n, int64_t k, rt_dtype in_dtype) {
+    int64_t tiles = ((m + 127) / 128) * ((n + 255) / 256);
     if (tiles <= 0) return 1;
     if (tiles * 4 >= (int64_t)ctx->sm_count * 3) return 1;
     // k blocks of the tensor-core loop: 64 deep for bf16, three 32-deep
     // segments for the 3xTF32 f32 path
-    int64_t kblocks = g.in_dtype == RT_F32 ? 3 * ((g.k + 31) / 32) : (g.k + 63) / 64;
+    int64_t kblocks = in_dtype == RT_F32 ? 3 * ((k + 31) / 32) : (k + 63) / 64;
+    if (kblocks < 24) return 1;
     int64_t s = (int64_t)ctx->sm_count / tiles;
-    if (s > kblocks / 4) s = kblocks / 4;
+    if (s > kblocks / 8) s = kblocks / 8;
     if (s > 16) s = 16;
     return s < 1 ? 1 : (int)s;
+}
+
+static int choose_split(const rt_ctx* ctx, const GemmDesc& g) {
+    return choose_split_k(ctx, g.m, g.n, g.k, g.in_dtype);
 }
 
 // The context's 3xTF32 operand workspace, grown to `need` bytes unless

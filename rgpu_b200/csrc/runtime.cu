@@ -85,6 +85,8 @@ int rt_ctx_create(int device, rt_ctx** out) {
     c->pair_gemm = !(pair_env && pair_env[0] == '0');
     const char* f32_env = getenv("RTGPU_F32_TENSOR");
     c->f32_tensor = !(f32_env && f32_env[0] == '0');
+    const char* st_env = getenv("RTGPU_TMA_STORE");
+    c->tma_store = !(st_env && st_env[0] == '0');
     int st = gemm_tc_init(c);
     if (st == RT_OK) st = gemm_tc2_init(c);
     if (st == RT_OK) st = gemm_x3_init(c);

@@ -91,6 +91,28 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// TMA store of a shared-memory box to global memory (bulk-group completion);
+// the box is clipped at the tensor's bounds.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(src), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int32_t x, int32_t y, int32_t z) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(src), "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until the shared-memory sources of this thread's bulk stores are read.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Wait until this thread's bulk stores are complete.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Make this thread's generic-proxy shared-memory writes visible to the async proxy (TMA).
+__device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -178,7 +200,12 @@ struct TcParams {
     int* err;
     OptFuse opt;
     int kb_seg;  // 3xTF32: k blocks per product segment (the k loop runs 3 * kb_seg blocks); 0 otherwise
+    int tma_store;  // through shared-memory staging and TMA stores: 1 = C, 2 = the split-K partials (0 = direct)
 };
+
+// Epilogue staging: one 32 x 32 output chunk per epilogue warp (4 KB), the
+// layout of a 128-byte (f32) or 64-byte (bf16) swizzled TMA box.
+constexpr int kStageBytes = 32 * 32 * 4;
 
 // Stage geometry shared by host and device.
 template <typename TIn, int BN>
@@ -192,7 +219,8 @@ struct Geo {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
     static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int EPI_BYTES = 4 * kStageBytes;  // 4 epilogue warps
+    static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 __device__ __forceinline__ void tile_coords(const TcParams& p, int t, int& split, int& mb, int& nb) {
@@ -223,9 +251,9 @@ __device__ __forceinline__ float load_mask_elem<__nv_bfloat16>(const void* mask,
     return __bfloat162float(static_cast<const __nv_bfloat16*>(mask)[idx]);
 }
 
-// Epilogue for 32 consecutive columns of one row.
+// Epilogue arithmetic for 32 consecutive columns of one row (row < m).
 template <typename TOut>
-__device__ __forceinline__ void epilogue_chunk(const TcParams& p, int64_t row, int64_t col0, float (&v)[32]) {
+__device__ __forceinline__ void epilogue_math(const TcParams& p, int64_t row, int64_t col0, float (&v)[32]) {
     const int64_t n = p.n;
     const bool full = col0 + 32 <= n;
     if (p.epi == RT_EPI_BIAS || p.epi == RT_EPI_BIAS_RELU) {
@@ -262,6 +290,13 @@ __device__ __forceinline__ void epilogue_chunk(const TcParams& p, int64_t row, i
                 if (col0 + j < n) v[j] = v[j] * (load_mask_elem<TOut>(p.mask, base + j) > 0.0f ? 1.0f : 0.0f);
         }
     }
+}
+
+// Direct stores of one row's 32 columns (the thread's own row).
+template <typename TOut>
+__device__ __forceinline__ void store_chunk(const TcParams& p, int64_t row, int64_t col0, const float (&v)[32]) {
+    const int64_t n = p.n;
+    const bool full = col0 + 32 <= n;
     if constexpr (sizeof(TOut) == 2) {
         __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.c) + row * p.ldc + col0;
         if (full) {
@@ -297,6 +332,64 @@ __device__ __forceinline__ void epilogue_chunk(const TcParams& p, int64_t row, i
     }
 }
 
+template <typename TOut>
+__device__ __forceinline__ void epilogue_chunk(const TcParams& p, int64_t row, int64_t col0, float (&v)[32]) {
+    epilogue_math<TOut>(p, row, col0, v);
+    store_chunk<TOut>(p, row, col0, v);
+}
+
+// Writes lane `lane`'s row of a 32 x 32 chunk into the warp's staging box,
+// swizzled as the C tensor map expects: f32 rows are 128 bytes (16-byte
+// unit q of row r at q ^ (r & 7)), bf16 rows 64 bytes (unit q at
+// q ^ ((r >> 1) & 3)).  Each 8-lane phase of a 16-byte store then covers all
+// 32 banks once.
+template <typename TOut>
+__device__ __forceinline__ void stage_row(uint8_t* box, int lane, const float (&v)[32]) {
+    if constexpr (sizeof(TOut) == 2) {
+        uint8_t* row = box + lane * 64;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            uint4 u;
+            __nv_bfloat162 h0 = __floats2bfloat162_rn(v[q * 8 + 0], v[q * 8 + 1]);
+            __nv_bfloat162 h1 = __floats2bfloat162_rn(v[q * 8 + 2], v[q * 8 + 3]);
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(v[q * 8 + 4], v[q * 8 + 5]);
+            __nv_bfloat162 h3 = __floats2bfloat162_rn(v[q * 8 + 6], v[q * 8 + 7]);
+            u.x = *reinterpret_cast<uint32_t*>(&h0);
+            u.y = *reinterpret_cast<uint32_t*>(&h1);
+            u.z = *reinterpret_cast<uint32_t*>(&h2);
+            u.w = *reinterpret_cast<uint32_t*>(&h3);
+            *reinterpret_cast<uint4*>(row + ((q ^ ((lane >> 1) & 3)) << 4)) = u;
+        }
+    } else {
+        uint8_t* row = box + lane * 128;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(row + ((q ^ (lane & 7)) << 4)) =
+                make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+    }
+}
+
+// Staged store of a warp's 32 x 32 chunk at (row0, col0): wait until the
+// box's previous TMA store has read it, fill it, hand it to the async proxy
+// and issue the store from lane 0.  Rows >= m and columns >= n are clipped
+// by the TMA unit.
+template <typename TOut>
+__device__ __forceinline__ void stage_and_store(const CUtensorMap* tmap_c, uint8_t* box, int lane, int64_t row0,
+                                                int64_t col0, const float (&v)[32], int split = -1) {
+    if (lane == 0) bulk_wait_read_all();
+    __syncwarp();
+    stage_row<TOut>(box, lane, v);
+    fence_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+        if (split < 0)
+            tma_store_2d(tmap_c, smem_u32(box), (int32_t)col0, (int32_t)row0);
+        else
+            tma_store_3d(tmap_c, smem_u32(box), (int32_t)col0, (int32_t)row0, split);
+        bulk_commit();
+    }
+}
+
 // ------------------------------------------------------------------ host
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -318,7 +411,7 @@ inline EncodeTiledFn encode_fn() {
 // 2-D row-major tensor: `inner` contiguous elements per row, `outer` rows,
 // row stride `ld` elements; box (box_inner x box_outer), 128-byte swizzle.
 inline int make_tmap(CUtensorMap* map, const void* base, bool bf16, int64_t inner, int64_t outer, int64_t ld,
-              int box_inner, int box_outer) {
+              int box_inner, int box_outer, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return fail(RT_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled is not available from the driver");
     const int es = bf16 ? 2 : 4;
@@ -327,13 +420,18 @@ inline int make_tmap(CUtensorMap* map, const void* base, bool bf16, int64_t inne
     cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
-                     const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                     const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return fail(RT_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d): inner %lld outer %lld ld %lld box %dx%d",
                     (int)r, (long long)inner, (long long)outer, (long long)ld, box_inner, box_outer);
     return RT_OK;
+}
+
+// Output map for the staged epilogue: [m, n] row-major, row stride ldc, box
+// 32 x 32 (128-byte swizzle for f32 rows, 64-byte for bf16 rows).
+inline int make_tmap_out(CUtensorMap* map, void* c, bool bf16, int64_t m, int64_t n, int64_t ldc) {
+    return make_tmap(map, c, bf16, n, m, ldc, 32, 32, bf16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 // 3-D f32 tensor of `planes` [outer, inner] planes, row stride `ld`, plane
@@ -354,6 +452,12 @@ inline int make_tmap_planes(CUtensorMap* map, const float* base, int64_t inner, 
                     "cuTensorMapEncodeTiled (planes) failed (%d): inner %lld outer %lld ld %lld plane %lld box %dx%d",
                     (int)r, (long long)inner, (long long)outer, (long long)ld, (long long)plane, box_inner, box_outer);
     return RT_OK;
+}
+
+// Split-K partials [splits][m][n] f32 (row stride n) for the staged epilogue:
+// box 32 x 32 x 1, 128-byte swizzle.  n * 4 must be a multiple of 16.
+inline int make_tmap_ws(CUtensorMap* map, float* ws, int64_t m, int64_t n, int splits) {
+    return make_tmap_planes(map, ws, n, m, n, m * n, splits, 32, 32);
 }
 
 }  // namespace tc
