@@ -207,14 +207,59 @@ __global__ void splitk_reduce_kernel(SimtParams p, int slices) {
     int64_t total = p.m * p.n;
     for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
          idx += (int64_t)gridDim.x * blockDim.x) {
+        // slices summed in order; loads issued eight at a time ahead of the adds
         float s = 0.0f;
-        for (int z = 0; z < slices; ++z) s += p.ws[(int64_t)z * total + idx];
+        for (int z0 = 0; z0 < slices; z0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = z0 + u < slices ? __ldg(p.ws + (int64_t)(z0 + u) * total + idx) : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (z0 + u < slices) s += v[u];
+        }
         int64_t i = idx / p.n, j = idx % p.n;
         if (p.out_bf16)
             finish<__nv_bfloat16>(p, i, j, s);
         else
             finish<float>(p, i, j, s);
         if (p.opt.kind) opt_apply_row<1>(p.opt, i * p.ldc + j, &s, 1);
+    }
+}
+
+// The same reduction four columns at a time (n, ldc and, for the epilogue
+// inputs, ldmask multiples of 4; f32 output, no optimiser): blockIdx.y walks
+// rows, the x threads walk 4-column groups, every load and store 16 bytes.
+// Slices are summed in the same fixed order.
+__global__ void splitk_reduce4_kernel(SimtParams p, int slices) {
+    const int64_t total = p.m * p.n;
+    const int64_t groups = p.n / 4;
+    for (int64_t i = blockIdx.y; i < p.m; i += gridDim.y) {
+        for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < groups;
+             g += (int64_t)gridDim.x * blockDim.x) {
+            const int64_t j = 4 * g;
+            const float* src = p.ws + i * p.n + j;
+            float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            for (int z0 = 0; z0 < slices; z0 += 4) {
+                float4 v[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    v[u] = z0 + u < slices ? __ldg(reinterpret_cast<const float4*>(src + (int64_t)(z0 + u) * total))
+                                           : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (z0 + u < slices) s.x += v[u].x, s.y += v[u].y, s.z += v[u].z, s.w += v[u].w;
+            }
+            if (p.epi == RT_EPI_BIAS || p.epi == RT_EPI_BIAS_RELU) {
+                s.x += p.bias[j], s.y += p.bias[j + 1], s.z += p.bias[j + 2], s.w += p.bias[j + 3];
+                if (p.epi == RT_EPI_BIAS_RELU)
+                    s.x = fmaxf(s.x, 0.0f), s.y = fmaxf(s.y, 0.0f), s.z = fmaxf(s.z, 0.0f), s.w = fmaxf(s.w, 0.0f);
+            } else if (p.epi == RT_EPI_RELU_MASK) {
+                const float4 mk = *reinterpret_cast<const float4*>(static_cast<const float*>(p.mask) + i * p.ldmask + j);
+                s.x = s.x * (mk.x > 0.0f ? 1.0f : 0.0f), s.y = s.y * (mk.y > 0.0f ? 1.0f : 0.0f);
+                s.z = s.z * (mk.z > 0.0f ? 1.0f : 0.0f), s.w = s.w * (mk.w > 0.0f ? 1.0f : 0.0f);
+            }
+            *reinterpret_cast<float4*>(static_cast<float*>(p.c) + i * p.ldc + j) = s;
+        }
     }
 }
 
@@ -272,6 +317,19 @@ int launch_gemm_simt(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream) {
 
 int launch_splitk_reduce(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream) {
     SimtParams p = make_params(g);
+    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    const bool vec = g.out_dtype == RT_F32 && !g.opt.kind && g.n % 4 == 0 && g.ldc % 4 == 0 && al16(g.c) &&
+                     al16(g.workspace) && (g.epi != RT_EPI_RELU_MASK || (g.ldmask % 4 == 0 && al16(g.mask)));
+    if (vec) {
+        const int64_t groups = g.n / 4;
+        const int threads = groups >= 256 ? 256 : (int)((groups + 31) / 32 * 32);
+        const int64_t gx = (groups + threads - 1) / threads;
+        int64_t gy = g.m < 65535 ? g.m : 65535;
+        splitk_reduce4_kernel<<<dim3((unsigned)gx, (unsigned)gy), threads, 0, stream>>>(p, g.split_k);
+        count_launch(ctx);
+        RT_CUDA(cudaGetLastError());
+        return RT_OK;
+    }
     int64_t total = g.m * g.n;
     int64_t blocks = (total + 255) / 256;
     int64_t cap = (int64_t)ctx->sm_count * 16;

@@ -17,6 +17,7 @@ namespace rt {
 namespace {
 
 constexpr int kThreads = 256;
+constexpr int kSkinnyNSmem = 1024 * 20 * 4;  // skinny_n_kernel's staged B chunk
 
 template <typename T>
 __device__ __forceinline__ float ld_f(const T* p, int64_t i);
@@ -61,81 +62,172 @@ __device__ __forceinline__ void finish_one(const SkinnyParams& p, int64_t i, int
         static_cast<float*>(p.c)[i * p.ldc + j] = v;
 }
 
-// Narrow N, A K-major (layouts NN and NT): a block owns ROWS rows of C and
-// its 8 warps split k (warp w takes k indices w*32 + lane + 256 i, four at a
-// time so that 4 x ROWS loads of A are in flight per lane); a shuffle tree
-// sums each warp's lanes and the warps' sums are added in fixed order.  The
-// small operand B is read through L1.
-template <typename TIn, int NMAX, bool B_KMAJOR, int ROWS>
-__global__ void __launch_bounds__(kThreads) skinny_n_kernel(SkinnyParams p) {
-    constexpr int U = 4;
-    constexpr int WARPS = kThreads / 32;
-    __shared__ float red[WARPS][ROWS][NMAX];
-    const TIn* A = static_cast<const TIn*>(p.a);
-    const TIn* B = static_cast<const TIn*>(p.b);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int64_t i0 = (int64_t)blockIdx.x * ROWS;
-    const int n = (int)p.n;
-    float acc[ROWS][NMAX];
+// Vector epilogue of 4 consecutive columns j0..j0+3 of row i (all < n): the
+// same arithmetic as finish_one, with 16-byte loads and stores where the
+// rows are aligned for them.
+__device__ __forceinline__ void finish_four(const SkinnyParams& p, int64_t i, int64_t j0, float (&v)[4], bool vec) {
+    if (!vec || p.opt.kind) {
 #pragma unroll
-    for (int r = 0; r < ROWS; ++r)
+        for (int c = 0; c < 4; ++c) finish_one(p, i, j0 + c, v[c]);
+        return;
+    }
+    if (p.epi == RT_EPI_BIAS || p.epi == RT_EPI_BIAS_RELU) {
+        const float4 b = *reinterpret_cast<const float4*>(p.bias + j0);
+        v[0] += b.x, v[1] += b.y, v[2] += b.z, v[3] += b.w;
+        if (p.epi == RT_EPI_BIAS_RELU)
 #pragma unroll
-        for (int j = 0; j < NMAX; ++j) acc[r][j] = 0.0f;
-    for (int64_t q0 = (int64_t)warp * 32 + lane; q0 < p.k; q0 += (int64_t)kThreads * U) {
-        float a[U][ROWS];
+            for (int c = 0; c < 4; ++c) v[c] = fmaxf(v[c], 0.0f);
+    } else if (p.epi == RT_EPI_RELU_MASK) {
+        const int64_t mi = i * p.ldmask + j0;
+        float mk[4];
+        if (p.out_bf16) {
+            const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.mask) + mi);
+            const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int64_t q = q0 + (int64_t)u * kThreads;
-#pragma unroll
-            for (int r = 0; r < ROWS; ++r) a[u][r] = (q < p.k && i0 + r < p.m) ? ld_f(A, (i0 + r) * p.lda + q) : 0.0f;
+            for (int c = 0; c < 4; ++c) mk[c] = __bfloat162float(h[c]);
+        } else {
+            const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(p.mask) + mi);
+            mk[0] = f.x, mk[1] = f.y, mk[2] = f.z, mk[3] = f.w;
         }
 #pragma unroll
+        for (int c = 0; c < 4; ++c) v[c] = v[c] * (mk[c] > 0.0f ? 1.0f : 0.0f);
+    }
+    if (p.out_bf16) {
+        __nv_bfloat162 lo = __floats2bfloat162_rn(v[0], v[1]), hi = __floats2bfloat162_rn(v[2], v[3]);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&lo);
+        u.y = *reinterpret_cast<uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.c) + i * p.ldc + j0) = u;
+    } else {
+        *reinterpret_cast<float4*>(static_cast<float*>(p.c) + i * p.ldc + j0) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+}
+
+// 16-byte loads and stores of 4-column groups are legal for this call.
+__host__ __device__ __forceinline__ bool four_aligned(const SkinnyParams& p) {
+    const int es = p.out_bf16 ? 2 : 4;
+    bool ok = (p.ldc % 4) == 0 && (reinterpret_cast<uintptr_t>(p.c) % (4 * es)) == 0;
+    if (p.epi == RT_EPI_BIAS || p.epi == RT_EPI_BIAS_RELU) ok = ok && (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0;
+    if (p.epi == RT_EPI_RELU_MASK)
+        ok = ok && (p.ldmask % 4) == 0 && (reinterpret_cast<uintptr_t>(p.mask) % (4 * es)) == 0;
+    return ok;
+}
+
+// Sum of v[0..15] over the 32 lanes of a warp, reduce-scattered: at each of
+// four levels a lane keeps the half of its values its lane bit selects and
+// adds its partner's copy of that half (8 + 4 + 2 + 1 shuffles), then one
+// more exchange completes the pair.  Lanes 2c and 2c + 1 end with column c's
+// total; the summation order is fixed.
+__device__ __forceinline__ float warp_sum16_scatter(float (&v)[16], int lane) {
+    float a8[8], a4[4], a2[2], a1;
+    const bool b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1, b1 = (lane >> 1) & 1;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float send = b4 ? v[i] : v[8 + i];
+        const float keep = b4 ? v[8 + i] : v[i];
+        a8[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float send = b3 ? a8[i] : a8[4 + i];
+        const float keep = b3 ? a8[4 + i] : a8[i];
+        a4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const float send = b2 ? a4[i] : a4[2 + i];
+        const float keep = b2 ? a4[2 + i] : a4[i];
+        a2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    {
+        const float send = b1 ? a2[0] : a2[1];
+        const float keep = b1 ? a2[1] : a2[0];
+        a1 = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    }
+    return a1 + __shfl_xor_sync(0xffffffffu, a1, 1);
+}
+
+// Narrow N (n <= 16), A K-major (layouts NN and NT): one warp per row of C,
+// eight rows per block.  The block stages B in 1024-row chunks in shared
+// memory ([k][16], rows padded to 20 floats so a warp's 16-byte reads of 8
+// different rows hit distinct banks); the warp's lanes stride over k reading
+// A coalesced, all 32 of a chunk's loads in flight per lane, and accumulate
+// the 16 partial dot products, which a reduce-scatter (16 shuffles) leaves in
+// lane 2c for column c.  One chunk covers the output layers of the reference
+// MLPs (k <= 1024), so their A and B loads are a single round trip.
+template <typename TIn, bool B_KMAJOR>
+__global__ void __launch_bounds__(kThreads) skinny_n_kernel(SkinnyParams p) {
+    constexpr int U = 32, KC = 32 * U, BP = 20;  // k rows per chunk, padded row length of staged B
+    extern __shared__ __align__(16) float sb_raw[];
+    float(*sb)[BP] = reinterpret_cast<float(*)[BP]>(sb_raw);
+    const TIn* A = static_cast<const TIn*>(p.a);
+    const TIn* B = static_cast<const TIn*>(p.b);
+    const int lane = threadIdx.x & 31;
+    const int64_t i = ((int64_t)blockIdx.x * kThreads + threadIdx.x) >> 5;
+    const bool row_ok = i < p.m;  // warp-uniform; every warp still helps stage B
+    const int n = (int)p.n;
+    float acc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
+    const TIn* arow = A + (row_ok ? i : 0) * p.lda;
+    for (int64_t kc = 0; kc < p.k; kc += KC) {
+        float a[U];
+#pragma unroll
         for (int u = 0; u < U; ++u) {
-            const int64_t q = q0 + (int64_t)u * kThreads;
-            if (q < p.k) {
+            const int64_t q = kc + lane + 32 * u;
+            a[u] = (row_ok && q < p.k) ? ld_f(arow, q) : 0.0f;
+        }
+        __syncthreads();  // the previous chunk's reads of sb are done
+        const int kn = (int)min((int64_t)KC, p.k - kc);
+        if (!B_KMAJOR && sizeof(TIn) == 4 && n == 16 && (p.ldb % 4) == 0 &&
+            (reinterpret_cast<uintptr_t>(p.b) & 15) == 0) {
+            // whole 16-float B rows as four 16-byte loads
+            for (int t = threadIdx.x; t < kn * 4; t += kThreads) {
+                const int r = t / 4, c4 = t % 4;
+                const float4 v = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(B) +
+                                                                       (kc + r) * p.ldb) + c4);
+                *reinterpret_cast<float4*>(&sb[r][4 * c4]) = v;
+            }
+        } else {
+            for (int t = threadIdx.x; t < kn * 16; t += kThreads) {
+                // NN: consecutive threads walk a B row (16 columns); NT: a B row is a
+                // column j of C, so consecutive threads walk k instead
+                const int r = B_KMAJOR ? t % kn : t / 16, j = B_KMAJOR ? t / kn : t % 16;
+                const int64_t q = kc + r;
+                sb[r][j] = j < n ? ld_f(B, B_KMAJOR ? (int64_t)j * p.ldb + q : q * p.ldb + j) : 0.0f;
+            }
+        }
+        __syncthreads();
 #pragma unroll
-                for (int j = 0; j < NMAX; ++j) {
-                    if (j < n) {
-                        const float bv = B_KMAJOR ? ld_f(B, (int64_t)j * p.ldb + q) : ld_f(B, q * p.ldb + j);
+        for (int u = 0; u < U; ++u) {
+            if (32 * u >= kn) break;  // a[u] is zero past k; its B rows were not staged
+            const float4* br = reinterpret_cast<const float4*>(&sb[lane + 32 * u][0]);
 #pragma unroll
-                        for (int r = 0; r < ROWS; ++r) acc[r][j] = fmaf(a[u][r], bv, acc[r][j]);
-                    }
-                }
+            for (int t4 = 0; t4 < 4; ++t4) {
+                const float4 b = br[t4];
+                acc[4 * t4 + 0] = fmaf(a[u], b.x, acc[4 * t4 + 0]);
+                acc[4 * t4 + 1] = fmaf(a[u], b.y, acc[4 * t4 + 1]);
+                acc[4 * t4 + 2] = fmaf(a[u], b.z, acc[4 * t4 + 2]);
+                acc[4 * t4 + 3] = fmaf(a[u], b.w, acc[4 * t4 + 3]);
             }
         }
     }
-#pragma unroll
-    for (int r = 0; r < ROWS; ++r)
-#pragma unroll
-        for (int j = 0; j < NMAX; ++j) {
-            float v = acc[r][j];
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-            if (lane == 0) red[warp][r][j] = v;
-        }
-    __syncthreads();
-    if (threadIdx.x < ROWS * NMAX) {
-        const int r = threadIdx.x / NMAX, j = threadIdx.x % NMAX;
-        if (j < n && i0 + r < p.m) {
-            float v = 0.0f;
-#pragma unroll
-            for (int w = 0; w < WARPS; ++w) v += red[w][r][j];
-            finish_one(p, i0 + r, j, v);
-        }
-    }
+    const float v = warp_sum16_scatter(acc, lane);
+    const int c = lane >> 1;
+    if (row_ok && (lane & 1) == 0 && c < n) finish_one(p, i, c, v);
 }
 
 // Narrow N, A MN-major (layout TN, the dW of the output layer): thread i of
 // the grid owns row i of C (column i of A's storage); every k row of A is
-// read coalesced once (eight rows in flight per thread), the k rows of B are
-// broadcast from shared memory.  blockIdx.y takes a k slice; with more than
-// one slice the partial sums go to p.ws and the fixed-order split-K reduction
-// finishes them.
+// read coalesced once (sixteen rows in flight per thread), the k rows of B
+// are broadcast from shared memory.  blockIdx.y takes a k slice; with more
+// than one slice the partial sums go to p.ws and the fixed-order split-K
+// reduction finishes them.
 template <typename TIn, int NMAX>
 __global__ void __launch_bounds__(kThreads) skinny_n_tn_kernel(SkinnyParams p) {
     constexpr int KC = 64;  // k rows of B staged per pass
-    constexpr int U = 8;
-    __shared__ float sb[KC][NMAX];
+    constexpr int U = 16;
+    __shared__ __align__(16) float sb[KC][NMAX];
     const TIn* A = static_cast<const TIn*>(p.a);
     const TIn* B = static_cast<const TIn*>(p.b);
     const int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
@@ -159,9 +251,17 @@ __global__ void __launch_bounds__(kThreads) skinny_n_tn_kernel(SkinnyParams p) {
 #pragma unroll
                 for (int u = 0; u < U; ++u) a[u] = r0 + u < kn ? ld_f(A, (kc + r0 + u) * p.lda + i) : 0.0f;
 #pragma unroll
-                for (int u = 0; u < U; ++u)
+                for (int u = 0; u < U; ++u) {
+                    const float4* br = reinterpret_cast<const float4*>(&sb[r0 + u][0]);  // a broadcast
 #pragma unroll
-                    for (int j = 0; j < NMAX; ++j) acc[j] = fmaf(a[u], sb[r0 + u][j], acc[j]);
+                    for (int t4 = 0; t4 < NMAX / 4; ++t4) {
+                        const float4 b = br[t4];
+                        acc[4 * t4 + 0] = fmaf(a[u], b.x, acc[4 * t4 + 0]);
+                        acc[4 * t4 + 1] = fmaf(a[u], b.y, acc[4 * t4 + 1]);
+                        acc[4 * t4 + 2] = fmaf(a[u], b.z, acc[4 * t4 + 2]);
+                        acc[4 * t4 + 3] = fmaf(a[u], b.w, acc[4 * t4 + 3]);
+                    }
+                }
             }
         }
     }
@@ -178,15 +278,15 @@ __global__ void __launch_bounds__(kThreads) skinny_n_tn_kernel(SkinnyParams p) {
     }
 }
 
-// Narrow K (k <= KMAX): a block computes a TM x 256 tile of C.  Its threads
-// each hold the k x 4 slab of B for four consecutive columns in registers and
-// walk down the tile's rows, reading the row's k values of A from shared
-// memory (a broadcast) and storing four columns at once when the row is
-// aligned for it.
+// Narrow K (k <= KMAX): a block computes a 32 x 256 tile of C.  Each thread
+// holds the k x 4 slab of B for four consecutive columns in registers and
+// walks down eight of the tile's rows, reading each row's k values of A from
+// shared memory (a 16-byte broadcast per four k) and finishing four columns
+// with 16-byte loads and stores.
 template <typename TIn, int KMAX, bool A_KMAJOR, bool B_KMAJOR>
 __global__ void __launch_bounds__(kThreads) skinny_k_kernel(SkinnyParams p) {
-    constexpr int TM = 64, TN = 4 * 64;
-    __shared__ float sa[TM][KMAX];
+    constexpr int TM = 32, TN = 4 * 64, RPT = TM / (kThreads / 64);  // rows per thread
+    __shared__ __align__(16) float sa[TM][KMAX];
     const TIn* A = static_cast<const TIn*>(p.a);
     const TIn* B = static_cast<const TIn*>(p.b);
     const int64_t m0 = (int64_t)blockIdx.y * TM, n0 = (int64_t)blockIdx.x * TN;
@@ -196,8 +296,8 @@ __global__ void __launch_bounds__(kThreads) skinny_k_kernel(SkinnyParams p) {
         const int64_t i = m0 + r;
         sa[r][q] = (i < p.m && q < k) ? ld_f(A, A_KMAJOR ? i * p.lda + q : (int64_t)q * p.lda + i) : 0.0f;
     }
-    const int cg = threadIdx.x % 64;        // column group: 4 columns
-    const int rg = threadIdx.x / 64;        // row phase: rows rg, rg + 4, ...
+    const int cg = threadIdx.x % 64;  // column group: 4 columns
+    const int rg = threadIdx.x / 64;  // rows rg, rg + 4, ...
     const int64_t j0 = n0 + cg * 4;
     float b[KMAX][4];
 #pragma unroll
@@ -206,24 +306,42 @@ __global__ void __launch_bounds__(kThreads) skinny_k_kernel(SkinnyParams p) {
         for (int c = 0; c < 4; ++c)
             b[q][c] = (q < k && j0 + c < p.n) ? ld_f(B, B_KMAJOR ? (j0 + c) * p.ldb + q : (int64_t)q * p.ldb + j0 + c)
                                              : 0.0f;
+    const bool vec = j0 + 4 <= p.n && four_aligned(p);
+    // the ReLU-mask epilogue's loads for all of this thread's rows, in flight together
+    float4 mk[RPT];
+    const bool pre_mask = vec && p.epi == RT_EPI_RELU_MASK && !p.out_bf16 && !p.opt.kind;
+    if (pre_mask) {
+#pragma unroll
+        for (int t = 0; t < RPT; ++t) {
+            const int64_t i = m0 + rg + t * (kThreads / 64);
+            mk[t] = i < p.m ? *reinterpret_cast<const float4*>(static_cast<const float*>(p.mask) + i * p.ldmask + j0)
+                            : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+    }
     __syncthreads();
     if (j0 >= p.n) return;
-    const bool plain_vec = p.epi == RT_EPI_NONE && !p.opt.kind && !p.out_bf16 && j0 + 4 <= p.n &&
-                           (p.ldc % 4) == 0 && ((reinterpret_cast<uintptr_t>(p.c) & 15) == 0);
-    for (int r = rg; r < TM; r += kThreads / 64) {
+#pragma unroll
+    for (int t = 0; t < RPT; ++t) {
+        const int r = rg + t * (kThreads / 64);
         const int64_t i = m0 + r;
         if (i >= p.m) break;
         float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int q = 0; q < KMAX; ++q) {
-            if (q < k) {
-                const float av = sa[r][q];
+        for (int q4 = 0; q4 < KMAX; q4 += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(&sa[r][q4]);
+            const float av[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
-                for (int c = 0; c < 4; ++c) v[c] = fmaf(av, b[q][c], v[c]);
-            }
+            for (int t = 0; t < 4; ++t)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) v[c] = fmaf(av[t], b[q4 + t][c], v[c]);
         }
-        if (plain_vec) {
-            *reinterpret_cast<float4*>(static_cast<float*>(p.c) + i * p.ldc + j0) = make_float4(v[0], v[1], v[2], v[3]);
+        if (pre_mask) {
+            const float4 m4 = mk[t];
+            *reinterpret_cast<float4*>(static_cast<float*>(p.c) + i * p.ldc + j0) =
+                make_float4(v[0] * (m4.x > 0.0f ? 1.0f : 0.0f), v[1] * (m4.y > 0.0f ? 1.0f : 0.0f),
+                            v[2] * (m4.z > 0.0f ? 1.0f : 0.0f), v[3] * (m4.w > 0.0f ? 1.0f : 0.0f));
+        } else if (vec) {
+            finish_four(p, i, j0, v, true);
         } else {
 #pragma unroll
             for (int c = 0; c < 4; ++c)
@@ -252,6 +370,15 @@ SkinnyParams make_params(const GemmDesc& g) {
     return p;
 }
 
+template <typename TIn, int KMAX>
+void launch_narrow_k(const GemmDesc& g, const SkinnyParams& p, dim3 grid, cudaStream_t st) {
+    switch (g.layout) {
+        case RT_NN: skinny_k_kernel<TIn, KMAX, true, false><<<grid, kThreads, 0, st>>>(p); break;
+        case RT_NT: skinny_k_kernel<TIn, KMAX, true, true><<<grid, kThreads, 0, st>>>(p); break;
+        case RT_TN: skinny_k_kernel<TIn, KMAX, false, false><<<grid, kThreads, 0, st>>>(p); break;
+    }
+}
+
 template <typename TIn>
 int launch_typed(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     SkinnyParams p = make_params(g);
@@ -259,7 +386,7 @@ int launch_typed(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
         if (g.layout == RT_TN) {
             int slices = g.split_k > 1 && g.workspace ? g.split_k : 1;
             int64_t kps = (g.k + slices - 1) / slices;
-            kps = (kps + 63) / 64 * 64;
+            kps = (kps + 15) / 16 * 16;
             slices = (int)((g.k + kps - 1) / kps);
             p.k_per_slice = kps;
             p.ws = slices > 1 ? g.workspace : nullptr;
@@ -274,20 +401,20 @@ int launch_typed(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
             }
             return RT_OK;
         }
-        constexpr int ROWS = 4;
-        const int64_t blocks = (g.m + ROWS - 1) / ROWS;
+        const int64_t blocks = (g.m * 32 + kThreads - 1) / kThreads;  // one warp per row
         if (g.layout == RT_NT)
-            skinny_n_kernel<TIn, kSkinnyMax, true, ROWS><<<(unsigned)blocks, kThreads, 0, st>>>(p);
+            skinny_n_kernel<TIn, true><<<(unsigned)blocks, kThreads, kSkinnyNSmem, st>>>(p);
         else
-            skinny_n_kernel<TIn, kSkinnyMax, false, ROWS><<<(unsigned)blocks, kThreads, 0, st>>>(p);
+            skinny_n_kernel<TIn, false><<<(unsigned)blocks, kThreads, kSkinnyNSmem, st>>>(p);
     } else {
-        dim3 grid((unsigned)((g.n + 255) / 256), (unsigned)((g.m + 63) / 64));
+        dim3 grid((unsigned)((g.n + 255) / 256), (unsigned)((g.m + 31) / 32));
         if (grid.y > 65535u) return fail(RT_ERR_INVALID, "narrow-k GEMM m=%lld too large for its grid", (long long)g.m);
-        switch (g.layout) {
-            case RT_NN: skinny_k_kernel<TIn, kSkinnyMax, true, false><<<grid, kThreads, 0, st>>>(p); break;
-            case RT_NT: skinny_k_kernel<TIn, kSkinnyMax, true, true><<<grid, kThreads, 0, st>>>(p); break;
-            case RT_TN: skinny_k_kernel<TIn, kSkinnyMax, false, false><<<grid, kThreads, 0, st>>>(p); break;
-        }
+        if (g.k <= 4)
+            launch_narrow_k<TIn, 4>(g, p, grid, st);
+        else if (g.k <= 8)
+            launch_narrow_k<TIn, 8>(g, p, grid, st);
+        else
+            launch_narrow_k<TIn, 16>(g, p, grid, st);
     }
     count_launch(ctx);
     RT_CUDA(cudaGetLastError());
@@ -295,6 +422,18 @@ int launch_typed(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
 }
 
 }  // namespace
+
+int gemm_skinny_init() {
+    RT_CUDA(cudaFuncSetAttribute(skinny_n_kernel<float, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kSkinnyNSmem));
+    RT_CUDA(cudaFuncSetAttribute(skinny_n_kernel<float, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kSkinnyNSmem));
+    RT_CUDA(cudaFuncSetAttribute(skinny_n_kernel<__nv_bfloat16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kSkinnyNSmem));
+    RT_CUDA(cudaFuncSetAttribute(skinny_n_kernel<__nv_bfloat16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kSkinnyNSmem));
+    return RT_OK;
+}
 
 bool gemm_skinny_wanted(const GemmDesc& g) {
     return g.m >= 1 && g.k >= 1 && (g.n <= kSkinnyMax || g.k <= kSkinnyMax);

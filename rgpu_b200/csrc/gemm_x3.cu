@@ -16,7 +16,7 @@
 // workspace, K-major for both ([m][k] for A, [n][k] for B): tcgen05 reads
 // MN-major tf32 operands only in the 32-byte-atom 128-byte swizzle, so an
 // operand stored MN-major ([k][m] for A in dW = X^T dY, [k][n] for B in
-// Y = X W) is transposed on the way, through a 32 x 32 shared-memory tile
+// Y = X W) is transposed on the way, through a 64 x 64 shared-memory tile
 // that keeps both the reads and the writes coalesced.  The GEMM is the
 // one-CTA tcgen05 kernel of gemm_tc.cu in its X3 form (both operands
 // K-major): 3-D TMA maps whose third coordinate picks the plane, and a k loop
@@ -78,16 +78,17 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
     }
 }
 
-constexpr int kSplitThreads = 256;  // (32, 8)
+constexpr int kSplitThreads = 256;
+constexpr int kT = 64;  // transposing tile: 64 k x 64 mn
 
 // blockIdx.y selects the operand (uniform per block, so the barriers of the
 // transposing form are reached by every thread of the block).
 __global__ void __launch_bounds__(kSplitThreads) split_planes_kernel(Operand a, Operand b) {
-    __shared__ float tile[32][33];
+    __shared__ float tile[kT][kT + 1];
     const Operand& o = blockIdx.y == 0 ? a : b;
     float* hi_plane = o.dst;
     float* lo_plane = o.dst + (size_t)o.mn * o.ldw;
-    const int tid = threadIdx.y * 32 + threadIdx.x;
+    const int tid = threadIdx.x;
     if (!o.transpose) {
         const int64_t stride = (int64_t)gridDim.x * kSplitThreads;
         const bool vec = (o.k % 4 == 0) && (o.ld_src % 4 == 0) && ((reinterpret_cast<uintptr_t>(o.src) & 15) == 0);
@@ -117,25 +118,51 @@ __global__ void __launch_bounds__(kSplitThreads) split_planes_kernel(Operand a, 
         }
         return;
     }
-    // transposing form: source [k][mn] -> planes [mn][k], one 32 x 32 tile at a time
-    const int64_t tiles_mn = (o.mn + 31) / 32, tiles_k = (o.k + 31) / 32;
-    const int tx = threadIdx.x, ty = threadIdx.y;
+    // transposing form: source [k][mn] -> planes [mn][k], one 64 x 64 tile at a
+    // time.  Reads: 16 threads cover a 256-byte source row segment (float4);
+    // writes: 16 threads cover a 256-byte plane row segment (float4).
+    const int64_t tiles_mn = (o.mn + kT - 1) / kT, tiles_k = (o.k + kT - 1) / kT;
+    const int quad = tid % 16, rsub = tid / 16;  // 16 quads x 16 rows per pass, 4 passes
+    const bool src_vec = (o.ld_src % 4 == 0) && ((reinterpret_cast<uintptr_t>(o.src) & 15) == 0);
     for (int64_t t = blockIdx.x; t < tiles_mn * tiles_k; t += gridDim.x) {
-        const int64_t mn0 = (t % tiles_mn) * 32, k0 = (t / tiles_mn) * 32;
+        const int64_t mn0 = (t % tiles_mn) * kT, k0 = (t / tiles_mn) * kT;
+        const bool full_mn = mn0 + kT <= o.mn;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int64_t r = k0 + ty + 8 * j, c = mn0 + tx;
-            tile[ty + 8 * j][tx] = (r < o.k && c < o.mn) ? __ldg(o.src + r * o.ld_src + c) : 0.0f;
+        for (int pass = 0; pass < 4; ++pass) {
+            const int r = rsub + 16 * pass;  // k row within the tile
+            const int64_t kk = k0 + r, c = mn0 + 4 * quad;
+            float v[4];
+            if (kk < o.k && full_mn && src_vec) {
+                const float4 x = __ldg(reinterpret_cast<const float4*>(o.src + kk * o.ld_src + c));
+                v[0] = x.x, v[1] = x.y, v[2] = x.z, v[3] = x.w;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) v[e] = (kk < o.k && c + e < o.mn) ? __ldg(o.src + kk * o.ld_src + c + e) : 0.0f;
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) tile[r][4 * quad + e] = v[e];
         }
         __syncthreads();
+        const bool full_k = k0 + kT <= o.k;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int64_t r = mn0 + ty + 8 * j, c = k0 + tx;
-            if (r < o.mn && c < o.k) {
-                float h, l;
-                split_tf32(tile[tx][ty + 8 * j], h, l);
-                hi_plane[r * o.ldw + c] = h;
-                lo_plane[r * o.ldw + c] = l;
+        for (int pass = 0; pass < 4; ++pass) {
+            const int r = rsub + 16 * pass;  // mn row within the tile
+            const int64_t row = mn0 + r, c = k0 + 4 * quad;
+            if (row < o.mn) {
+                float h[4], l[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) split_tf32(tile[4 * quad + e][r], h[e], l[e]);
+                if (full_k) {
+                    *reinterpret_cast<float4*>(hi_plane + row * o.ldw + c) = make_float4(h[0], h[1], h[2], h[3]);
+                    *reinterpret_cast<float4*>(lo_plane + row * o.ldw + c) = make_float4(l[0], l[1], l[2], l[3]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        if (c + e < o.k) {
+                            hi_plane[row * o.ldw + c + e] = h[e];
+                            lo_plane[row * o.ldw + c + e] = l[e];
+                        }
+                }
             }
         }
         __syncthreads();
@@ -173,13 +200,13 @@ int launch_gemm_x3(rt_ctx* ctx, const GemmDesc& g, float* ws, size_t ws_bytes, c
     Operand a = operand_a(g), b = operand_b(g);
     a.dst = ws;
     b.dst = ws + round_up((int64_t)(2 * plane_floats(a)), 64);
-    // enough blocks for the larger operand: 1024 elements per block and pass
+    // enough blocks for the larger operand: 4096 elements per block and pass
     const int64_t work = a.mn * a.k > b.mn * b.k ? a.mn * a.k : b.mn * b.k;
-    int64_t blocks = (work + 1023) / 1024;
+    int64_t blocks = (work + 4095) / 4096;
     const int64_t cap = (int64_t)ctx->sm_count * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    split_planes_kernel<<<dim3((unsigned)blocks, 2), dim3(32, 8), 0, st>>>(a, b);
+    split_planes_kernel<<<dim3((unsigned)blocks, 2), kSplitThreads, 0, st>>>(a, b);
     count_launch(ctx);
     RT_CUDA(cudaGetLastError());
     X3Planes x3{a.dst, a.ldw, (int64_t)plane_floats(a), b.dst, b.ldw, (int64_t)plane_floats(b)};

@@ -133,6 +133,7 @@ int choose_split_k(const rt_ctx* ctx, int64_t m, int64_t n, int64_t k, rt_dtype 
 // output layer) on CUDA cores: one pass over the large operand.
 constexpr int kSkinnyMax = 16;
 bool gemm_skinny_wanted(const GemmDesc& g);
+int gemm_skinny_init();
 int launch_gemm_skinny(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream);
 
 int launch_xent(rt_ctx* ctx, const float* logits, int64_t ldz, const uint32_t* labels, int64_t n,

@@ -594,9 +594,9 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
         // (the library's rule; the output layer's narrow-N dW slices the same way)
         int split = choose_split_k(ctx, P.d + 1, P.u, m->n, m->adt);
         if (P.u <= kSkinnyMax) {
-            // the skinny dW kernel slices k in 64-row steps: up to 16 slices, >= 128 rows each
-            int64_t sp = m->n / 128;
-            split = (int)(sp < 1 ? 1 : sp > 16 ? 16 : sp);
+            // the skinny dW kernel: up to 64 k slices of >= 32 rows (its threads are latency bound)
+            int64_t sp = m->n / 32;
+            split = (int)(sp < 1 ? 1 : sp > 64 ? 64 : sp);
         }
         P.split_dw = split;
         if (split > 1) {

@@ -90,6 +90,7 @@ int rt_ctx_create(int device, rt_ctx** out) {
     int st = gemm_tc_init(c);
     if (st == RT_OK) st = gemm_tc2_init(c);
     if (st == RT_OK) st = gemm_x3_init(c);
+    if (st == RT_OK) st = gemm_skinny_init();
     if (st != RT_OK) {
         cudaFree(c->dev_err);
         cudaStreamDestroy(c->own_stream);
