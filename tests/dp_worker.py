@@ -35,7 +35,10 @@ def main():
     comm = rgpu_b200.Comm(gpu, rank, world, bytes(uid.cpu().numpy().tobytes()))
 
     rng = np.random.default_rng(7)
-    dims = [64, 256, 192, 10]
+    # 1025 rows of [W_0; b_0]: the plan can cut the first layer's dW GEMM into
+    # 4 chunks on 256-row edges (RTGPU_FIRST_LAYER_CHUNKS=4 below), whose
+    # allreduces and updates then run per chunk
+    dims = [1024, 256, 192, 10]
     params = []
     for l in range(len(dims) - 1):
         lim = np.sqrt(6.0 / dims[l])
@@ -47,7 +50,10 @@ def main():
     per = n_global // world
     xs, ls = x[rank * per:(rank + 1) * per], labels[rank * per:(rank + 1) * per]
     result = {}
-    for dtype in ("f32", "bf16"):
+    for dtype, chunks in (("f32", "1"), ("bf16", "1"), ("f32_chunked", "4")):
+        os.environ["RTGPU_FIRST_LAYER_CHUNKS"] = chunks
+        dtype_name = dtype
+        dtype = dtype.split("_")[0]
         mlp = rgpu_b200.GpuMlp.from_params(gpu, params, per, 0.0, dtype=dtype, optimizer="none",
                                            global_batch=n_global)
         mlp.set_comm(comm)
@@ -59,8 +65,10 @@ def main():
             ref.step(gpu.upload(x), rgpu_b200.upload_labels(gpu, labels))
             g_ref = ref.grads()
             ref.close()
-            result[dtype] = [float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)) for a, b in zip(g_dp, g_ref)]
-    # Adam: replicas stay bit-identical.
+            result[dtype_name] = [float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+                                  for a, b in zip(g_dp, g_ref)]
+    # Adam with the chunked first layer: replicas stay bit-identical.
+    os.environ["RTGPU_FIRST_LAYER_CHUNKS"] = "4"
     mlp = rgpu_b200.GpuMlp.from_params(gpu, params, per, 1e-3, dtype="bf16", optimizer="adam", global_batch=n_global)
     mlp.set_comm(comm)
     gx, gl = gpu.upload(xs), rgpu_b200.upload_labels(gpu, ls)
