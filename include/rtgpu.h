@@ -244,6 +244,29 @@ int rt_mlp_weights(rt_mlp* mlp, int layer, float* w, float* b);
 int rt_mlp_grads(rt_mlp* mlp, int layer, float* dw, float* db);
 /* Param::set (tape.rs:119-121) on the device copy: overwrite W_l / b_l. */
 int rt_mlp_set_weights(rt_mlp* mlp, int layer, const float* w, const float* b);
+/* Checkpoint / resume of a plan's training state: the f32 masters [W_l; b_l],
+ * the Adam moments m_l, v_l and the Adam step count.  The reference keeps no
+ * such state format; its nearest pieces are GpuMlp::weights
+ * (gpu/mod.rs:1534-1551) and Param::set (tape.rs:119-121), which carry the
+ * weights but not the optimiser.  Buffer layout (host byte order):
+ *   rt_mlp_state_header, dims[n_layers + 1] (int64),
+ *   then per layer l: [d_l + 1, d_{l+1}] f32 row-major ([W_l; b_l], bias last),
+ *   and for Adam the m_l and v_l blocks of the same shape.
+ * Save waits for the device; load checks the header against the plan (layer
+ * dims and optimiser must match), restores the step count and rebuilds the
+ * bf16 weight shadow.  Data-parallel ranks hold identical state: save on one
+ * rank, load on every rank. */
+#define RT_MLP_STATE_MAGIC 0x534D5452u /* "RTMS" */
+typedef struct {
+    uint32_t magic;
+    uint32_t version;  /* 1 */
+    int32_t n_layers;
+    int32_t optimizer; /* rt_optimizer */
+    int64_t adam_step; /* Adam steps taken (bias-correction t) */
+} rt_mlp_state_header;
+int rt_mlp_state_size(rt_mlp* mlp, size_t* bytes);
+int rt_mlp_save_state(rt_mlp* mlp, void* host, size_t bytes);
+int rt_mlp_load_state(rt_mlp* mlp, const void* host, size_t bytes);
 /* GpuMlp::dispatches_por_passo (gpu/mod.rs:1559-1561): kernels per step. */
 int rt_mlp_dispatches_per_step(rt_mlp* mlp, int* out);
 /* Gpu::perfilar (gpu/mod.rs:1245-1286): when on, the captured step records a

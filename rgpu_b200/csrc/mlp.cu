@@ -723,6 +723,115 @@ int rt_mlp_set_weights(rt_mlp* m, int layer, const float* w, const float* b) {
     return RT_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+// Byte size of the state buffer and, when `blocks` is non-null, each layer's
+// block sizes in floats.
+size_t state_bytes(const rt_mlp* m) {
+    size_t b = sizeof(rt_mlp_state_header) + sizeof(int64_t) * m->dims.size();
+    const size_t per = m->cfg.optimizer == RT_OPT_ADAM ? 3 : 1;
+    for (const PlanLayer& P : m->L) b += per * (size_t)(P.d + 1) * P.u * sizeof(float);
+    return b;
+}
+
+// Copies the [d+1, u] block of a [d+1, ld] device buffer to or from packed host memory.
+int copy_block(rt_mlp* m, const PlanLayer& P, float* dev, uint8_t* host, bool to_host) {
+    cudaStream_t st = m->ctx->stream;
+    if (to_host)
+        RT_CUDA(cudaMemcpy2DAsync(host, P.u * 4, dev, P.ld * 4, P.u * 4, P.d + 1, cudaMemcpyDeviceToHost, st));
+    else
+        RT_CUDA(cudaMemcpy2DAsync(dev, P.ld * 4, host, P.u * 4, P.u * 4, P.d + 1, cudaMemcpyHostToDevice, st));
+    return RT_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int rt_mlp_state_size(rt_mlp* m, size_t* bytes) {
+    RT_CHECK(m && bytes, "rt_mlp_state_size: bad arguments");
+    *bytes = state_bytes(m);
+    return RT_OK;
+}
+
+int rt_mlp_save_state(rt_mlp* m, void* host, size_t bytes) {
+    RT_CHECK(m && host, "rt_mlp_save_state: bad arguments");
+    RT_CHECK(bytes >= state_bytes(m), "rt_mlp_save_state: buffer of %zu bytes, state needs %zu", bytes,
+             state_bytes(m));
+    cudaStream_t st = m->ctx->stream;
+    RT_CUDA(cudaStreamSynchronize(st));  // the last step (and its side-stream updates) are done
+    OptScalars sc{};
+    RT_CUDA(cudaMemcpy(&sc, m->opt, sizeof(sc), cudaMemcpyDeviceToHost));
+    uint8_t* p = static_cast<uint8_t*>(host);
+    rt_mlp_state_header h{};
+    h.magic = RT_MLP_STATE_MAGIC;
+    h.version = 1;
+    h.n_layers = (int32_t)m->L.size();
+    h.optimizer = m->cfg.optimizer;
+    h.adam_step = sc.t;
+    std::memcpy(p, &h, sizeof(h));
+    p += sizeof(h);
+    std::memcpy(p, m->dims.data(), sizeof(int64_t) * m->dims.size());
+    p += sizeof(int64_t) * m->dims.size();
+    for (PlanLayer& P : m->L) {
+        const size_t blk = (size_t)(P.d + 1) * P.u * 4;
+        RT_TRY(copy_block(m, P, P.w32, p, true));
+        p += blk;
+        if (m->cfg.optimizer == RT_OPT_ADAM) {
+            RT_TRY(copy_block(m, P, P.m, p, true));
+            p += blk;
+            RT_TRY(copy_block(m, P, P.v, p, true));
+            p += blk;
+        }
+    }
+    RT_CUDA(cudaStreamSynchronize(st));
+    return RT_OK;
+}
+
+int rt_mlp_load_state(rt_mlp* m, const void* host, size_t bytes) {
+    RT_CHECK(m && host, "rt_mlp_load_state: bad arguments");
+    RT_CHECK(bytes >= sizeof(rt_mlp_state_header), "rt_mlp_load_state: buffer too small for a header");
+    const uint8_t* p = static_cast<const uint8_t*>(host);
+    rt_mlp_state_header h;
+    std::memcpy(&h, p, sizeof(h));
+    RT_CHECK(h.magic == RT_MLP_STATE_MAGIC && h.version == 1, "rt_mlp_load_state: not a version-1 plan state");
+    RT_CHECK(h.n_layers == (int32_t)m->L.size(), "rt_mlp_load_state: state has %d layers, plan %d", h.n_layers,
+             (int)m->L.size());
+    RT_CHECK(h.optimizer == m->cfg.optimizer, "rt_mlp_load_state: state optimiser %d, plan %d", h.optimizer,
+             (int)m->cfg.optimizer);
+    RT_CHECK(bytes >= state_bytes(m), "rt_mlp_load_state: buffer of %zu bytes, state needs %zu", bytes,
+             state_bytes(m));
+    p += sizeof(h);
+    for (size_t l = 0; l < m->dims.size(); ++l) {
+        int64_t d;
+        std::memcpy(&d, p + l * sizeof(int64_t), sizeof(d));
+        RT_CHECK(d == m->dims[l], "rt_mlp_load_state: dims[%zu] is %lld in the state, %lld in the plan", l,
+                 (long long)d, (long long)m->dims[l]);
+    }
+    p += sizeof(int64_t) * m->dims.size();
+    cudaStream_t st = m->ctx->stream;
+    RT_CUDA(cudaStreamSynchronize(st));
+    for (PlanLayer& P : m->L) {
+        const size_t blk = (size_t)(P.d + 1) * P.u * 4;
+        RT_TRY(copy_block(m, P, P.w32, const_cast<uint8_t*>(p), false));
+        p += blk;
+        if (m->cfg.optimizer == RT_OPT_ADAM) {
+            RT_TRY(copy_block(m, P, P.m, const_cast<uint8_t*>(p), false));
+            p += blk;
+            RT_TRY(copy_block(m, P, P.v, const_cast<uint8_t*>(p), false));
+            p += blk;
+        }
+        RT_TRY(refresh_shadow(m, P, st));
+    }
+    OptScalars sc{};
+    sc.t = (int)h.adam_step;  // the next step recomputes the bias corrections from t + 1
+    RT_CUDA(cudaMemcpyAsync(m->opt, &sc, sizeof(sc), cudaMemcpyHostToDevice, st));
+    RT_CUDA(cudaStreamSynchronize(st));
+    return RT_OK;
+}
+
 int rt_mlp_dispatches_per_step(rt_mlp* m, int* out) {
     RT_CHECK(m && out, "bad arguments");
     if (!m->slot[0].exec) RT_TRY(capture_step(m, 0));

@@ -114,6 +114,9 @@ _SIGS = [
     ("rt_mlp_weights", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     ("rt_mlp_grads", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     ("rt_mlp_set_weights", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
+    ("rt_mlp_state_size", C.c_int, [C.c_void_p, C.POINTER(C.c_size_t)]),
+    ("rt_mlp_save_state", C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
+    ("rt_mlp_load_state", C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
     ("rt_mlp_dispatches_per_step", C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
     ("rt_mlp_enable_timing", C.c_int, [C.c_void_p, C.c_int]),
     ("rt_mlp_op_count", C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
@@ -519,6 +522,28 @@ class GpuMlp:
         b = None if b is None else np.ascontiguousarray(b, np.float32)
         _check(lib().rt_mlp_set_weights(self.handle, layer, None if w is None else w.ctypes.data,
                                         None if b is None else b.ctypes.data))
+
+    def save_state(self) -> bytes:
+        """Checkpoint of the training state: f32 weights and biases, Adam
+        moments and step count (the rt_mlp_state_header layout)."""
+        n = C.c_size_t()
+        _check(lib().rt_mlp_state_size(self.handle, C.byref(n)))
+        buf = np.empty(n.value, np.uint8)
+        _check(lib().rt_mlp_save_state(self.handle, buf.ctypes.data, n.value))
+        return buf.tobytes()
+
+    def load_state(self, state: bytes):
+        """Resume from save_state()'s bytes (same layer dims and optimiser)."""
+        buf = np.frombuffer(state, np.uint8)
+        _check(lib().rt_mlp_load_state(self.handle, buf.ctypes.data, buf.nbytes))
+
+    def save(self, path: str):
+        with open(path, "wb") as f:
+            f.write(self.save_state())
+
+    def load(self, path: str):
+        with open(path, "rb") as f:
+            self.load_state(f.read())
 
     def batch_size(self) -> int:
         return self.lote

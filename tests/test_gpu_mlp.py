@@ -254,3 +254,48 @@ def test_timing_records_every_op(gpu):
     assert labels_seen.count("dx_gemm_relu_mask") == 2
     assert "softmax_xent" in labels_seen
     assert all(ms >= 0 for _, _, ms in ops)
+
+
+@pytest.mark.parametrize("dtype,opt,lr", [("bf16", "adam", 1e-3), ("f32", "sgd", 0.01), ("f32", "adam", 1e-3)])
+def test_checkpoint_resume_is_bit_exact(gpu, tmp_path, dtype, opt, lr):
+    # 3 steps, save, resume in a plan built from other weights, 2 more steps:
+    # identical (bit for bit) to 5 uninterrupted steps, moments and Adam step
+    # count included.
+    dims = [256, 512, 512, 10]
+    model, x, labels = baseline_inputs(dims, 128, 2030)
+    gx, gy = gpu.upload(x), rgpu_b200.upload_labels(gpu, labels)
+    ref = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 128, lr, dtype=dtype, optimizer=opt)
+    for _ in range(5):
+        ref.step(gx, gy)
+    want = ref.weights()
+    a = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 128, lr, dtype=dtype, optimizer=opt)
+    for _ in range(3):
+        a.step(gx, gy)
+    path = tmp_path / "state.rtms"
+    a.save(str(path))
+    other, _, _ = baseline_inputs(dims, 128, 99)
+    b = rgpu_b200.GpuMlp.from_params(gpu, other.params(), 128, lr, dtype=dtype, optimizer=opt)
+    b.load(str(path))
+    for wa, wb in zip(a.weights(), b.weights()):
+        assert np.array_equal(wa, wb)
+    for _ in range(2):
+        b.step(gx, gy)
+    for i, (w, g) in enumerate(zip(want, b.weights())):
+        assert np.array_equal(w, g), f"param {i} differs after resume"
+    assert b.save_state() == ref.save_state()
+
+
+def test_checkpoint_rejects_another_architecture(gpu):
+    model, x, labels = baseline_inputs([64, 128, 10], 32, 1)
+    a = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 32, 1e-3, optimizer="adam")
+    state = a.save_state()
+    other, _, _ = baseline_inputs([64, 96, 10], 32, 1)
+    b = rgpu_b200.GpuMlp.from_params(gpu, other.params(), 32, 1e-3, optimizer="adam")
+    with pytest.raises(rgpu_b200.RtError) as e:
+        b.load_state(state)
+    assert "dims[1]" in str(e.value)
+    c = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 32, 1e-3, optimizer="sgd")
+    with pytest.raises(rgpu_b200.RtError):
+        c.load_state(state)
+    with pytest.raises(rgpu_b200.RtError):
+        a.load_state(b"\0" * 64)
