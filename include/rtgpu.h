@@ -315,6 +315,40 @@ int rt_var_relu(rt_var* a, rt_var** out);
  * (u32 [rows]) in place of the one-hot rows; the scalar loss must be the root
  * of the backward sweep. */
 int rt_softmax_cross_entropy(rt_var* logits, const rt_tensor* labels, rt_var** out);
+/* The remaining differentiable ops of ops.rs on rank-2 values.  Binary ops
+ * broadcast a [1,n] row, [m,1] column or [1,1] scalar operand against [m,n]
+ * (tensor.rs:183-246) and reduce each operand's adjoint back to its shape
+ * (tensor.rs:399-438):
+ *   RT_ADD Var::add (ops.rs:49-53)   RT_SUB Var::sub (61-64)
+ *   RT_MUL Var::mul (76-82)          RT_DIV Var::div (93-101) */
+typedef enum { RT_ADD = 0, RT_SUB = 1, RT_MUL = 2, RT_DIV = 3 } rt_binary_op;
+int rt_var_binary(rt_var* a, rt_var* b, rt_binary_op op, rt_var** out);
+/* Pointwise ops; `param` is k for scale/offset and the slope for leaky_relu:
+ *   RT_SCALE Var::scale (ops.rs:132-135)   RT_OFFSET Var::offset (139-142)
+ *   RT_NEG Var::neg (145-147)              RT_SQUARE Var::square (150-154)
+ *   RT_SQRT Var::sqrt (158-162)            RT_EXP Var::exp (166-170)
+ *   RT_LN Var::ln (176-180)                RT_RELU Var::relu (190-194)
+ *   RT_LEAKY_RELU Var::leaky_relu (197-204)
+ *   RT_SIGMOID Var::sigmoid (212-216)      RT_TANH Var::tanh (223-227) */
+typedef enum {
+    RT_SCALE = 0, RT_OFFSET = 1, RT_NEG = 2, RT_SQUARE = 3, RT_SQRT = 4, RT_EXP = 5,
+    RT_LN = 6, RT_RELU = 7, RT_LEAKY_RELU = 8, RT_SIGMOID = 9, RT_TANH = 10
+} rt_unary_op;
+int rt_var_unary(rt_var* a, rt_unary_op op, float param, rt_var** out);
+/* Var::sum, Var::mean (ops.rs:239-255): scalar [1,1] results. */
+int rt_var_sum(rt_var* a, rt_var** out);
+int rt_var_mean(rt_var* a, rt_var** out);
+/* Var::softmax (ops.rs:288-309): row softmax with its O(c) adjoint. */
+int rt_var_softmax(rt_var* a, rt_var** out);
+/* losses::mse (losses.rs:31-34), losses::mae (46-55) and
+ * losses::binary_cross_entropy (143-160) against an f32 target of the
+ * prediction's shape (copied into the tape). */
+int rt_loss_mse(rt_var* pred, const rt_tensor* target, rt_var** out);
+int rt_loss_mae(rt_var* pred, const rt_tensor* target, rt_var** out);
+int rt_loss_bce(rt_var* probs, const rt_tensor* target, rt_var** out);
+/* losses::accuracy (losses.rs:181-185): fraction of rows whose first arg-max
+ * equals the label (u32 [rows]); blocking. */
+int rt_accuracy(rt_ctx* ctx, const rt_tensor* logits, const rt_tensor* labels, float* out);
 /* Var::value (tape.rs:143-145) as a device view; Tensor::item (blocking). */
 int rt_var_value(rt_var* v, rt_tensor** view);
 int rt_var_item(rt_var* v, float* out);
@@ -329,6 +363,12 @@ int rt_sgd_step(rt_ctx* ctx, int n, rt_param* const* params, rt_tape* grads, flo
 int rt_adam_create(rt_ctx* ctx, float lr, float beta1, float beta2, float eps, rt_adam_state** out);
 int rt_adam_destroy(rt_adam_state* a);
 int rt_adam_step(rt_adam_state* a, int n, rt_param* const* params, rt_tape* grads);
+/* Sgd::new / Sgd::with_momentum (optim.rs:64-77) and Sgd::step (81-114): the
+ * velocity v = v * mu + g * lr is kept per parameter, theta -= v. */
+typedef struct rt_sgd_state rt_sgd_state;
+int rt_sgd_create(rt_ctx* ctx, float lr, float momentum, rt_sgd_state** out);
+int rt_sgd_destroy(rt_sgd_state* s);
+int rt_sgd_state_step(rt_sgd_state* s, int n, rt_param* const* params, rt_tape* grads);
 
 /* ------------------------------------------------------------------ NCCL */
 /* 128-byte ncclUniqueId, created on one rank and shared out of band. */

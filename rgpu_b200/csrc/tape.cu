@@ -15,53 +15,15 @@
 // consumer (in-place accumulation, tape.rs:213-224), and Param::watch reuses
 // the parameter's leaf node when the same parameter is watched twice on one
 // tape (tape.rs:124-131).
-#include <functional>
-#include <unordered_map>
-#include <vector>
-
-#include "internal.h"
-
-namespace rt {
-int run_gemm(rt_ctx* ctx, GemmDesc g, cudaStream_t stream, size_t ws_bytes);
-
-int launch_axpy_inplace(rt_ctx* ctx, float* dst, int64_t ldd, const float* src, int64_t lds, int64_t rows,
-                        int64_t cols, cudaStream_t st);
-int launch_mean_rows(rt_ctx* ctx, const float* rows, int64_t n, float* out, cudaStream_t st);
-}  // namespace rt
+#include "tape_internal.h"
 
 using namespace rt;
+using rt::tp::Buf;
+using rt::tp::check_var;
+using rt::tp::ld_for;
+using rt::tp::Node;
 
 namespace {
-
-int64_t ld_for(int64_t cols) { return cols <= 4 ? 4 : (cols + 3) / 4 * 4; }
-
-// A device f32 matrix owned by a tape (or borrowed from a parameter).
-struct Buf {
-    float* p = nullptr;
-    int64_t rows = 0, cols = 0, ld = 0;
-};
-
-}  // namespace
-
-struct rt_param {
-    rt_ctx* ctx = nullptr;
-    Buf value;
-    uint64_t id = 0;
-};
-
-struct rt_var {
-    rt_tape* tape = nullptr;
-    int idx = 0;
-};
-
-namespace {
-
-struct Node {
-    std::vector<int> parents;
-    // Given the node's adjoint, adds each parent's contribution (via acc).
-    std::function<int(const Buf& g)> backward;
-    Buf value;
-};
 
 uint64_t next_param_id() {
     static uint64_t id = 0;
@@ -69,52 +31,6 @@ uint64_t next_param_id() {
 }
 
 }  // namespace
-
-struct rt_tape {
-    rt_ctx* ctx = nullptr;
-    std::vector<Node> nodes;
-    std::vector<rt_var*> vars;
-    std::unordered_map<uint64_t, int> param_nodes;
-    std::vector<Buf> grads;   // adjoint per node after backward (p == nullptr: none)
-    std::vector<void*> owned; // stream-ordered allocations to release
-    bool backward_done = false;
-
-    int alloc(Buf& b, int64_t rows, int64_t cols) {
-        b.rows = rows;
-        b.cols = cols;
-        b.ld = ld_for(cols);
-        size_t bytes = (size_t)(rows > 0 ? rows : 1) * (size_t)b.ld * 4;
-        RT_CUDA(cudaMallocAsync((void**)&b.p, bytes, ctx->stream));
-        owned.push_back(b.p);
-        RT_CUDA(cudaMemsetAsync(b.p, 0, bytes, ctx->stream));
-        return RT_OK;
-    }
-
-    rt_var* push(std::vector<int> parents, std::function<int(const Buf&)> bw, const Buf& value) {
-        Node n;
-        n.parents = std::move(parents);
-        n.backward = std::move(bw);
-        n.value = value;
-        nodes.push_back(std::move(n));
-        rt_var* v = new rt_var;
-        v->tape = this;
-        v->idx = (int)nodes.size() - 1;
-        vars.push_back(v);
-        return v;
-    }
-
-    // grads[i] += g   (allocates the adjoint on first contribution)
-    int accumulate(int i, const Buf& g) {
-        Buf& dst = grads[i];
-        if (!dst.p) {
-            RT_TRY(alloc(dst, g.rows, g.cols));
-            RT_CUDA(cudaMemcpy2DAsync(dst.p, dst.ld * 4, g.p, g.ld * 4, g.cols * 4, g.rows, cudaMemcpyDeviceToDevice,
-                                      ctx->stream));
-            return RT_OK;
-        }
-        return launch_axpy_inplace(ctx, dst.p, dst.ld, g.p, g.ld, g.rows, g.cols, ctx->stream);
-    }
-};
 
 namespace {
 
@@ -135,11 +51,6 @@ GemmDesc f32_gemm(rt_layout layout, int64_t m, int64_t n, int64_t k, const Buf& 
     g.epi = RT_EPI_NONE;
     g.split_k = 1;
     return g;
-}
-
-int check_var(const rt_var* v) {
-    RT_CHECK(v && v->tape && v->idx >= 0 && v->idx < (int)v->tape->nodes.size(), "invalid variable");
-    return RT_OK;
 }
 
 }  // namespace
@@ -287,7 +198,8 @@ int rt_var_matmul(rt_var* a, rt_var* b, rt_var** out) {
     return RT_OK;
 }
 
-// C = A + B with the row broadcast of a [1, n] operand (the +1b of Dense).
+// C = A + B; same shapes and the row broadcast of a [1, n] operand (the +1b
+// of Dense) run here, the other broadcasts through rt_var_binary.
 // Adjoints (ops.rs:49-53): each operand receives g reduced to its shape
 // (tensor.rs:399-438: the broadcast axis summed).
 int rt_var_add(rt_var* a, rt_var* b, rt_var** out) {
@@ -306,8 +218,9 @@ int rt_var_add(rt_var* a, rt_var* b, rt_var** out) {
     (void)swapped;
     const bool same = A.rows == B.rows && A.cols == B.cols;
     const bool row_bcast = B.rows == 1 && B.cols == A.cols;
-    RT_CHECK(same || row_bcast, "add: shapes [%lld,%lld] and [%lld,%lld] do not broadcast", (long long)A.rows,
-             (long long)A.cols, (long long)B.rows, (long long)B.cols);
+    // the other broadcasts (a column, a scalar, row against column) take the
+    // general elementwise path of tape_ops.cu
+    if (!same && !row_bcast) return rt_var_binary(a, b, RT_ADD, out);
     Buf C;
     RT_TRY(t->alloc(C, A.rows, A.cols));
     if (A.rows * A.cols > 0)

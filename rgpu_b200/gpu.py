@@ -137,6 +137,15 @@ _SIGS = [
     ("rt_var_add", C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
     ("rt_var_relu", C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
     ("rt_softmax_cross_entropy", C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("rt_var_binary", C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.POINTER(C.c_void_p)]),
+    ("rt_var_unary", C.c_int, [C.c_void_p, C.c_int, C.c_float, C.POINTER(C.c_void_p)]),
+    ("rt_var_sum", C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("rt_var_mean", C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("rt_var_softmax", C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("rt_loss_mse", C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("rt_loss_mae", C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("rt_loss_bce", C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("rt_accuracy", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(C.c_float)]),
     ("rt_var_value", C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
     ("rt_var_item", C.c_int, [C.c_void_p, C.POINTER(C.c_float)]),
     ("rt_var_backward", C.c_int, [C.c_void_p]),
@@ -145,6 +154,9 @@ _SIGS = [
     ("rt_adam_create", C.c_int, [C.c_void_p, C.c_float, C.c_float, C.c_float, C.c_float, C.POINTER(C.c_void_p)]),
     ("rt_adam_destroy", C.c_int, [C.c_void_p]),
     ("rt_adam_step", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
+    ("rt_sgd_create", C.c_int, [C.c_void_p, C.c_float, C.c_float, C.POINTER(C.c_void_p)]),
+    ("rt_sgd_destroy", C.c_int, [C.c_void_p]),
+    ("rt_sgd_state_step", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     ("rt_comm_unique_id", C.c_int, [C.c_void_p]),
     ("rt_comm_init", C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.POINTER(C.c_void_p)]),
     ("rt_comm_destroy", C.c_int, [C.c_void_p]),
