@@ -39,7 +39,7 @@ CPU_SAMPLE_ROWS = {"wide": 64, "small": 256}
 # two-CTA kernel), from an ncu capture (dram__bytes_read.sum +
 # dram__bytes_write.sum) of `bench.py --gemm TN --mnk 8192 8192 8192`; scaled
 # to other dW launches by their FLOPs.
-DW_GEMM_TRAFFIC_BYTES = 1.084e9 + 0.251e9
+DW_GEMM_TRAFFIC_BYTES = 1.099e9 + 0.251e9
 DW_GEMM_TRAFFIC_FLOPS = 2.0 * 8192 ** 3
 
 
@@ -301,6 +301,58 @@ def run_dw_sweep(args):
     gpu.close()
 
 
+def run_op(args):
+    """One HBM-bound kernel of the step on its own (the small case for ncu
+    captures of the elementwise kernels): `adam` updates an [rows, cols] f32
+    parameter (30 algorithmic bytes per element: theta, m, v, g read; theta, m,
+    v written; no shadow here, so 28), `xent` is the softmax-CE of [rows, cols]
+    f32 logits (4 C + 4 bytes read, 4 C + 4 written per row)."""
+    import torch
+
+    import rgpu_b200
+
+    gpu = rgpu_b200.Gpu(0)
+    rows, cols = args.op_shape
+    rng = np.random.default_rng(0)
+    st = torch.cuda.ExternalStream(gpu.stream())
+    if args.op == "adam":
+        z = lambda: gpu.upload(rng.standard_normal((rows, cols)).astype(np.float32))  # noqa: E731
+        theta, m, v, g = z(), gpu.zeros((rows, cols)), gpu.zeros((rows, cols)), z()
+        t = [0]
+
+        def fn():
+            t[0] += 1
+            gpu.adam(theta, m, v, g, 1e-3, t[0])
+
+        nbytes = 28.0 * rows * cols
+    else:
+        logits = gpu.upload(rng.standard_normal((rows, cols)).astype(np.float32))
+        labels = rgpu_b200.upload_labels(gpu, rng.integers(0, cols, rows))
+        delta, loss = gpu.zeros((rows, cols)), gpu.zeros((1, rows))
+
+        def fn():
+            gpu.softmax_xent(logits, labels, delta, loss)
+
+        nbytes = rows * (8.0 * cols + 8.0)
+    for _ in range(3):
+        fn()
+    gpu.sync()
+    with torch.cuda.stream(st):
+        torch.cuda._sleep(20000000)  # the host enqueues the timed launches meanwhile
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(args.reps):
+            fn()
+        e1.record(st)
+    gpu.sync()
+    ms = e0.elapsed_time(e1) / args.reps
+    pk = peaks()
+    print(json.dumps({"op": args.op, "rows": rows, "cols": cols, "ms": ms, "bytes": nbytes,
+                      "gbs": nbytes / (ms / 1e3) / 1e9, "frac_of_hbm": nbytes / (ms / 1e3) / 1e9 / pk["hbm"],
+                      "peak_source": pk["source"]}), flush=True)
+    gpu.close()
+
+
 def config_dict(cfg_name, cfg, n, global_batch):
     d = cfg["dims"]
     return {"workload": ("wide MLP " if cfg_name == "wide" else "MLP ") + "->".join(map(str, d)),
@@ -325,11 +377,16 @@ def main():
     ap.add_argument("--l2-group", type=int, default=0, help="GEMM raster group (tile rows), 0 = library default")
     ap.add_argument("--gemm-dtype", default="bf16", choices=["bf16", "f32"], help="operand dtype of --gemm")
     ap.add_argument("--sweep", action="store_true", help="dW = X^T dY sweep (BASELINE configs[3])")
+    ap.add_argument("--op", choices=["adam", "xent"], help="time one HBM-bound kernel alone")
+    ap.add_argument("--op-shape", type=int, nargs=2, default=[8192, 8192], metavar=("ROWS", "COLS"))
     ap.add_argument("--sweep-dtypes", default="f32,bf16")
     ap.add_argument("--sweep-k", default="", help="comma-separated K values (default: the full sweep)")
     args = ap.parse_args()
     if args.sweep:
         run_dw_sweep(args)
+        return
+    if args.op:
+        run_op(args)
         return
     if args.gemm:
         run_gemm_only(args)

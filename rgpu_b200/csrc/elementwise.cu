@@ -149,6 +149,15 @@ __device__ float powi_f32(float a, int b) {
     return recip ? 1.0f / r : r;
 }
 
+// Bias-correction scalars of Adam step t (optim.rs:574-583), t from the host.
+__global__ void opt_scalars_at_kernel(OptScalars* s, int t, float beta1, float beta2) {
+    s->t = t;
+    float c1 = __fsub_rn(1.0f, powi_f32(beta1, t));
+    float c2 = __fsub_rn(1.0f, powi_f32(beta2, t));
+    s->inv_c1 = __fdiv_rn(1.0f, c1);
+    s->inv_c2 = __fdiv_rn(1.0f, c2);
+}
+
 __global__ void opt_step_begin_kernel(OptScalars* s, float beta1, float beta2) {
     int t = s->t + 1;
     s->t = t;
@@ -423,6 +432,13 @@ int launch_fill_column(rt_ctx* ctx, void* p, rt_dtype dt, int64_t rows, int64_t 
 
 int launch_opt_step_begin(rt_ctx* ctx, OptScalars* s, float beta1, float beta2, cudaStream_t st) {
     opt_step_begin_kernel<<<1, 1, 0, st>>>(s, beta1, beta2);
+    count_launch(ctx);
+    RT_CUDA(cudaGetLastError());
+    return RT_OK;
+}
+
+int launch_opt_scalars_at(rt_ctx* ctx, OptScalars* s, int t, float beta1, float beta2, cudaStream_t st) {
+    opt_scalars_at_kernel<<<1, 1, 0, st>>>(s, t, beta1, beta2);
     count_launch(ctx);
     RT_CUDA(cudaGetLastError());
     return RT_OK;

@@ -51,6 +51,7 @@ struct rt_ctx {
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;
     int* dev_err = nullptr;  // [4] ints: first device error code, detail
+    rt::OptScalars* op_scalars = nullptr;  // Adam scalars for op-level rt_adam (inside dev_err's allocation)
     bool fast_gemm = true;
     bool pair_gemm = true;  // two-CTA tcgen05 tiles where the problem is large enough
     bool f32_tensor = true;  // f32 GEMMs on the tensor cores (3xTF32) when fast_gemm is on
@@ -169,6 +170,8 @@ struct OptTensor {
 };
 constexpr int kMaxOptTensors = 16;
 int launch_opt_step_begin(rt_ctx* ctx, OptScalars* s, float beta1, float beta2, cudaStream_t stream);
+// The scalars of Adam step t (t given by the host, no device read of t).
+int launch_opt_scalars_at(rt_ctx* ctx, OptScalars* s, int t, float beta1, float beta2, cudaStream_t stream);
 int launch_adam(rt_ctx* ctx, const OptTensor* ts, int count, const OptScalars* s, float lr, float beta1,
                 float beta2, float eps, cudaStream_t stream);
 int launch_sgd(rt_ctx* ctx, const OptTensor* ts, int count, float lr, cudaStream_t stream);

@@ -292,19 +292,12 @@ int rt_adam(rt_ctx* ctx, rt_tensor* theta, rt_tensor* m, rt_tensor* v, const rt_
              "adam: all buffers must be f32");
     RT_CHECK(flat_ok(theta, m) && flat_ok(theta, v) && flat_ok(theta, g), "adam: buffer layouts differ");
     RT_CHECK(t >= 1, "adam: step t must be >= 1");
-    OptScalars* s = nullptr;
-    // Scalars for an explicit t: computed by the same device routine the plan
-    // uses, from t-1.
-    RT_CUDA(cudaMallocAsync((void**)&s, sizeof(OptScalars), ctx->stream));
-    OptScalars h{t - 1, 0.f, 0.f, 0.f};
-    RT_CUDA(cudaMemcpyAsync(s, &h, sizeof h, cudaMemcpyHostToDevice, ctx->stream));
-    int st = launch_opt_step_begin(ctx, s, beta1, beta2, ctx->stream);
+    // Scalars for the explicit t in the context's slot (stream-ordered, so
+    // consecutive calls on the context stream do not overlap); no host wait.
+    RT_TRY(launch_opt_scalars_at(ctx, ctx->op_scalars, t, beta1, beta2, ctx->stream));
     OptTensor T{(float*)theta->ptr, (const float*)g->ptr, (float*)m->ptr, (float*)v->ptr, nullptr, 0, theta->ld,
                 theta->rows * theta->ld};
-    if (st == RT_OK) st = launch_adam(ctx, &T, 1, s, lr, beta1, beta2, eps, ctx->stream);
-    cudaFreeAsync(s, ctx->stream);
-    RT_CUDA(cudaStreamSynchronize(ctx->stream));  // h lives on this stack frame
-    return st;
+    return launch_adam(ctx, &T, 1, ctx->op_scalars, lr, beta1, beta2, eps, ctx->stream);
 }
 
 int rt_sgd(rt_ctx* ctx, rt_tensor* theta, const rt_tensor* g, float lr) {

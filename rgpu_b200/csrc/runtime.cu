@@ -73,13 +73,16 @@ int rt_ctx_create(int device, rt_ctx** out) {
     snprintf(c->name, sizeof c->name, "%s (sm_%d%d, %d SMs, %.1f GB)", prop.name, prop.major, prop.minor,
              prop.multiProcessorCount, prop.totalGlobalMem / 1e9);
     cudaError_t e1 = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking);
-    cudaError_t e2 = cudaMalloc(&c->dev_err, 4 * sizeof(int));
+    // one allocation: the device error word (16 bytes) and, 32 bytes in, the
+    // Adam scalars of op-level rt_adam calls
+    cudaError_t e2 = cudaMalloc(&c->dev_err, 64);
     if (e1 != cudaSuccess || e2 != cudaSuccess) {
         delete c;
         return fail(RT_ERR_CUDA, "context setup failed: %s", cudaGetErrorString(e1 != cudaSuccess ? e1 : e2));
     }
     c->stream = c->own_stream;
-    cudaMemsetAsync(c->dev_err, 0, 4 * sizeof(int), c->stream);
+    cudaMemsetAsync(c->dev_err, 0, 64, c->stream);
+    c->op_scalars = reinterpret_cast<rt::OptScalars*>(reinterpret_cast<char*>(c->dev_err) + 32);
     cudaStreamSynchronize(c->stream);
     const char* pair_env = getenv("RTGPU_PAIR_GEMM");
     c->pair_gemm = !(pair_env && pair_env[0] == '0');
