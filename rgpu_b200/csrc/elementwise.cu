@@ -42,6 +42,51 @@ __device__ __forceinline__ float warp_sum(float v) {
 // One warp per row (kernels.rs:146-166 uses one thread per row).  Loss is
 // -ln(max(p_y, 1e-12)) as losses.rs:104-111 computes it; delta is
 // (p - 1[j == y]) * scale (losses.rs:114, scale = g/n).
+//
+// Rows of up to 32 * VPL classes stay in registers: one read of the logits,
+// one exp per element, one write of delta (the generic form below reads a
+// row three times and takes each exp twice).  Both forms give the same bits.
+template <typename TD, int VPL>
+__global__ void xent_reg_kernel(const float* __restrict__ logits, int64_t ldz, const uint32_t* __restrict__ labels,
+                                int64_t n, int64_t C, float scale, TD* __restrict__ delta, int64_t ldd,
+                                float* __restrict__ loss) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+    if (r >= n) return;
+    const float* z = logits + r * ldz;
+    float v[VPL];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+        const int64_t j = lane + 32 * k;
+        v[k] = j < C ? __ldg(z + j) : -INFINITY;
+        mx = fmaxf(mx, v[k]);
+    }
+    mx = warp_max(mx);
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+        const int64_t j = lane + 32 * k;
+        if (j < C) {
+            v[k] = expf(v[k] - mx);
+            s += v[k];
+        }
+    }
+    s = warp_sum(s);
+    const uint32_t y = labels[r];
+    TD* d = delta + r * ldd;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+        const int64_t j = lane + 32 * k;
+        if (j < C) {
+            const float p = v[k] / s;
+            stf<TD>(d, j, (p - (j == (int64_t)y ? 1.0f : 0.0f)) * scale);
+            if (j == (int64_t)y) loss[r] = -logf(fmaxf(p, 1e-12f));
+        }
+    }
+    if (lane == 0 && (int64_t)y >= C) loss[r] = __int_as_float(0x7fc00000);  // label out of range: NaN loss
+}
+
 template <typename TD>
 __global__ void xent_kernel(const float* __restrict__ logits, int64_t ldz, const uint32_t* __restrict__ labels,
                             int64_t n, int64_t C, float scale, TD* __restrict__ delta, int64_t ldd,
@@ -291,12 +336,20 @@ int launch_xent(rt_ctx* ctx, const float* logits, int64_t ldz, const uint32_t* l
                 float scale, void* delta, rt_dtype ddt, int64_t ldd, float* loss_rows, cudaStream_t st) {
     if (n == 0) return RT_OK;
     unsigned blocks = (unsigned)((n + 7) / 8);
-    if (ddt == RT_BF16)
+    if (classes <= 32 * 32) {
+        if (ddt == RT_BF16)
+            xent_reg_kernel<__nv_bfloat16, 32><<<blocks, 256, 0, st>>>(logits, ldz, labels, n, classes, scale,
+                                                                        (__nv_bfloat16*)delta, ldd, loss_rows);
+        else
+            xent_reg_kernel<float, 32><<<blocks, 256, 0, st>>>(logits, ldz, labels, n, classes, scale, (float*)delta,
+                                                                ldd, loss_rows);
+    } else if (ddt == RT_BF16) {
         xent_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(logits, ldz, labels, n, classes, scale,
                                                             (__nv_bfloat16*)delta, ldd, loss_rows);
-    else
+    } else {
         xent_kernel<float><<<blocks, 256, 0, st>>>(logits, ldz, labels, n, classes, scale, (float*)delta, ldd,
                                                     loss_rows);
+    }
     count_launch(ctx);
     RT_CUDA(cudaGetLastError());
     return RT_OK;
