@@ -81,6 +81,14 @@ int comm_allreduce(rt_comm* comm, float* buf, int64_t count, cudaStream_t st) {
     return RT_OK;
 }
 
+int comm_allreduce_bf16(rt_comm* comm, __nv_bfloat16* buf, int64_t count, cudaStream_t st) {
+    if (!comm || count == 0) return RT_OK;
+    NcclApi& A = nccl_api();
+    ncclResult_t r = A.AllReduce(buf, buf, (size_t)count, ncclBfloat16, ncclSum, comm->nccl, st);
+    if (r != ncclSuccess) return fail(RT_ERR_NCCL, "ncclAllReduce (bf16) failed: %s", A.GetErrorString(r));
+    return RT_OK;
+}
+
 }  // namespace rt
 
 using namespace rt;

@@ -21,9 +21,11 @@
 //     optimiser update runs on a side stream once the dX GEMM, the last reader
 //     of W_l, is done (and, under data parallelism, the allreduce), so the
 //     update's HBM traffic overlaps the remaining backward GEMMs; the comm
-//     stream carries nothing but the allreduces.  The first layer's dW GEMM,
-//     the last GEMM of the step, runs in row chunks so that its allreduce and
-//     update trail it by one chunk only.
+//     stream carries the allreduces (and, when gradients are summed in bf16,
+//     their casts).  dW GEMMs run in row chunks: the first layer's always (it
+//     is the last GEMM of the step, so its update then trails it by one chunk
+//     only), every layer's under data parallelism (each chunk's allreduce
+//     starts while the next chunk computes).
 //   - two input slots: a host step copies the next batch on a copy stream
 //     while the previous step computes.
 #include <cstdlib>
@@ -35,6 +37,7 @@
 namespace rt {
 int run_gemm(rt_ctx* ctx, GemmDesc g, cudaStream_t stream, size_t ws_bytes);
 int comm_allreduce(rt_comm* comm, float* buf, int64_t count, cudaStream_t st);
+int comm_allreduce_bf16(rt_comm* comm, __nv_bfloat16* buf, int64_t count, cudaStream_t st);
 }  // namespace rt
 
 using namespace rt;
@@ -67,6 +70,12 @@ struct PlanLayer {
     int split_dw = 1;
     float* ws = nullptr;    // split-K partials for the dW GEMM
     size_t ws_bytes = 0;
+    __nv_bfloat16* g16 = nullptr;  // bf16 copy of g for a bf16 gradient allreduce
+    // The dW GEMM in `chunks` row chunks of [dW; db], each with its events:
+    // computed (ready), allreduced (comm), updated (opt); dx: the dX GEMM done.
+    int chunks = 1;
+    std::vector<cudaEvent_t> ev_ready, ev_comm, ev_opt;
+    cudaEvent_t ev_dx = nullptr;
 };
 
 struct Slot {
@@ -114,13 +123,9 @@ struct rt_mlp {
     rt_comm* comm = nullptr;
     int comm_sm_reserve = 0;  // SMs the backward GEMMs leave to NCCL while gradients are reduced
     cudaStream_t comm_stream = nullptr;
-    std::vector<cudaEvent_t> comm_ready, comm_done;
+    bool comm_bf16 = false;  // allreduce the gradients in bf16 (bf16 plans, RTGPU_GRAD_COMM=bf16)
     // per-layer optimiser on a side stream, overlapping the remaining backward GEMMs
     cudaStream_t opt_stream = nullptr;
-    std::vector<cudaEvent_t> grad_ready, opt_done;
-    // the first layer's dW GEMM in row chunks (1 = whole), with their events
-    int chunks0 = 1;
-    std::vector<cudaEvent_t> chunk_ready, chunk_comm_done, chunk_opt_done;
 };
 
 namespace {
@@ -159,13 +164,12 @@ void free_all(rt_mlp* m) {
         if (s.stage) cudaFree(s.stage);
     }
     for (auto e : m->events) cudaEventDestroy(e);
-    for (auto e : m->comm_ready) cudaEventDestroy(e);
-    for (auto e : m->comm_done) cudaEventDestroy(e);
-    for (auto e : m->grad_ready) cudaEventDestroy(e);
-    for (auto e : m->opt_done) cudaEventDestroy(e);
-    for (auto e : m->chunk_ready) cudaEventDestroy(e);
-    for (auto e : m->chunk_comm_done) cudaEventDestroy(e);
-    for (auto e : m->chunk_opt_done) cudaEventDestroy(e);
+    for (auto& P : m->L) {
+        for (auto e : P.ev_ready) cudaEventDestroy(e);
+        for (auto e : P.ev_comm) cudaEventDestroy(e);
+        for (auto e : P.ev_opt) cudaEventDestroy(e);
+        if (P.ev_dx) cudaEventDestroy(P.ev_dx);
+    }
     if (m->comm_stream) cudaStreamDestroy(m->comm_stream);
     if (m->opt_stream) cudaStreamDestroy(m->opt_stream);
     if (m->copy_stream) cudaStreamDestroy(m->copy_stream);
@@ -209,7 +213,7 @@ struct Enqueuer {
     }
 
     const void* input_of(int l) const { return l == 0 ? m->slot[s].x : m->L[l - 1].act; }
-    int64_t chunk_row(int64_t rows, int c) const { return chunk_row_of(rows, m->chunks0, c); }
+
     int64_t ld_in(int l) const { return l == 0 ? m->ldx : m->L[l - 1].ld_act; }
     int backward_sms() const {
         return m->comm && m->comm_sm_reserve > 0 ? m->ctx->sm_count - m->comm_sm_reserve : 0;
@@ -247,55 +251,53 @@ struct Enqueuer {
         return RT_OK;
     }
 
-    // The first layer has no dX GEMM, so nothing reads W_0 after its dW GEMM,
-    // and that GEMM is the last of the step: its update (and, under data
-    // parallelism, its allreduce) would trail every GEMM.  The GEMM is cut
-    // into row chunks of [dW_0; db_0] instead (contiguous rows of the
-    // parameter block); each chunk's allreduce and update start on the side
-    // streams while the next chunk computes, so only the last chunk's trail.
-    int first_layer_chunked(PlanLayer& P) {
-        const bool update = m->cfg.optimizer != RT_OPT_NONE;
+    // [dW_l; db_l] rows [r0, r1) = ([A_{l-1}, 1] columns r0..r1)^T delta_l (TN, K = batch), f32.
+    int dw_gemm_rows(PlanLayer& P, int l, int64_t r0, int64_t r1) {
         const int64_t rows = P.d + 1;
-        for (int c = 0; c < m->chunks0; ++c) {
-            const int64_t r0 = chunk_row(rows, c), r1 = chunk_row(rows, c + 1);
-            GemmDesc g{};
-            g.layout = RT_TN;
-            g.in_dtype = m->adt;
-            g.out_dtype = RT_F32;
-            g.m = r1 - r0;
-            g.n = P.u;
-            g.k = m->n;
-            g.a = static_cast<const uint8_t*>(input_of(0)) + r0 * dtype_size(m->adt);  // A columns r0..r1
-            g.lda = ld_in(0);
-            g.b = P.delta;
-            g.ldb = P.ld;
-            g.c = P.g + r0 * P.ld;
-            g.ldc = P.ld;
-            g.epi = RT_EPI_NONE;
-            g.split_k = P.split_dw;
-            g.workspace = P.ws;
-            g.max_sms = backward_sms();
-            g.x3_ws = m->x3_ws;
-            g.x3_ws_bytes = m->x3_ws_bytes;
-            RT_TRY(run_gemm(m->ctx, g, st, P.ws_bytes));
-            // FLOPs of the weight rows (the bias row is not counted, as everywhere)
-            RT_TRY(mark("dw_gemm", 2.0 * m->n * (double)(r1 - r0 - (r1 == rows ? 1 : 0)) * P.u));
-            RT_CUDA(cudaEventRecord(m->chunk_ready[c], st));
-            if (m->comm) {
-                RT_CUDA(cudaStreamWaitEvent(m->comm_stream, m->chunk_ready[c], 0));
-                RT_TRY(comm_allreduce(m->comm, P.g + r0 * P.ld, (r1 - r0) * P.ld, m->comm_stream));
-                RT_CUDA(cudaEventRecord(m->chunk_comm_done[c], m->comm_stream));
-            }
-            if (update) {
-                RT_CUDA(cudaStreamWaitEvent(m->opt_stream, m->chunk_ready[c], 0));
-                if (m->comm) RT_CUDA(cudaStreamWaitEvent(m->opt_stream, m->chunk_comm_done[c], 0));
-                RT_TRY(enqueue_update_rows(m, P, r0, r1, m->opt_stream));
-                RT_CUDA(cudaEventRecord(m->chunk_opt_done[c], m->opt_stream));
-            }
-        }
-        return RT_OK;
+        GemmDesc g{};
+        g.layout = RT_TN;
+        g.in_dtype = m->adt;
+        g.out_dtype = RT_F32;
+        g.m = r1 - r0;
+        g.n = P.u;
+        g.k = m->n;
+        g.a = static_cast<const uint8_t*>(input_of(l)) + r0 * dtype_size(m->adt);  // A columns r0..r1
+        g.lda = ld_in(l);
+        g.b = P.delta;
+        g.ldb = P.ld;
+        g.c = P.g + r0 * P.ld;
+        g.ldc = P.ld;
+        g.epi = RT_EPI_NONE;
+        g.split_k = P.split_dw;
+        g.workspace = P.ws;
+        g.max_sms = backward_sms();
+        g.x3_ws = m->x3_ws;
+        g.x3_ws_bytes = m->x3_ws_bytes;
+        RT_TRY(run_gemm(m->ctx, g, st, P.ws_bytes));
+        // FLOPs of the weight rows (the bias row is not counted, as everywhere)
+        return mark("dw_gemm", 2.0 * m->n * (double)(r1 - r0 - (r1 == rows ? 1 : 0)) * P.u);
     }
 
+    // Sums gradient rows [r0, r1) over the ranks on the comm stream (in bf16 when
+    // the plan reduces in bf16: cast, allreduce, cast back into g).
+    int allreduce_rows(PlanLayer& P, int64_t r0, int64_t r1) {
+        cudaStream_t cs = m->comm_stream;
+        const int64_t count = (r1 - r0) * P.ld;
+        if (!m->comm_bf16) return comm_allreduce(m->comm, P.g + r0 * P.ld, count, cs);
+        __nv_bfloat16* h = P.g16 + r0 * P.ld;
+        RT_TRY(launch_cast(m->ctx, P.g + r0 * P.ld, RT_F32, P.ld, h, RT_BF16, P.ld, r1 - r0, P.ld, cs));
+        RT_TRY(comm_allreduce_bf16(m->comm, h, count, cs));
+        return launch_cast(m->ctx, h, RT_BF16, P.ld, P.g + r0 * P.ld, RT_F32, P.ld, r1 - r0, P.ld, cs);
+    }
+
+    // Backward and update.  Per layer, top down: the dW GEMM (in row chunks of
+    // [dW; db], contiguous rows of the parameter block), each chunk handed to
+    // the comm stream for its allreduce as soon as it is computed; then the dX
+    // GEMM, the last reader of W_l in the step; then, on the optimiser stream,
+    // each chunk's update once dX is done and the chunk is reduced.  The first
+    // layer has no dX GEMM, so its chunk updates follow the chunk GEMMs
+    // directly: its dW GEMM is the last GEMM of the step, and chunking it keeps
+    // the trailing update (and allreduce) to one chunk.
     int backward_and_update() {
         const int nl = (int)m->L.size();
         const bool update = m->cfg.optimizer != RT_OPT_NONE;
@@ -310,43 +312,25 @@ struct Enqueuer {
         RT_TRY(mark("softmax_xent", 0));
         for (int l = nl - 1; l >= 0; --l) {
             PlanLayer& P = m->L[l];
-            if (l == 0 && m->chunks0 > 1) {
-                RT_TRY(first_layer_chunked(P));
-                continue;
-            }
-            // [dW_l; db_l] = [A_{l-1}, 1]^T delta_l  (TN, K = batch, M = d + 1), f32 gradient.
-            // It runs before the dX GEMM so that the layer's allreduce starts as early as possible.
-            GemmDesc g{};
-            g.layout = RT_TN;
-            g.in_dtype = m->adt;
-            g.out_dtype = RT_F32;
-            g.m = P.d + 1;
-            g.n = P.u;
-            g.k = m->n;
-            g.a = input_of(l);
-            g.lda = ld_in(l);
-            g.b = P.delta;
-            g.ldb = P.ld;
-            g.c = P.g;
-            g.ldc = P.ld;
-            g.epi = RT_EPI_NONE;
-            g.split_k = P.split_dw;
-            g.workspace = P.ws;
-            g.max_sms = backward_sms();
-            g.x3_ws = m->x3_ws;
-            g.x3_ws_bytes = m->x3_ws_bytes;
-            RT_TRY(run_gemm(m->ctx, g, st, P.ws_bytes));
-            RT_TRY(mark("dw_gemm", 2.0 * m->n * P.d * P.u));
-            if (m->comm) {
-                // the comm stream carries only the allreduces, back to back
-                RT_CUDA(cudaEventRecord(m->comm_ready[l], st));
-                RT_CUDA(cudaStreamWaitEvent(m->comm_stream, m->comm_ready[l], 0));
-                RT_TRY(comm_allreduce(m->comm, P.g, (P.d + 1) * P.ld, m->comm_stream));
-                RT_CUDA(cudaEventRecord(m->comm_done[l], m->comm_stream));
+            const int64_t rows = P.d + 1;
+            for (int c = 0; c < P.chunks; ++c) {
+                const int64_t r0 = chunk_row_of(rows, P.chunks, c), r1 = chunk_row_of(rows, P.chunks, c + 1);
+                RT_TRY(dw_gemm_rows(P, l, r0, r1));
+                RT_CUDA(cudaEventRecord(P.ev_ready[c], st));
+                if (m->comm) {
+                    RT_CUDA(cudaStreamWaitEvent(m->comm_stream, P.ev_ready[c], 0));
+                    RT_TRY(allreduce_rows(P, r0, r1));
+                    RT_CUDA(cudaEventRecord(P.ev_comm[c], m->comm_stream));
+                }
+                if (update && l == 0) {
+                    RT_CUDA(cudaStreamWaitEvent(m->opt_stream, P.ev_ready[c], 0));
+                    if (m->comm) RT_CUDA(cudaStreamWaitEvent(m->opt_stream, P.ev_comm[c], 0));
+                    RT_TRY(enqueue_update_rows(m, P, r0, r1, m->opt_stream));
+                    RT_CUDA(cudaEventRecord(P.ev_opt[c], m->opt_stream));
+                }
             }
             if (l > 0) {
-                // delta_{l-1} = (delta_l W_l^T) * 1[A_{l-1} > 0]  (NT, fused mask): the last
-                // reader of W_l in the step.
+                // delta_{l-1} = (delta_l W_l^T) * 1[A_{l-1} > 0]  (NT, fused mask)
                 PlanLayer& Q = m->L[l - 1];
                 GemmDesc h{};
                 h.layout = RT_NT;
@@ -370,35 +354,65 @@ struct Enqueuer {
                 h.x3_ws_bytes = m->x3_ws_bytes;
                 RT_TRY(run_gemm(m->ctx, h, st, 0));
                 RT_TRY(mark("dx_gemm_relu_mask", 2.0 * m->n * P.d * P.u));
-            }
-            if (update) {
-                // W_l's update waits for its last reader (this dX GEMM) and, under data
-                // parallelism, for its allreduce
-                RT_CUDA(cudaEventRecord(m->grad_ready[l], st));
-                RT_CUDA(cudaStreamWaitEvent(m->opt_stream, m->grad_ready[l], 0));
-                if (m->comm) RT_CUDA(cudaStreamWaitEvent(m->opt_stream, m->comm_done[l], 0));
-                RT_TRY(enqueue_update_rows(m, P, 0, P.d + 1, m->opt_stream));
-                RT_CUDA(cudaEventRecord(m->opt_done[l], m->opt_stream));
-            }
-        }
-        for (int l = 0; l < nl; ++l) {
-            if (l == 0 && m->chunks0 > 1) {
-                for (int c = 0; c < m->chunks0; ++c) {
-                    if (update)
-                        RT_CUDA(cudaStreamWaitEvent(st, m->chunk_opt_done[c], 0));
-                    else if (m->comm)
-                        RT_CUDA(cudaStreamWaitEvent(st, m->chunk_comm_done[c], 0));
+                if (update) {
+                    RT_CUDA(cudaEventRecord(P.ev_dx, st));
+                    RT_CUDA(cudaStreamWaitEvent(m->opt_stream, P.ev_dx, 0));
+                    for (int c = 0; c < P.chunks; ++c) {
+                        const int64_t r0 = chunk_row_of(rows, P.chunks, c), r1 = chunk_row_of(rows, P.chunks, c + 1);
+                        if (m->comm) RT_CUDA(cudaStreamWaitEvent(m->opt_stream, P.ev_comm[c], 0));
+                        RT_TRY(enqueue_update_rows(m, P, r0, r1, m->opt_stream));
+                        RT_CUDA(cudaEventRecord(P.ev_opt[c], m->opt_stream));
+                    }
                 }
-            } else if (update) {
-                RT_CUDA(cudaStreamWaitEvent(st, m->opt_done[l], 0));
-            } else if (m->comm) {
-                RT_CUDA(cudaStreamWaitEvent(st, m->comm_done[l], 0));
             }
         }
+        for (PlanLayer& P : m->L)
+            for (int c = 0; c < P.chunks; ++c) {
+                if (update)
+                    RT_CUDA(cudaStreamWaitEvent(st, P.ev_opt[c], 0));
+                else if (m->comm)
+                    RT_CUDA(cudaStreamWaitEvent(st, P.ev_comm[c], 0));
+            }
         if (update) RT_TRY(mark(m->cfg.optimizer == RT_OPT_ADAM ? "adam_tail" : "sgd_tail", 0));
         return RT_OK;
     }
 };
+
+// Chunks of each layer's dW GEMM: the first layer always (its update would
+// otherwise trail the step), every layer under data parallelism (its
+// allreduce starts a chunk after the GEMM does); 4 chunks for >= 4096 rows,
+// 2 for >= 2048.  RTGPU_FIRST_LAYER_CHUNKS / RTGPU_DW_CHUNKS override.
+int prepare_chunks(rt_mlp* m) {
+    auto rule = [](int64_t rows) { return rows >= 4096 ? 4 : rows >= 2048 ? 2 : 1; };
+    const char* env0 = getenv("RTGPU_FIRST_LAYER_CHUNKS");
+    const char* envd = getenv("RTGPU_DW_CHUNKS");
+    for (size_t l = 0; l < m->L.size(); ++l) {
+        PlanLayer& P = m->L[l];
+        const int64_t rows = P.d + 1;
+        int ch = 1;
+        if (l == 0) ch = env0 && env0[0] ? atoi(env0) : rule(rows);
+        else if (m->comm) ch = envd && envd[0] ? atoi(envd) : rule(rows);
+        if (ch < 1) ch = 1;
+        if (ch > 8) ch = 8;
+        while (ch > 1 && chunk_row_of(rows, ch, 1) == 0) --ch;  // every chunk non-empty
+        if (ch == P.chunks && !P.ev_ready.empty()) continue;
+        for (auto e : P.ev_ready) cudaEventDestroy(e);
+        for (auto e : P.ev_comm) cudaEventDestroy(e);
+        for (auto e : P.ev_opt) cudaEventDestroy(e);
+        P.chunks = ch;
+        P.ev_ready.assign(ch, nullptr);
+        P.ev_comm.assign(ch, nullptr);
+        P.ev_opt.assign(ch, nullptr);
+        for (int c = 0; c < ch; ++c)
+            if (cudaEventCreateWithFlags(&P.ev_ready[c], cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&P.ev_comm[c], cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&P.ev_opt[c], cudaEventDisableTiming) != cudaSuccess)
+                return fail(RT_ERR_CUDA, "event creation failed");
+        if (!P.ev_dx && cudaEventCreateWithFlags(&P.ev_dx, cudaEventDisableTiming) != cudaSuccess)
+            return fail(RT_ERR_CUDA, "event creation failed");
+    }
+    return RT_OK;
+}
 
 int capture_step(rt_mlp* m, int s) {
     cudaStream_t st = m->ctx->stream;
@@ -534,31 +548,6 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
     if (cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaStreamCreateWithFlags(&m->opt_stream, cudaStreamNonBlocking) != cudaSuccess)
         return bail(fail(RT_ERR_CUDA, "stream creation failed"));
-    m->grad_ready.resize(nl);
-    m->opt_done.resize(nl);
-    for (int l = 0; l < nl; ++l)
-        if (cudaEventCreateWithFlags(&m->grad_ready[l], cudaEventDisableTiming) != cudaSuccess ||
-            cudaEventCreateWithFlags(&m->opt_done[l], cudaEventDisableTiming) != cudaSuccess)
-            return bail(fail(RT_ERR_CUDA, "event creation failed"));
-    {
-        // first-layer dW chunks: 4 for >= 4096 rows, 2 for >= 2048 (see first_layer_chunked)
-        const int64_t rows0 = m->dims[0] + 1;
-        const char* env = getenv("RTGPU_FIRST_LAYER_CHUNKS");
-        int ch = rows0 >= 4096 ? 4 : rows0 >= 2048 ? 2 : 1;
-        if (env && env[0]) ch = atoi(env);
-        if (ch < 1) ch = 1;
-        if (ch > 8) ch = 8;
-        while (ch > 1 && chunk_row_of(rows0, ch, 1) == 0) --ch;  // every chunk non-empty
-        m->chunks0 = ch;
-        m->chunk_ready.resize(ch);
-        m->chunk_comm_done.resize(ch);
-        m->chunk_opt_done.resize(ch);
-        for (int c = 0; c < ch; ++c)
-            if (cudaEventCreateWithFlags(&m->chunk_ready[c], cudaEventDisableTiming) != cudaSuccess ||
-                cudaEventCreateWithFlags(&m->chunk_comm_done[c], cudaEventDisableTiming) != cudaSuccess ||
-                cudaEventCreateWithFlags(&m->chunk_opt_done[c], cudaEventDisableTiming) != cudaSuccess)
-                return bail(fail(RT_ERR_CUDA, "event creation failed"));
-    }
     if ((s = dalloc_t(m, &m->loss_rows, (size_t)m->n))) return bail(s);
     if ((s = dalloc_t(m, &m->opt, 1))) return bail(s);
     m->L.resize(nl);
@@ -620,6 +609,7 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
         if ((s = dalloc(m, (void**)&m->x3_ws, need))) return bail(s);
         m->x3_ws_bytes = need;
     }
+    if ((s = prepare_chunks(m))) return bail(s);
     if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) return bail(fail(RT_ERR_CUDA, "plan setup sync failed"));
     *out = m;
     return RT_OK;
@@ -872,13 +862,19 @@ int rt_mlp_set_comm(rt_mlp* m, rt_comm* comm) {
     const char* r = getenv("RTGPU_COMM_SM_RESERVE");
     m->comm_sm_reserve = r ? (atoi(r) + 1) / 2 * 2 : 16;
     if (m->comm_sm_reserve < 0 || m->comm_sm_reserve >= m->ctx->sm_count) m->comm_sm_reserve = 0;
-    if (comm && !m->comm_stream) {
-        RT_CUDA(cudaStreamCreateWithFlags(&m->comm_stream, cudaStreamNonBlocking));
-        m->comm_ready.resize(m->L.size());
-        m->comm_done.resize(m->L.size());
-        for (auto& e : m->comm_ready) RT_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-        for (auto& e : m->comm_done) RT_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-    }
+    if (comm && !m->comm_stream) RT_CUDA(cudaStreamCreateWithFlags(&m->comm_stream, cudaStreamNonBlocking));
+    // RTGPU_GRAD_COMM=bf16: bf16 plans sum their gradients in bf16 (half the
+    // NVLink bytes; the parity bar of bf16 plans is 2e-2)
+    const char* gc = getenv("RTGPU_GRAD_COMM");
+    m->comm_bf16 = comm && m->adt == RT_BF16 && gc && std::strcmp(gc, "bf16") == 0;
+    if (m->comm_bf16)
+        for (PlanLayer& P : m->L)
+            if (!P.g16) {
+                void* p = nullptr;
+                RT_TRY(dalloc(m, &p, (size_t)(P.d + 1) * P.ld * 2));
+                P.g16 = static_cast<__nv_bfloat16*>(p);
+            }
+    RT_TRY(prepare_chunks(m));
     m->ops.clear();
     drop_graphs(m);
     return RT_OK;

@@ -38,7 +38,8 @@ def main():
     # 1025 rows of [W_0; b_0]: the plan can cut the first layer's dW GEMM into
     # 4 chunks on 256-row edges (RTGPU_FIRST_LAYER_CHUNKS=4 below), whose
     # allreduces and updates then run per chunk
-    dims = [1024, 256, 192, 10]
+    # (and 513 rows of layer 1: 2 chunks under RTGPU_DW_CHUNKS=2)
+    dims = [1024, 512, 192, 10]
     params = []
     for l in range(len(dims) - 1):
         lim = np.sqrt(6.0 / dims[l])
@@ -50,8 +51,12 @@ def main():
     per = n_global // world
     xs, ls = x[rank * per:(rank + 1) * per], labels[rank * per:(rank + 1) * per]
     result = {}
-    for dtype, chunks in (("f32", "1"), ("bf16", "1"), ("f32_chunked", "4")):
+    cases = (("f32", "1", "1", "f32"), ("bf16", "1", "1", "f32"), ("f32_chunked", "4", "2", "f32"),
+             ("bf16_gradcomm", "4", "2", "bf16"))
+    for dtype, chunks, dw_chunks, grad_comm in cases:
         os.environ["RTGPU_FIRST_LAYER_CHUNKS"] = chunks
+        os.environ["RTGPU_DW_CHUNKS"] = dw_chunks
+        os.environ["RTGPU_GRAD_COMM"] = grad_comm
         dtype_name = dtype
         dtype = dtype.split("_")[0]
         mlp = rgpu_b200.GpuMlp.from_params(gpu, params, per, 0.0, dtype=dtype, optimizer="none",
@@ -67,8 +72,10 @@ def main():
             ref.close()
             result[dtype_name] = [float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
                                   for a, b in zip(g_dp, g_ref)]
-    # Adam with the chunked first layer: replicas stay bit-identical.
+    # Adam with chunked dW GEMMs and bf16 gradient sums: replicas stay bit-identical.
     os.environ["RTGPU_FIRST_LAYER_CHUNKS"] = "4"
+    os.environ["RTGPU_DW_CHUNKS"] = "2"
+    os.environ["RTGPU_GRAD_COMM"] = "bf16"
     mlp = rgpu_b200.GpuMlp.from_params(gpu, params, per, 1e-3, dtype="bf16", optimizer="adam", global_batch=n_global)
     mlp.set_comm(comm)
     gx, gl = gpu.upload(xs), rgpu_b200.upload_labels(gpu, ls)

@@ -27,5 +27,6 @@ def test_two_rank_dp_equals_single_gpu(tmp_path):
     res = json.load(open(out))
     assert max(res["f32"]) <= 1e-5, res["f32"]
     assert max(res["f32_chunked"]) <= 1e-5, res["f32_chunked"]
+    assert max(res["bf16_gradcomm"]) <= 2e-2, res["bf16_gradcomm"]
     assert max(res["bf16"]) <= 2e-2, res["bf16"]
     assert res["replicas_identical"]
