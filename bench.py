@@ -553,7 +553,7 @@ def main():
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": cfg["dtype"],
             "data": "synthetic (seeded N(0,1) inputs, uniform labels, Kaiming-uniform weights)",
-            "config": config_dict(args.config, cfg, world, global_batch),
+            "config": dict(config_dict(args.config, cfg, world, global_batch), grad_sync=mlp.comm_mode()),
             "roofline": roof,
             "ms_per_step_with_kernel_events": ms_events / args.steps,
             "step_tensor_frac": {"achieved_tflops": step_tflops, "peak": pk["bf16"], "frac": step_tflops / pk["bf16"],

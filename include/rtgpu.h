@@ -276,9 +276,19 @@ int rt_mlp_dispatches_per_step(rt_mlp* mlp, int* out);
 int rt_mlp_enable_timing(rt_mlp* mlp, int on);
 int rt_mlp_op_count(rt_mlp* mlp, int* count);
 int rt_mlp_op_time(rt_mlp* mlp, int i, const char** label, double* flops, float* ms);
-/* Attach a communicator: dW/db are summed over ranks with ncclAllReduce on a
- * second stream, layer by layer as backward produces them. */
+/* Attach a communicator: dW/db are summed over ranks on a second stream,
+ * chunk by chunk as backward produces them.  f32 plans, plans without an
+ * optimiser and RTGPU_GRAD_COMM=bf16 allreduce the gradients.  bf16 plans with
+ * SGD or Adam shard the optimiser (ZeRO stage 1; RTGPU_SHARDED_OPT=0 turns it
+ * off): each chunk's weight-row gradients are reduce-scattered, every rank
+ * updates its 1/world slice of the f32 masters and moments, and the bf16
+ * weights the GEMMs read are all-gathered; bias rows stay replicated.  On a
+ * sharded plan rt_mlp_weights, rt_mlp_grads and rt_mlp_save_state first
+ * all-gather the f32 state, so every rank must call them together. */
 int rt_mlp_set_comm(rt_mlp* mlp, rt_comm* comm);
+/* How the attached communicator sums gradients (rt_comm_mode). */
+typedef enum { RT_COMM_NONE = 0, RT_COMM_ALLREDUCE = 1, RT_COMM_ALLREDUCE_BF16 = 2, RT_COMM_SHARDED_OPT = 3 } rt_comm_mode;
+int rt_mlp_comm_mode(rt_mlp* mlp, int* mode);
 
 /* ------------------------------------------------------ autodiff tape */
 /* Reverse-mode tape on the GPU for the ops a Dense network is made of.  All

@@ -27,6 +27,9 @@ struct NcclApi {
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
     ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t) = nullptr;
+    ncclResult_t (*ReduceScatter)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                                  cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     const char* (*GetErrorString)(ncclResult_t) = nullptr;
 };
 
@@ -47,8 +50,11 @@ NcclApi& nccl_api() {
         api.CommInitRank = (decltype(api.CommInitRank))dlsym(h, "ncclCommInitRank");
         api.CommDestroy = (decltype(api.CommDestroy))dlsym(h, "ncclCommDestroy");
         api.AllReduce = (decltype(api.AllReduce))dlsym(h, "ncclAllReduce");
+        api.ReduceScatter = (decltype(api.ReduceScatter))dlsym(h, "ncclReduceScatter");
+        api.AllGather = (decltype(api.AllGather))dlsym(h, "ncclAllGather");
         api.GetErrorString = (decltype(api.GetErrorString))dlsym(h, "ncclGetErrorString");
-        if (!api.GetUniqueId || !api.CommInitRank || !api.CommDestroy || !api.AllReduce || !api.GetErrorString) {
+        if (!api.GetUniqueId || !api.CommInitRank || !api.CommDestroy || !api.AllReduce || !api.ReduceScatter ||
+            !api.AllGather || !api.GetErrorString) {
             api.error = "libnccl.so.2 lacks a required symbol";
             return;
         }
@@ -78,6 +84,32 @@ int comm_allreduce(rt_comm* comm, float* buf, int64_t count, cudaStream_t st) {
     NcclApi& A = nccl_api();
     ncclResult_t r = A.AllReduce(buf, buf, (size_t)count, ncclFloat32, ncclSum, comm->nccl, st);
     if (r != ncclSuccess) return fail(RT_ERR_NCCL, "ncclAllReduce failed: %s", A.GetErrorString(r));
+    return RT_OK;
+}
+
+int comm_rank(const rt_comm* comm) { return comm ? comm->rank : 0; }
+int comm_world(const rt_comm* comm) { return comm ? comm->world : 1; }
+
+// In place: buf holds world * count elements; rank r's slice
+// [r * count, (r + 1) * count) receives the sum of that slice over the ranks.
+int comm_reduce_scatter(rt_comm* comm, float* buf, int64_t count, cudaStream_t st) {
+    if (!comm || count == 0) return RT_OK;
+    NcclApi& A = nccl_api();
+    ncclResult_t r = A.ReduceScatter(buf, buf + (int64_t)comm->rank * count, (size_t)count, ncclFloat32, ncclSum,
+                                     comm->nccl, st);
+    if (r != ncclSuccess) return fail(RT_ERR_NCCL, "ncclReduceScatter failed: %s", A.GetErrorString(r));
+    return RT_OK;
+}
+
+// In place: rank r's slice [r * count, (r + 1) * count) of buf is copied to
+// the same slice of every rank's buf (elem_bytes 2 for bf16, 4 for f32).
+int comm_all_gather(rt_comm* comm, void* buf, int64_t count, int elem_bytes, cudaStream_t st) {
+    if (!comm || count == 0) return RT_OK;
+    NcclApi& A = nccl_api();
+    char* b = static_cast<char*>(buf);
+    ncclResult_t r = A.AllGather(b + (int64_t)comm->rank * count * elem_bytes, b, (size_t)count,
+                                 elem_bytes == 2 ? ncclBfloat16 : ncclFloat32, comm->nccl, st);
+    if (r != ncclSuccess) return fail(RT_ERR_NCCL, "ncclAllGather failed: %s", A.GetErrorString(r));
     return RT_OK;
 }
 

@@ -38,6 +38,10 @@ namespace rt {
 int run_gemm(rt_ctx* ctx, GemmDesc g, cudaStream_t stream, size_t ws_bytes);
 int comm_allreduce(rt_comm* comm, float* buf, int64_t count, cudaStream_t st);
 int comm_allreduce_bf16(rt_comm* comm, __nv_bfloat16* buf, int64_t count, cudaStream_t st);
+int comm_reduce_scatter(rt_comm* comm, float* buf, int64_t count, cudaStream_t st);
+int comm_all_gather(rt_comm* comm, void* buf, int64_t count, int elem_bytes, cudaStream_t st);
+int comm_rank(const rt_comm* comm);
+int comm_world(const rt_comm* comm);
 }  // namespace rt
 
 using namespace rt;
@@ -74,7 +78,7 @@ struct PlanLayer {
     // The dW GEMM in `chunks` row chunks of [dW; db], each with its events:
     // computed (ready), allreduced (comm), updated (opt); dx: the dX GEMM done.
     int chunks = 1;
-    std::vector<cudaEvent_t> ev_ready, ev_comm, ev_opt;
+    std::vector<cudaEvent_t> ev_ready, ev_comm, ev_opt, ev_ag;
     cudaEvent_t ev_dx = nullptr;
 };
 
@@ -124,6 +128,14 @@ struct rt_mlp {
     int comm_sm_reserve = 0;  // SMs the backward GEMMs leave to NCCL while gradients are reduced
     cudaStream_t comm_stream = nullptr;
     bool comm_bf16 = false;  // allreduce the gradients in bf16 (bf16 plans, RTGPU_GRAD_COMM=bf16)
+    // Sharded optimiser (bf16 plans with an optimiser under data parallelism):
+    // each gradient chunk is reduce-scattered, every rank updates its 1/world
+    // slice of the f32 masters and moments, and the bf16 weights are
+    // all-gathered; the f32 masters, moments and reduced gradients outside a
+    // rank's slices are gathered only when read (rt_mlp_weights / grads /
+    // save_state, then collective).
+    bool sharded = false;
+    int rank = 0, world = 1;
     // per-layer optimiser on a side stream, overlapping the remaining backward GEMMs
     cudaStream_t opt_stream = nullptr;
 };
@@ -168,6 +180,7 @@ void free_all(rt_mlp* m) {
         for (auto e : P.ev_ready) cudaEventDestroy(e);
         for (auto e : P.ev_comm) cudaEventDestroy(e);
         for (auto e : P.ev_opt) cudaEventDestroy(e);
+        for (auto e : P.ev_ag) cudaEventDestroy(e);
         if (P.ev_dx) cudaEventDestroy(P.ev_dx);
     }
     if (m->comm_stream) cudaStreamDestroy(m->comm_stream);
@@ -177,15 +190,32 @@ void free_all(rt_mlp* m) {
     m->allocs.clear();
 }
 
-// Enqueues the optimiser update of rows [r0, r1) of layer P's [d+1, ld]
-// parameter block on st.
-int enqueue_update_rows(rt_mlp* m, PlanLayer& P, int64_t r0, int64_t r1, cudaStream_t st) {
-    const int64_t o = r0 * P.ld;
+// Enqueues the optimiser update of the flat elements [o, o + n) of layer P's
+// [d+1, ld] parameter block on st.
+int enqueue_update_flat(rt_mlp* m, PlanLayer& P, int64_t o, int64_t n, cudaStream_t st) {
     OptTensor t{P.w32 + o, P.g + o, P.m ? P.m + o : nullptr, P.v ? P.v + o : nullptr, P.w16 ? P.w16 + o : nullptr,
-                P.ld, P.ld, (r1 - r0) * P.ld};
+                P.ld, P.ld, n};
     if (m->cfg.optimizer == RT_OPT_ADAM)
         return launch_adam(m->ctx, &t, 1, m->opt, m->cfg.lr, m->cfg.beta1, m->cfg.beta2, m->cfg.eps, st);
     if (m->cfg.optimizer == RT_OPT_SGD) return launch_sgd(m->ctx, &t, 1, m->cfg.lr, st);
+    return RT_OK;
+}
+
+// Under the sharded optimiser the weight rows [r0, min(r1, d)) of a chunk are
+// split into world equal flat slices; the bias row d, which the forward
+// epilogue reads in f32, stays replicated (allreduced, updated on every rank).
+int64_t shard_end(const PlanLayer& P, int64_t r1) { return r1 < P.d ? r1 : P.d; }
+
+// Rows [r0, r1) of the parameter block: the whole range, or under the sharded
+// optimiser this rank's slice of the weight rows plus the bias row.
+int enqueue_update_rows(rt_mlp* m, PlanLayer& P, int64_t r0, int64_t r1, cudaStream_t st) {
+    if (!m->sharded) return enqueue_update_flat(m, P, r0 * P.ld, (r1 - r0) * P.ld, st);
+    const int64_t e = shard_end(P, r1);
+    if (e > r0) {
+        const int64_t piece = (e - r0) * P.ld / m->world;
+        RT_TRY(enqueue_update_flat(m, P, r0 * P.ld + (int64_t)m->rank * piece, piece, st));
+    }
+    if (r1 > P.d) RT_TRY(enqueue_update_flat(m, P, P.d * P.ld, P.ld, st));
     return RT_OK;
 }
 
@@ -283,11 +313,28 @@ struct Enqueuer {
     int allreduce_rows(PlanLayer& P, int64_t r0, int64_t r1) {
         cudaStream_t cs = m->comm_stream;
         const int64_t count = (r1 - r0) * P.ld;
+        if (m->sharded) {
+            const int64_t e = shard_end(P, r1);
+            if (e > r0) RT_TRY(comm_reduce_scatter(m->comm, P.g + r0 * P.ld, (e - r0) * P.ld / m->world, cs));
+            if (r1 > P.d) RT_TRY(comm_allreduce(m->comm, P.db, P.ld, cs));
+            return RT_OK;
+        }
         if (!m->comm_bf16) return comm_allreduce(m->comm, P.g + r0 * P.ld, count, cs);
         __nv_bfloat16* h = P.g16 + r0 * P.ld;
         RT_TRY(launch_cast(m->ctx, P.g + r0 * P.ld, RT_F32, P.ld, h, RT_BF16, P.ld, r1 - r0, P.ld, cs));
         RT_TRY(comm_allreduce_bf16(m->comm, h, count, cs));
         return launch_cast(m->ctx, h, RT_BF16, P.ld, P.g + r0 * P.ld, RT_F32, P.ld, r1 - r0, P.ld, cs);
+    }
+
+    // Sharded optimiser: once this rank has updated its slice of chunk c, the
+    // chunk's bf16 weights are all-gathered on the comm stream.
+    int gather_weights(PlanLayer& P, int c, int64_t r0, int64_t r1) {
+        if (!m->sharded) return RT_OK;
+        RT_CUDA(cudaStreamWaitEvent(m->comm_stream, P.ev_opt[c], 0));
+        const int64_t e = shard_end(P, r1);
+        if (e > r0) RT_TRY(comm_all_gather(m->comm, P.w16 + r0 * P.ld, (e - r0) * P.ld / m->world, 2, m->comm_stream));
+        RT_CUDA(cudaEventRecord(P.ev_ag[c], m->comm_stream));
+        return RT_OK;
     }
 
     // Backward and update.  Per layer, top down: the dW GEMM (in row chunks of
@@ -327,6 +374,7 @@ struct Enqueuer {
                     if (m->comm) RT_CUDA(cudaStreamWaitEvent(m->opt_stream, P.ev_comm[c], 0));
                     RT_TRY(enqueue_update_rows(m, P, r0, r1, m->opt_stream));
                     RT_CUDA(cudaEventRecord(P.ev_opt[c], m->opt_stream));
+                    RT_TRY(gather_weights(P, c, r0, r1));
                 }
             }
             if (l > 0) {
@@ -362,13 +410,16 @@ struct Enqueuer {
                         if (m->comm) RT_CUDA(cudaStreamWaitEvent(m->opt_stream, P.ev_comm[c], 0));
                         RT_TRY(enqueue_update_rows(m, P, r0, r1, m->opt_stream));
                         RT_CUDA(cudaEventRecord(P.ev_opt[c], m->opt_stream));
+                        RT_TRY(gather_weights(P, c, r0, r1));
                     }
                 }
             }
         }
         for (PlanLayer& P : m->L)
             for (int c = 0; c < P.chunks; ++c) {
-                if (update)
+                if (m->sharded)
+                    RT_CUDA(cudaStreamWaitEvent(st, P.ev_ag[c], 0));
+                else if (update)
                     RT_CUDA(cudaStreamWaitEvent(st, P.ev_opt[c], 0));
                 else if (m->comm)
                     RT_CUDA(cudaStreamWaitEvent(st, P.ev_comm[c], 0));
@@ -399,14 +450,17 @@ int prepare_chunks(rt_mlp* m) {
         for (auto e : P.ev_ready) cudaEventDestroy(e);
         for (auto e : P.ev_comm) cudaEventDestroy(e);
         for (auto e : P.ev_opt) cudaEventDestroy(e);
+        for (auto e : P.ev_ag) cudaEventDestroy(e);
         P.chunks = ch;
         P.ev_ready.assign(ch, nullptr);
         P.ev_comm.assign(ch, nullptr);
         P.ev_opt.assign(ch, nullptr);
+        P.ev_ag.assign(ch, nullptr);
         for (int c = 0; c < ch; ++c)
             if (cudaEventCreateWithFlags(&P.ev_ready[c], cudaEventDisableTiming) != cudaSuccess ||
                 cudaEventCreateWithFlags(&P.ev_comm[c], cudaEventDisableTiming) != cudaSuccess ||
-                cudaEventCreateWithFlags(&P.ev_opt[c], cudaEventDisableTiming) != cudaSuccess)
+                cudaEventCreateWithFlags(&P.ev_opt[c], cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&P.ev_ag[c], cudaEventDisableTiming) != cudaSuccess)
                 return fail(RT_ERR_CUDA, "event creation failed");
         if (!P.ev_dx && cudaEventCreateWithFlags(&P.ev_dx, cudaEventDisableTiming) != cudaSuccess)
             return fail(RT_ERR_CUDA, "event creation failed");
@@ -497,6 +551,21 @@ int read_packed(rt_mlp* m, const void* src, rt_dtype dt, int64_t rows, int64_t c
         RT_CUDA(cudaFreeAsync(tmp, st));
     }
     RT_CUDA(cudaStreamSynchronize(st));
+    return RT_OK;
+}
+
+// Sharded optimiser: completes a [d+1, ld] f32 buffer of layer P (masters,
+// moments or reduced gradients, of which each rank holds its slices) by an
+// in-place all-gather of every chunk's weight rows.  Collective: every rank
+// calls it, in the same order.
+int gather_block(rt_mlp* m, PlanLayer& P, float* buf) {
+    if (!m->sharded || !buf) return RT_OK;
+    cudaStream_t st = m->ctx->stream;
+    for (int c = 0; c < P.chunks; ++c) {
+        const int64_t r0 = chunk_row_of(P.d + 1, P.chunks, c);
+        const int64_t e = shard_end(P, chunk_row_of(P.d + 1, P.chunks, c + 1));
+        if (e > r0) RT_TRY(comm_all_gather(m->comm, buf + r0 * P.ld, (e - r0) * P.ld / m->world, 4, st));
+    }
     return RT_OK;
 }
 
@@ -689,6 +758,7 @@ int rt_mlp_last_loss(rt_mlp* m, float* out) {
 int rt_mlp_weights(rt_mlp* m, int layer, float* w, float* b) {
     RT_CHECK(m && layer >= 0 && layer < (int)m->L.size(), "bad layer index");
     PlanLayer& P = m->L[layer];
+    if (w) RT_TRY(gather_block(m, P, P.w32));
     if (w) RT_TRY(read_packed(m, P.w32, RT_F32, P.d, P.u, P.ld, w));
     if (b) RT_TRY(read_packed(m, P.b, RT_F32, 1, P.u, P.u, b));
     return RT_OK;
@@ -697,6 +767,7 @@ int rt_mlp_weights(rt_mlp* m, int layer, float* w, float* b) {
 int rt_mlp_grads(rt_mlp* m, int layer, float* dw, float* db) {
     RT_CHECK(m && layer >= 0 && layer < (int)m->L.size(), "bad layer index");
     PlanLayer& P = m->L[layer];
+    if (dw) RT_TRY(gather_block(m, P, P.g));
     if (dw) RT_TRY(read_packed(m, P.g, RT_F32, P.d, P.u, P.ld, dw));
     if (db) RT_TRY(read_packed(m, P.db, RT_F32, 1, P.u, P.u, db));
     return rt_ctx_sync(m->ctx);
@@ -765,6 +836,11 @@ int rt_mlp_save_state(rt_mlp* m, void* host, size_t bytes) {
     p += sizeof(h);
     std::memcpy(p, m->dims.data(), sizeof(int64_t) * m->dims.size());
     p += sizeof(int64_t) * m->dims.size();
+    for (PlanLayer& P : m->L) {
+        RT_TRY(gather_block(m, P, P.w32));
+        RT_TRY(gather_block(m, P, P.m));
+        RT_TRY(gather_block(m, P, P.v));
+    }
     for (PlanLayer& P : m->L) {
         const size_t blk = (size_t)(P.d + 1) * P.u * 4;
         RT_TRY(copy_block(m, P, P.w32, p, true));
@@ -853,6 +929,15 @@ int rt_mlp_op_time(rt_mlp* m, int i, const char** label, double* flops, float* m
     return RT_OK;
 }
 
+int rt_mlp_comm_mode(rt_mlp* m, int* mode) {
+    RT_CHECK(m && mode, "bad arguments");
+    *mode = !m->comm ? RT_COMM_NONE
+            : m->sharded ? RT_COMM_SHARDED_OPT
+            : m->comm_bf16 ? RT_COMM_ALLREDUCE_BF16
+                           : RT_COMM_ALLREDUCE;
+    return RT_OK;
+}
+
 int rt_mlp_set_comm(rt_mlp* m, rt_comm* comm) {
     RT_CHECK(m, "bad arguments");
     m->comm = comm;
@@ -875,6 +960,21 @@ int rt_mlp_set_comm(rt_mlp* m, rt_comm* comm) {
                 P.g16 = static_cast<__nv_bfloat16*>(p);
             }
     RT_TRY(prepare_chunks(m));
+    // Sharded optimiser: bf16 plans (their GEMMs read only the bf16 weights)
+    // with an optimiser, more than one rank, every chunk divisible by the
+    // world size; RTGPU_SHARDED_OPT=0 keeps the replicated update.
+    m->rank = comm_rank(comm);
+    m->world = comm_world(comm);
+    const char* so = getenv("RTGPU_SHARDED_OPT");
+    bool sharded = comm && m->world > 1 && m->adt == RT_BF16 && m->cfg.optimizer != RT_OPT_NONE &&
+                   !m->comm_bf16 && !(so && so[0] == '0');
+    for (const PlanLayer& P : m->L)
+        for (int c = 0; sharded && c < P.chunks; ++c) {
+            const int64_t r0 = chunk_row_of(P.d + 1, P.chunks, c);
+            const int64_t e = shard_end(P, chunk_row_of(P.d + 1, P.chunks, c + 1));
+            if (e > r0 && ((e - r0) * P.ld) % m->world) sharded = false;
+        }
+    m->sharded = sharded;
     m->ops.clear();
     drop_graphs(m);
     return RT_OK;

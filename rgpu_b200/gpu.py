@@ -123,6 +123,7 @@ _SIGS = [
     ("rt_mlp_op_time", C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_double),
                                  C.POINTER(C.c_float)]),
     ("rt_mlp_set_comm", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("rt_mlp_comm_mode", C.c_int, [C.c_void_p, C.c_void_p]),
     ("rt_param_create", C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.POINTER(C.c_void_p)]),
     ("rt_param_destroy", C.c_int, [C.c_void_p]),
     ("rt_param_read", C.c_int, [C.c_void_p, C.c_void_p]),
@@ -584,6 +585,13 @@ class GpuMlp:
     def set_comm(self, comm: Comm | None):
         self._comm = comm
         _check(lib().rt_mlp_set_comm(self.handle, comm.handle if comm else None))
+
+    def comm_mode(self) -> str:
+        """How gradients are summed: "none", "allreduce", "allreduce_bf16" or
+        "sharded_opt" (reduce-scatter, sliced update, weight all-gather)."""
+        v = C.c_int()
+        _check(lib().rt_mlp_comm_mode(self.handle, C.byref(v)))
+        return ("none", "allreduce", "allreduce_bf16", "sharded_opt")[v.value]
 
 
 def _is_bf16(t: GpuTensor) -> bool:

@@ -30,3 +30,8 @@ def test_two_rank_dp_equals_single_gpu(tmp_path):
     assert max(res["bf16_gradcomm"]) <= 2e-2, res["bf16_gradcomm"]
     assert max(res["bf16"]) <= 2e-2, res["bf16"]
     assert res["replicas_identical"]
+    sh = res["sharded"]
+    assert sh["modes"] == ["allreduce", "sharded_opt"], sh
+    # two ranks: a + b in either collective, the same elementwise update
+    assert sh["weights"] <= 1e-6 and sh["grads"] <= 1e-6 and sh["state"] <= 1e-6, sh
+    assert sh["header_equal"] and sh["replicas_identical"], sh
