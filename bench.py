@@ -202,6 +202,8 @@ def run_gemm_only(args):
     gpu.sync()
     st = torch.cuda.ExternalStream(gpu.stream())
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(st):
+        torch.cuda._sleep(20000000)  # the host enqueues the timed launches meanwhile
     e0.record(st)
     for _ in range(args.reps):
         fn(a, b, c)
@@ -223,8 +225,11 @@ def run_dw_sweep(args):
     M in {1024,4096,8192} x N in {512,4096,8192} x K (the batch) in
     {1,...,16384}, f32 (3xTF32 tensor cores) and bf16 operands, f32 output,
     split-K chosen by the library.  Entries N(0,1).  Each point is timed with
-    CUDA events around the GEMM alone, with L2 flushed (a 256 MB write)
-    before every repetition.  Roofline time = max(2MNK / peak,
+    CUDA events around the GEMM alone, with L2 flushed before every
+    repetition: a 256 MB write, then a 256 MB read of another buffer, so the
+    GEMM starts from a cold L2 that holds no dirty lines (a write flush alone
+    leaves ~126 MB to be written back during the GEMM, a 50 % surcharge on
+    the output-write-bound small-K points).  Roofline time = max(2MNK / peak,
     ((M+N) K s_in + 4 M N) / HBM); the f32 peak is the bf16 figure / 2 (tf32
     rate) / 3 (three products).  Each timed span holds one rt_gemm call: the
     operand split (f32), the GEMM and the split-K reduction when it splits."""
@@ -238,6 +243,8 @@ def run_dw_sweep(args):
     dev = torch.device("cuda", 0)
     st = torch.cuda.ExternalStream(gpu.stream(), device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush_rd = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+    flush_sum = torch.empty((), dtype=torch.float32, device=dev)
     gen = torch.Generator(device=dev)
     gen.manual_seed(4)
     dtypes = args.sweep_dtypes.split(",")
@@ -267,13 +274,16 @@ def run_dw_sweep(args):
                     gpu.sync()
                     flops = 2.0 * m * n * k
                     reps = max(3, min(20, int(2e12 / max(flops, 1.0))))
-                    # flush, event, GEMM, event on the library's stream: the
-                    # flush keeps the GPU busy while the host enqueues the
-                    # GEMM, so its launch cost stays out of the timed span
+                    # flush, event, GEMM, event on the library's stream, all
+                    # enqueued behind a device sleep: the GPU starts only once
+                    # the host has enqueued every repetition, so host-side
+                    # launch cost stays out of the timed spans
                     evs = []
                     with torch.cuda.stream(st):
+                        torch.cuda._sleep(40000000)
                         for _ in range(reps):
                             flush.fill_(1)
+                            torch.sum(flush_rd, dim=None, out=flush_sum)
                             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                             e0.record(st)
                             gpu.gemm(a)

@@ -238,6 +238,10 @@ int rt_mlp_forward_only(rt_mlp* mlp, const void* x_dev, rt_dtype x_dtype);
 int rt_mlp_logits(rt_mlp* mlp, float* host);
 /* GpuMlp::last_loss (gpu/mod.rs:1529-1531): mean row loss, blocking. */
 int rt_mlp_last_loss(rt_mlp* mlp, float* out);
+/* The last step's mean loss over the global batch: with a communicator the
+ * ranks' per-row losses are all-gathered and summed in global row order
+ * (collective: every rank calls it); without one, rt_mlp_last_loss. */
+int rt_mlp_global_loss(rt_mlp* mlp, float* out);
 /* GpuMlp::weights / grads (gpu/mod.rs:1534-1551) for one layer, blocking,
  * packed f32 (w: d_l*d_{l+1}, b: d_{l+1}); either pointer may be NULL. */
 int rt_mlp_weights(rt_mlp* mlp, int layer, float* w, float* b);

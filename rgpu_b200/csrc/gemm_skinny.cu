@@ -30,6 +30,15 @@ __device__ __forceinline__ float ld_f<__nv_bfloat16>(const __nv_bfloat16* p, int
     return __bfloat162float(p[i]);
 }
 
+// Four consecutive elements from a 4-element-aligned address, as f32.
+__device__ __forceinline__ float4 ld4_f(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ float4 ld4_f(const __nv_bfloat16* p) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+    const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+
 struct SkinnyParams {
     const void* a;
     const void* b;
@@ -292,7 +301,8 @@ __global__ void __launch_bounds__(kThreads) skinny_k_kernel(SkinnyParams p) {
     const int64_t m0 = (int64_t)blockIdx.y * TM, n0 = (int64_t)blockIdx.x * TN;
     const int k = (int)p.k;
     for (int t = threadIdx.x; t < TM * KMAX; t += kThreads) {
-        const int r = t / KMAX, q = t % KMAX;
+        // consecutive threads read consecutive addresses of A
+        const int r = A_KMAJOR ? t / KMAX : t % TM, q = A_KMAJOR ? t % KMAX : t / TM;
         const int64_t i = m0 + r;
         sa[r][q] = (i < p.m && q < k) ? ld_f(A, A_KMAJOR ? i * p.lda + q : (int64_t)q * p.lda + i) : 0.0f;
     }
@@ -300,12 +310,26 @@ __global__ void __launch_bounds__(kThreads) skinny_k_kernel(SkinnyParams p) {
     const int rg = threadIdx.x / 64;  // rows rg, rg + 4, ...
     const int64_t j0 = n0 + cg * 4;
     float b[KMAX][4];
+    if (!B_KMAJOR && j0 + 4 <= p.n && (p.ldb % 4) == 0 &&
+        (reinterpret_cast<uintptr_t>(B) % (4 * sizeof(TIn))) == 0) {
+        // a row of B holds this thread's four columns: one vector load per k
 #pragma unroll
-    for (int q = 0; q < KMAX; ++q)
+        for (int q = 0; q < KMAX; ++q) {
+            const float4 v = q < k ? ld4_f(B + (int64_t)q * p.ldb + j0) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            b[q][0] = v.x;
+            b[q][1] = v.y;
+            b[q][2] = v.z;
+            b[q][3] = v.w;
+        }
+    } else {
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-            b[q][c] = (q < k && j0 + c < p.n) ? ld_f(B, B_KMAJOR ? (j0 + c) * p.ldb + q : (int64_t)q * p.ldb + j0 + c)
-                                             : 0.0f;
+        for (int q = 0; q < KMAX; ++q)
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                b[q][c] = (q < k && j0 + c < p.n)
+                              ? ld_f(B, B_KMAJOR ? (j0 + c) * p.ldb + q : (int64_t)q * p.ldb + j0 + c)
+                              : 0.0f;
+    }
     const bool vec = j0 + 4 <= p.n && four_aligned(p);
     // the ReLU-mask epilogue's loads for all of this thread's rows, in flight together
     float4 mk[RPT];

@@ -111,6 +111,7 @@ struct rt_mlp {
     int next_slot = 0;
     int last_slot = 0;
     float* loss_rows = nullptr;
+    float* loss_all = nullptr;  // [world * batch] per-row losses of every rank (rt_mlp_global_loss)
     OptScalars* opt = nullptr;
     // f32 plans: hi/lo operand planes of the 3xTF32 GEMMs, sized for the
     // largest GEMM of the step (the GEMMs run one after another on one stream)
@@ -753,6 +754,26 @@ int rt_mlp_last_loss(rt_mlp* m, float* out) {
     for (float v : rows) sum += v;
     *out = sum / (float)m->n;
     return rt_ctx_sync(m->ctx);
+}
+
+int rt_mlp_global_loss(rt_mlp* m, float* out) {
+    RT_CHECK(m && out, "bad arguments");
+    if (!m->comm || m->world == 1) return rt_mlp_last_loss(m, out);
+    // All-gather the ranks' per-row losses (rank r holds rows [r*n, (r+1)*n)
+    // of the global batch), then mean_all's sequential f32 sum over the
+    // global batch in row order: the single-device loss, bit for bit.
+    cudaStream_t st = m->ctx->stream;
+    const int64_t n = m->n, total = n * m->world;
+    if (!m->loss_all) RT_TRY(dalloc_t(m, &m->loss_all, (size_t)total));
+    RT_CUDA(cudaMemcpyAsync(m->loss_all + (int64_t)m->rank * n, m->loss_rows, (size_t)n * 4,
+                            cudaMemcpyDeviceToDevice, st));
+    RT_TRY(comm_all_gather(m->comm, m->loss_all, n, 4, st));
+    std::vector<float> rows((size_t)total);
+    RT_TRY(read_packed(m, m->loss_all, RT_F32, 1, total, total, rows.data()));
+    float sum = 0.0f;
+    for (float v : rows) sum += v;
+    *out = sum / (float)total;
+    return RT_OK;
 }
 
 int rt_mlp_weights(rt_mlp* m, int layer, float* w, float* b) {

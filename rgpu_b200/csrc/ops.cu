@@ -76,6 +76,22 @@ static int x3_context_scratch(rt_ctx* ctx, cudaStream_t stream, size_t need, flo
     return RT_OK;
 }
 
+// A narrow-K GEMM (k <= 16 < n) is one write of its output; the tensor-core
+// kernels (one k-block, zero-filled past k) write it faster than the CUDA-core
+// narrow-K kernel.  Measured on B200 with L2 flushed (dW sweep shapes, TN):
+// bf16 at k = 1 / 8 / 16 and 8192 x 8192 outputs, 60 / 60 / 60 us against
+// 70 / 108 / 168 us, and never slower at smaller outputs.  f32 operands pay
+// the 3xTF32 split and three products: ahead from k = 8 at 8192 x 8192
+// (83 against 100 us) and from k = 16 at 4096 x 4096 (36 against 51 us),
+// behind below that (k = 1: 167 against 69 us).
+bool narrow_k_on_tensor_cores(const rt_ctx* ctx, const GemmDesc& g) {
+    if (g.n <= kSkinnyMax) return false;
+    if (ctx->skinny_k_max >= 0 && g.k <= ctx->skinny_k_max) return false;
+    if (gemm_tc_supported(ctx, g)) return true;
+    if (g.no_alloc || !gemm_x3_supported(ctx, g)) return false;
+    return ctx->skinny_k_max >= 0 || (g.k >= 8 && (double)g.k * g.m * g.n >= (double)(1 << 28));
+}
+
 int run_gemm(rt_ctx* ctx, GemmDesc g, cudaStream_t stream, size_t ws_bytes) {
     RT_TRY(check_gemm(g));
     if (g.m == 0 || g.n == 0) return RT_OK;
@@ -89,7 +105,8 @@ int run_gemm(rt_ctx* ctx, GemmDesc g, cudaStream_t stream, size_t ws_bytes) {
         RT_CHECK((size_t)g.split_k * g.m * g.n * 4 <= ws_bytes, "split-K workspace too small: %zu < %zu bytes",
                  ws_bytes, (size_t)g.split_k * g.m * g.n * 4);
     }
-    if (ctx->fast_gemm && gemm_skinny_wanted(g)) return launch_gemm_skinny(ctx, g, stream);
+    if (ctx->fast_gemm && gemm_skinny_wanted(g) && !narrow_k_on_tensor_cores(ctx, g))
+        return launch_gemm_skinny(ctx, g, stream);
     if (ctx->fast_gemm && gemm_tc_supported(ctx, g)) return launch_gemm_tc(ctx, g, stream);
     if (ctx->fast_gemm && !g.no_alloc && gemm_x3_supported(ctx, g)) {
         const size_t need = gemm_x3_workspace_bytes(g);

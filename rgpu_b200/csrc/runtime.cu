@@ -90,6 +90,10 @@ int rt_ctx_create(int device, rt_ctx** out) {
     c->f32_tensor = !(f32_env && f32_env[0] == '0');
     const char* st_env = getenv("RTGPU_TMA_STORE");
     c->tma_store = !(st_env && st_env[0] == '0');
+    // RTGPU_SKINNY_K_MAX=<k>: narrow-K GEMMs deeper than k go to the tensor
+    // cores (default: chosen by dtype and size, see narrow_k_on_tensor_cores)
+    const char* sk_env = getenv("RTGPU_SKINNY_K_MAX");
+    if (sk_env) c->skinny_k_max = std::max(0, std::min(atoi(sk_env), (int)kSkinnyMax));
     int st = gemm_tc_init(c);
     if (st == RT_OK) st = gemm_tc2_init(c);
     if (st == RT_OK) st = gemm_x3_init(c);

@@ -111,6 +111,7 @@ _SIGS = [
     ("rt_mlp_forward_only", C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
     ("rt_mlp_logits", C.c_int, [C.c_void_p, C.c_void_p]),
     ("rt_mlp_last_loss", C.c_int, [C.c_void_p, C.POINTER(C.c_float)]),
+    ("rt_mlp_global_loss", C.c_int, [C.c_void_p, C.POINTER(C.c_float)]),
     ("rt_mlp_weights", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     ("rt_mlp_grads", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     ("rt_mlp_set_weights", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
@@ -510,6 +511,13 @@ class GpuMlp:
     def last_loss(self) -> float:
         v = C.c_float()
         _check(lib().rt_mlp_last_loss(self.handle, C.byref(v)))
+        return v.value
+
+    def global_loss(self) -> float:
+        """Mean loss of the last step over the global batch (all ranks'
+        rows, summed in global row order); collective under a communicator."""
+        v = C.c_float()
+        _check(lib().rt_mlp_global_loss(self.handle, C.byref(v)))
         return v.value
 
     def weights(self):

@@ -64,14 +64,17 @@ def main():
         mlp.set_comm(comm)
         mlp.step(gpu.upload(xs), rgpu_b200.upload_labels(gpu, ls))
         g_dp = mlp.grads()
+        loss_dp = mlp.global_loss()
         mlp.close()
         if rank == 0:
             ref = rgpu_b200.GpuMlp.from_params(gpu, params, n_global, 0.0, dtype=dtype, optimizer="none")
             ref.step(gpu.upload(x), rgpu_b200.upload_labels(gpu, labels))
             g_ref = ref.grads()
+            loss_ref = ref.last_loss()
             ref.close()
             result[dtype_name] = [float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
                                   for a, b in zip(g_dp, g_ref)]
+            result[dtype_name + "_loss"] = [loss_dp, loss_ref]
     # Adam with chunked dW GEMMs and bf16 gradient sums: replicas stay bit-identical.
     os.environ["RTGPU_FIRST_LAYER_CHUNKS"] = "4"
     os.environ["RTGPU_DW_CHUNKS"] = "2"

@@ -30,6 +30,12 @@ def test_two_rank_dp_equals_single_gpu(tmp_path):
     assert max(res["bf16_gradcomm"]) <= 2e-2, res["bf16_gradcomm"]
     assert max(res["bf16"]) <= 2e-2, res["bf16"]
     assert res["replicas_identical"]
+    # the global-batch loss from all-gathered per-row losses, summed in global
+    # row order, is the single-GPU loss (rows are independent; here both runs
+    # pick the same GEMM kernels, so it agrees to rounding of the last bit)
+    for case in ("f32", "bf16", "f32_chunked", "bf16_gradcomm"):
+        dp, single = res[case + "_loss"]
+        assert abs(dp - single) <= 1e-6 * abs(single), (case, dp, single)
     sh = res["sharded"]
     assert sh["modes"] == ["allreduce", "sharded_opt"], sh
     # two ranks: a + b in either collective, the same elementwise update

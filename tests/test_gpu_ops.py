@@ -216,7 +216,7 @@ def test_relu_mask_epilogue_via_rt_gemm(gpu):
 
 
 SKINNY = [(2048, 10, 1024), (1025, 10, 2048), (2048, 1024, 10), (37, 16, 300), (300, 200, 16), (5, 3, 7),
-          (129, 1, 4096), (64, 2000, 1)]
+          (129, 1, 4096), (64, 2000, 1), (70, 203, 5), (70, 204, 9)]
 
 
 def _skinny_ref(a, b, epi, bias, mask):
@@ -260,6 +260,41 @@ def test_skinny_gemms_every_layout_and_epilogue(gpu, m, n, k, dtype):
                 gpu.gemm(args)
                 e = rel_l2(gpu.download(c), _skinny_ref(a, b, epi, bias, mask))
                 assert e <= 1e-6 + 1.6e-9 * k, f"layout {layout} epi {epi} split {split} {m}x{n}x{k} {dtype}: {e:.2e}"
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 512, 1), (300, 200, 8), (512, 1024, 16), (2048, 1024, 10)])
+def test_narrow_k_gemms_on_the_tensor_cores(monkeypatch, m, n, k):
+    # RTGPU_SKINNY_K_MAX=0 sends every narrow-K GEMM that the tensor cores
+    # can take there (one k-block, zero-filled past k): f32 operands as
+    # 3xTF32 in two launches (operand split, GEMM), bf16 in one.  Against the
+    # exact product of the (bf16-rounded) operands, with the 3xTF32 bound.
+    monkeypatch.setenv("RTGPU_SKINNY_K_MAX", "0")
+    g = rgpu_b200.Gpu(0)
+    try:
+        a0, b0 = _ab(m, n, k)
+        mask = np.sin(np.arange(m * n, dtype=np.float32) * 0.5).reshape(m, n).astype(np.float32)
+        gmask = g.upload(mask)
+        for dtype, launches in (("f32", 2), ("bf16", 1)):
+            a, b = a0, b0
+            if dtype == "bf16":
+                a = rgpu_b200.bf16_to_f32(rgpu_b200.f32_to_bf16(a))
+                b = rgpu_b200.bf16_to_f32(rgpu_b200.f32_to_bf16(b))
+            ops = {G.RT_NN: (a, b), G.RT_NT: (a, np.ascontiguousarray(b.T)), G.RT_TN: (np.ascontiguousarray(a.T), b)}
+            for layout, (x, y) in ops.items():
+                gx, gy = g.upload(x, dtype), g.upload(y, dtype)
+                for epi in (G.RT_EPI_NONE, G.RT_EPI_RELU_MASK):
+                    c = g.zeros((m, n))
+                    args = G.GemmArgs(layout, G.RT_BF16 if dtype == "bf16" else G.RT_F32, G.RT_F32, m, n, k,
+                                      gx.ptr, gx.ld, gy.ptr, gy.ld, c.ptr, c.ld, epi, None, gmask.ptr, gmask.ld,
+                                      1, None, 0)
+                    before = g.launch_count()
+                    g.gemm(args)
+                    g.sync()
+                    assert g.launch_count() - before == launches, (dtype, layout, epi)
+                    e = rel_l2(g.download(c), _skinny_ref(a, b, epi, None, mask))
+                    assert e <= 1e-6 + 3e-9 * k, f"layout {layout} epi {epi} {m}x{n}x{k} {dtype}: {e:.2e}"
+    finally:
+        g.close()
 
 
 def test_skinny_gemm_is_one_launch(gpu):
