@@ -33,14 +33,25 @@ CONFIGS = {
     "wide": dict(dims=[4096, 8192, 8192, 8192, 1000], batch=8192, dtype="bf16", optimizer="adam", lr=1e-3),
     # 512 -> 1024 -> 1024 -> 10, f32, SGD 0.01, batch 2048
     "small": dict(dims=[512, 1024, 1024, 10], batch=2048, dtype="f32", optimizer="sgd", lr=0.01),
+    # profiling case for ncu: one 8192 -> 8192 layer of the wide MLP (its
+    # step is a forward GEMM, the softmax-CE and one dW GEMM with the Adam
+    # update fused into its epilogue), 1.6 GB on the device
+    "probe_dw": dict(dims=[8192, 8192], batch=8192, dtype="bf16", optimizer="adam", lr=1e-3),
 }
-CPU_SAMPLE_ROWS = {"wide": 64, "small": 256}
+CPU_SAMPLE_ROWS = {"wide": 64, "small": 256, "probe_dw": 64}
 # DRAM bytes (read + write) of one 8192 x 8192 x 8192 dW GEMM launch (the
 # two-CTA kernel), from an ncu capture (dram__bytes_read.sum +
 # dram__bytes_write.sum) of `bench.py --gemm TN --mnk 8192 8192 8192`; scaled
 # to other dW launches by their FLOPs.
 DW_GEMM_TRAFFIC_BYTES = 1.099e9 + 0.251e9
 DW_GEMM_TRAFFIC_FLOPS = 2.0 * 8192 ** 3
+# The same for the dW launch with the fused Adam update (the [W; b] block of
+# an 8192 -> 8192 layer at batch 8192: the dW GEMM of `bench.py --config
+# probe_dw`, 2 * 8192^3 FLOPs as the plan counts them, the bias row aside);
+# every dW launch of the wide step has k = 8192, so its bytes scale with its
+# FLOPs there too.
+DW_ADAM_TRAFFIC_BYTES = 2.187e9 + 1.183e9
+DW_ADAM_TRAFFIC_FLOPS = 2.0 * 8192 ** 3
 
 
 def peaks():
@@ -77,36 +88,66 @@ def make_inputs(cfg, rows, seed):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons during the timed region."""
+    """nvidia-smi clocks and throttle reasons during the timed region.
+
+    nvidia-smi takes a while to print its first sample, so the sampler is
+    started before the warm-up and waits for that first line; every sample is
+    time-stamped on arrival and only those between mark_start() and stop()
+    are kept (the window is widened to the warm-up when the timed region is
+    too short to hold one)."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, device_index):
         self.dev = device_index
         self.proc = None
+        self.lines = []
+        self.t_open = self.t0 = None
 
     def start(self):
+        import threading
+
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
+            return
+
+        def reader():
+            for line in self.proc.stdout:
+                self.lines.append((time.monotonic(), line))
+
+        threading.Thread(target=reader, daemon=True).start()
+        t_end = time.monotonic() + 10.0
+        while not self.lines and time.monotonic() < t_end and self.proc.poll() is None:
+            time.sleep(0.02)
+        self.t_open = time.monotonic()
+
+    def mark_start(self):
+        self.t0 = time.monotonic()
 
     def stop(self):
         if not self.proc:
             return None
+        t1 = time.monotonic()
+        time.sleep(0.06)  # the sample that covers the region's last moments
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-            return None
+        window = "timed"
+        lines = [ln for t, ln in self.lines if self.t0 is not None and self.t0 <= t <= t1 + 0.06]
+        if not lines:
+            window = "warm-up and timed"
+            lines = [ln for t, ln in self.lines if self.t_open is not None and self.t_open <= t <= t1 + 0.06]
         sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
+        for line in lines:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 7:
                 continue
@@ -115,13 +156,13 @@ class ClockSampler:
                 mx = float(f[1])
             except ValueError:
                 continue
-            for name, v in zip(names, f[3:7]):
+            for name, v in zip(self.NAMES, f[3:7]):
                 if v.lower().startswith("active"):
                     reasons.add(name)
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "window": window}
 
 
 def cpu_baseline(cfg_name, cfg, warm=1, reps=1, rows=None):
@@ -375,7 +416,7 @@ def config_dict(cfg_name, cfg, n, global_batch):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="wide", choices=sorted(CONFIGS))
@@ -487,13 +528,14 @@ def main():
         barrier()
         return float(t.item())
 
+    clocks = ClockSampler(local)
+    clocks.start()
     for _ in range(args.warmup):
         step_dev()
     gpu.sync()
 
     # ---- timed region: device-resident inputs (the captured step as shipped)
-    clocks = ClockSampler(local)
-    clocks.start()
+    clocks.mark_start()
     launches0 = gpu.launch_count()
     ms = timed(step_dev, args.steps)
     launches = gpu.launch_count() - launches0
@@ -538,9 +580,13 @@ def main():
         traffic = None
         if lab == "dw_gemm" and cfg["dtype"] == "bf16":  # plain dW launch, as captured
             traffic = DW_GEMM_TRAFFIC_BYTES * (fl / cnt) / DW_GEMM_TRAFFIC_FLOPS
+        elif lab == "dw_gemm_adam" and cfg["dtype"] == "bf16" and DW_ADAM_TRAFFIC_BYTES:
+            traffic = DW_ADAM_TRAFFIC_BYTES * (fl / cnt) / DW_ADAM_TRAFFIC_FLOPS
         roof = {"bound": "tensor", "kernel": lab, "launches_per_step": cnt, "achieved": ach, "peak": peak,
                 "unit": "TFLOP/s", "frac": ach / peak, "traffic": traffic,
-                "traffic_note": "bytes per launch, ncu capture of the 8192^3 dW GEMM scaled by FLOPs",
+                "traffic_note": "bytes per launch, ncu capture of the 8192^3 dW GEMM" + (
+                    " with fused Adam (bench.py --config probe_dw)" if lab == "dw_gemm_adam" else "")
+                + " scaled by FLOPs",
                 "peak_source": pk["source"] + (" bf16 dense (cuBLAS burst)" if cfg["dtype"] == "bf16"
                                                else " bf16 dense / 2 (tf32 rate) / 3 (3xTF32 products)")}
     gemm_t = sum(t for lab, fl, t in ops if fl > 0)

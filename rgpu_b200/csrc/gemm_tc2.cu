@@ -340,6 +340,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
                         if (row < p.m) epilogue_math<float>(p, row, col0, v);
                         stage_and_store<float>(&tmap_c, box, lane, row0, col0, v);
                     }
+                } else if (p.tma_store == 3) {
+                    // fused optimiser: the chunk updates theta / m / v / shadow and is stored as C
+                    opt_chunk(p, reinterpret_cast<float*>(smem_epi + (warp - 4) * kStageBytes), lane, row0, col0, v);
                 } else if (row < p.m) {
                     if (p.ws) {
                         float* dst = p.ws + (int64_t)split * p.m * p.n + row * p.n + col0;
@@ -371,7 +374,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
             record_error(p.err, DEV_TIMEOUT_EPILOGUE, blockIdx.x);
             raise_abort();
         }
-        if (p.tma_store && lane == 0) bulk_wait_all();  // this warp's output stores are complete
+        if ((p.tma_store == 1 || p.tma_store == 2) && lane == 0) bulk_wait_all();  // this warp's output stores are complete
     }
 
     __syncwarp();
@@ -449,6 +452,8 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X
     if (ctx->tma_store && splits == 1 && !g.opt.kind) {
         p.tma_store = 1;
         RT_TRY(make_tmap_out(&tc, g.c, p.out_bf16 != 0, g.m, g.n, g.ldc));
+    } else if (ctx->tma_store && splits == 1 && !p.out_bf16) {
+        p.tma_store = 3;  // fused optimiser through the epilogue boxes
     } else if (ctx->tma_store && splits > 1 && g.n % 4 == 0 && (reinterpret_cast<uintptr_t>(g.workspace) & 15) == 0) {
         p.tma_store = 2;
         RT_TRY(make_tmap_ws(&tc, g.workspace, g.m, g.n, splits));

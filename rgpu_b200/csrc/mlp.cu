@@ -129,6 +129,10 @@ struct rt_mlp {
     int comm_sm_reserve = 0;  // SMs the backward GEMMs leave to NCCL while gradients are reduced
     cudaStream_t comm_stream = nullptr;
     bool comm_bf16 = false;  // allreduce the gradients in bf16 (bf16 plans, RTGPU_GRAD_COMM=bf16)
+    // Fused update (one device, SGD or Adam; RTGPU_FUSED_OPT=0 turns it off):
+    // each dW GEMM applies the optimiser to its output tile in the epilogue,
+    // so the update rides inside the GEMM instead of running after it.
+    bool fuse_opt = false;
     // Sharded optimiser (bf16 plans with an optimiser under data parallelism):
     // each gradient chunk is reduce-scattered, every rank updates its 1/world
     // slice of the f32 masters and moments, and the bf16 weights are
@@ -304,9 +308,26 @@ struct Enqueuer {
         g.max_sms = backward_sms();
         g.x3_ws = m->x3_ws;
         g.x3_ws_bytes = m->x3_ws_bytes;
+        if (m->fuse_opt) {
+            // the epilogue applies the update to rows [r0, r1) of theta (and m, v, shadow)
+            const int64_t o = r0 * P.ld;
+            g.opt.kind = m->cfg.optimizer == RT_OPT_ADAM ? 2 : 1;
+            g.opt.theta = P.w32 + o;
+            g.opt.m = P.m ? P.m + o : nullptr;
+            g.opt.v = P.v ? P.v + o : nullptr;
+            g.opt.shadow = P.w16 ? P.w16 + o : nullptr;
+            g.opt.sc = m->opt;
+            g.opt.lr = m->cfg.lr;
+            g.opt.beta1 = m->cfg.beta1;
+            g.opt.beta2 = m->cfg.beta2;
+            g.opt.eps = m->cfg.eps;
+        }
         RT_TRY(run_gemm(m->ctx, g, st, P.ws_bytes));
         // FLOPs of the weight rows (the bias row is not counted, as everywhere)
-        return mark("dw_gemm", 2.0 * m->n * (double)(r1 - r0 - (r1 == rows ? 1 : 0)) * P.u);
+        const char* label = !m->fuse_opt ? "dw_gemm"
+                            : m->cfg.optimizer == RT_OPT_ADAM ? "dw_gemm_adam"
+                                                              : "dw_gemm_sgd";
+        return mark(label, 2.0 * m->n * (double)(r1 - r0 - (r1 == rows ? 1 : 0)) * P.u);
     }
 
     // Sums gradient rows [r0, r1) over the ranks on the comm stream (in bf16 when
@@ -338,6 +359,57 @@ struct Enqueuer {
         return RT_OK;
     }
 
+    // delta_{l-1} = (delta_l W_l^T) * 1[A_{l-1} > 0]  (NT, fused mask)
+    int dx_gemm(int l) {
+        PlanLayer& P = m->L[l];
+        PlanLayer& Q = m->L[l - 1];
+        GemmDesc h{};
+        h.layout = RT_NT;
+        h.in_dtype = m->adt;
+        h.out_dtype = m->adt;
+        h.m = m->n;
+        h.n = P.d;
+        h.k = P.u;
+        h.a = P.delta;
+        h.lda = P.ld;
+        h.b = weights(P);
+        h.ldb = P.ld;
+        h.c = Q.delta;
+        h.ldc = Q.ld;
+        h.epi = RT_EPI_RELU_MASK;
+        h.mask = Q.act;
+        h.ldmask = Q.ld_act;
+        h.split_k = 1;
+        h.max_sms = backward_sms();
+        h.x3_ws = m->x3_ws;
+        h.x3_ws_bytes = m->x3_ws_bytes;
+        RT_TRY(run_gemm(m->ctx, h, st, 0));
+        return mark("dx_gemm_relu_mask", 2.0 * m->n * P.d * P.u);
+    }
+
+    // Backward with the update fused into the dW GEMMs (one device): per
+    // layer, top down, the dX GEMM first (the last reader of W_l), then the
+    // dW GEMM, whose epilogue updates W_l, b_l and their moments in place.
+    int backward_fused() {
+        const int nl = (int)m->L.size();
+        PlanLayer& Last = m->L[nl - 1];
+        double gb = (double)(m->cfg.global_batch > 0 ? m->cfg.global_batch : m->n);
+        if (m->cfg.optimizer == RT_OPT_ADAM) {
+            RT_TRY(launch_opt_step_begin(m->ctx, m->opt, m->cfg.beta1, m->cfg.beta2, st));
+            RT_TRY(mark("adam_scalars", 0));
+        }
+        RT_TRY(launch_xent(m->ctx, (const float*)Last.act, Last.ld, m->slot[s].labels, m->n, Last.u,
+                           (float)(1.0 / gb), Last.delta, m->adt, Last.ld, m->loss_rows, st));
+        RT_TRY(mark("softmax_xent", 0));
+        for (int l = nl - 1; l >= 0; --l) {
+            PlanLayer& P = m->L[l];
+            if (l > 0) RT_TRY(dx_gemm(l));
+            for (int c = 0; c < P.chunks; ++c)
+                RT_TRY(dw_gemm_rows(P, l, chunk_row_of(P.d + 1, P.chunks, c), chunk_row_of(P.d + 1, P.chunks, c + 1)));
+        }
+        return RT_OK;
+    }
+
     // Backward and update.  Per layer, top down: the dW GEMM (in row chunks of
     // [dW; db], contiguous rows of the parameter block), each chunk handed to
     // the comm stream for its allreduce as soon as it is computed; then the dX
@@ -347,6 +419,7 @@ struct Enqueuer {
     // directly: its dW GEMM is the last GEMM of the step, and chunking it keeps
     // the trailing update (and allreduce) to one chunk.
     int backward_and_update() {
+        if (m->fuse_opt) return backward_fused();
         const int nl = (int)m->L.size();
         const bool update = m->cfg.optimizer != RT_OPT_NONE;
         PlanLayer& Last = m->L[nl - 1];
@@ -379,30 +452,7 @@ struct Enqueuer {
                 }
             }
             if (l > 0) {
-                // delta_{l-1} = (delta_l W_l^T) * 1[A_{l-1} > 0]  (NT, fused mask)
-                PlanLayer& Q = m->L[l - 1];
-                GemmDesc h{};
-                h.layout = RT_NT;
-                h.in_dtype = m->adt;
-                h.out_dtype = m->adt;
-                h.m = m->n;
-                h.n = P.d;
-                h.k = P.u;
-                h.a = P.delta;
-                h.lda = P.ld;
-                h.b = weights(P);
-                h.ldb = P.ld;
-                h.c = Q.delta;
-                h.ldc = Q.ld;
-                h.epi = RT_EPI_RELU_MASK;
-                h.mask = Q.act;
-                h.ldmask = Q.ld_act;
-                h.split_k = 1;
-                h.max_sms = backward_sms();
-                h.x3_ws = m->x3_ws;
-                h.x3_ws_bytes = m->x3_ws_bytes;
-                RT_TRY(run_gemm(m->ctx, h, st, 0));
-                RT_TRY(mark("dx_gemm_relu_mask", 2.0 * m->n * P.d * P.u));
+                RT_TRY(dx_gemm(l));
                 if (update) {
                     RT_CUDA(cudaEventRecord(P.ev_dx, st));
                     RT_CUDA(cudaStreamWaitEvent(m->opt_stream, P.ev_dx, 0));
@@ -430,6 +480,11 @@ struct Enqueuer {
     }
 };
 
+void set_fuse_opt(rt_mlp* m) {
+    const char* e = getenv("RTGPU_FUSED_OPT");
+    m->fuse_opt = !m->comm && m->cfg.optimizer != RT_OPT_NONE && !(e && e[0] == '0');
+}
+
 // Chunks of each layer's dW GEMM: the first layer always (its update would
 // otherwise trail the step), every layer under data parallelism (its
 // allreduce starts a chunk after the GEMM does); 4 chunks for >= 4096 rows,
@@ -442,7 +497,7 @@ int prepare_chunks(rt_mlp* m) {
         PlanLayer& P = m->L[l];
         const int64_t rows = P.d + 1;
         int ch = 1;
-        if (l == 0) ch = env0 && env0[0] ? atoi(env0) : rule(rows);
+        if (l == 0 && !m->fuse_opt) ch = env0 && env0[0] ? atoi(env0) : rule(rows);
         else if (m->comm) ch = envd && envd[0] ? atoi(envd) : rule(rows);
         if (ch < 1) ch = 1;
         if (ch > 8) ch = 8;
@@ -679,6 +734,7 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
         if ((s = dalloc(m, (void**)&m->x3_ws, need))) return bail(s);
         m->x3_ws_bytes = need;
     }
+    set_fuse_opt(m);
     if ((s = prepare_chunks(m))) return bail(s);
     if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) return bail(fail(RT_ERR_CUDA, "plan setup sync failed"));
     *out = m;
@@ -980,6 +1036,7 @@ int rt_mlp_set_comm(rt_mlp* m, rt_comm* comm) {
                 RT_TRY(dalloc(m, &p, (size_t)(P.d + 1) * P.ld * 2));
                 P.g16 = static_cast<__nv_bfloat16*>(p);
             }
+    set_fuse_opt(m);
     RT_TRY(prepare_chunks(m));
     // Sharded optimiser: bf16 plans (their GEMMs read only the bf16 weights)
     // with an optimiser, more than one rank, every chunk divisible by the

@@ -200,7 +200,8 @@ struct TcParams {
     int* err;
     OptFuse opt;
     int kb_seg;  // 3xTF32: k blocks per product segment (the k loop runs 3 * kb_seg blocks); 0 otherwise
-    int tma_store;  // through shared-memory staging and TMA stores: 1 = C, 2 = the split-K partials (0 = direct)
+    int tma_store;  // epilogue: 1 = C and 2 = split-K partials through shared-memory staging and TMA stores,
+                    // 3 = fused optimiser through the staging boxes (opt_chunk), 0 = direct stores
 };
 
 // Epilogue staging: one 32 x 32 output chunk per epilogue warp (4 KB), the
@@ -388,6 +389,94 @@ __device__ __forceinline__ void stage_and_store(const CUtensorMap* tmap_c, uint8
             tma_store_3d(tmap_c, smem_u32(box), (int32_t)col0, (int32_t)row0, split);
         bulk_commit();
     }
+}
+
+// Fused optimiser epilogue (tma_store == 3) for one warp's 32 x 32 chunk of a
+// dW tile: lane = row row0 + lane, v = its gradients in columns col0..col0+31.
+// The chunk is transposed through the warp's 4 KB box (element (r, c) at
+// r * 32 + (c ^ r), conflict-free for the row-per-lane writes and for the
+// reads below); then one warp instruction covers four 128-byte rows (lane l:
+// row 4 i + (l >> 3), columns 4 (l & 7) .. + 3), so the optimiser's reads of
+// theta / m / v and its writes of them, of the bf16 shadow and of the
+// gradient itself (C) are whole-line accesses.  Four rows' loads are issued
+// before the first store.  Rounding as the stand-alone kernels (adam_one /
+// sgd_one), so the update is bit-identical to theirs.
+__device__ __forceinline__ void opt_chunk(const TcParams& p, float* box, int lane, int64_t row0, int64_t col0,
+                                          const float (&v)[32]) {
+#pragma unroll
+    for (int c = 0; c < 32; ++c) box[lane * 32 + (c ^ lane)] = v[c];
+    __syncwarp();
+    const OptFuse& o = p.opt;
+    const bool adam = o.kind == 2;
+    const int cq = (lane & 7) * 4;
+    const int64_t col = col0 + cq;
+    float* C = static_cast<float*>(p.c);
+    const uintptr_t al = reinterpret_cast<uintptr_t>(o.theta) | reinterpret_cast<uintptr_t>(C) |
+                         (adam ? reinterpret_cast<uintptr_t>(o.m) | reinterpret_cast<uintptr_t>(o.v) : 0);
+    const bool fast = row0 + 32 <= p.m && col0 + 32 <= p.n && (p.ldc & 3) == 0 && (al & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(o.shadow) & 7) == 0;
+    if (fast) {
+        const float b1 = o.beta1, b2 = o.beta2;
+        const float omb1 = __fsub_rn(1.0f, b1), omb2 = __fsub_rn(1.0f, b2);
+        const float ic1 = adam ? o.sc->inv_c1 : 0.0f, ic2 = adam ? o.sc->inv_c2 : 0.0f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float g[4][4];
+            float4 th[4], mm[4], vv[4];
+            int64_t idx[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int rr = (h * 4 + u) * 4 + (lane >> 3);
+                idx[u] = (row0 + rr) * p.ldc + col;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) g[u][j] = box[rr * 32 + ((cq + j) ^ rr)];
+                th[u] = *reinterpret_cast<const float4*>(o.theta + idx[u]);
+                mm[u] = adam ? *reinterpret_cast<const float4*>(o.m + idx[u]) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                vv[u] = adam ? *reinterpret_cast<const float4*>(o.v + idx[u]) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                float t4[4] = {th[u].x, th[u].y, th[u].z, th[u].w};
+                float m4[4] = {mm[u].x, mm[u].y, mm[u].z, mm[u].w};
+                float v4[4] = {vv[u].x, vv[u].y, vv[u].z, vv[u].w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    t4[j] = adam ? adam_one(t4[j], g[u][j], m4[j], v4[j], b1, b2, omb1, omb2, ic1, ic2, o.eps, o.lr)
+                                 : sgd_one(t4[j], g[u][j], o.lr);
+                *reinterpret_cast<float4*>(o.theta + idx[u]) = make_float4(t4[0], t4[1], t4[2], t4[3]);
+                if (adam) {
+                    *reinterpret_cast<float4*>(o.m + idx[u]) = make_float4(m4[0], m4[1], m4[2], m4[3]);
+                    *reinterpret_cast<float4*>(o.v + idx[u]) = make_float4(v4[0], v4[1], v4[2], v4[3]);
+                }
+                if (o.shadow) {
+                    __nv_bfloat162 lo = __floats2bfloat162_rn(t4[0], t4[1]);
+                    __nv_bfloat162 hi = __floats2bfloat162_rn(t4[2], t4[3]);
+                    uint2 pk;
+                    pk.x = *reinterpret_cast<uint32_t*>(&lo);
+                    pk.y = *reinterpret_cast<uint32_t*>(&hi);
+                    *reinterpret_cast<uint2*>(o.shadow + idx[u]) = pk;
+                }
+                *reinterpret_cast<float4*>(C + idx[u]) = make_float4(g[u][0], g[u][1], g[u][2], g[u][3]);
+            }
+        }
+    } else {
+        // ragged edge of the output, or unaligned buffers: element by element
+#pragma unroll 1
+        for (int it = 0; it < 8; ++it) {
+            const int rr = it * 4 + (lane >> 3);
+            const int64_t row = row0 + rr;
+            if (row >= p.m) continue;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (col + j >= p.n) break;
+                float g = box[rr * 32 + ((cq + j) ^ rr)];
+                const int64_t i = row * p.ldc + col + j;
+                opt_apply_row<1>(o, i, &g, 1);
+                C[i] = g;
+            }
+        }
+    }
+    __syncwarp();  // the box is rewritten by the next chunk
 }
 
 // ------------------------------------------------------------------ host

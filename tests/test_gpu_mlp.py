@@ -285,6 +285,39 @@ def test_checkpoint_resume_is_bit_exact(gpu, tmp_path, dtype, opt, lr):
     assert b.save_state() == ref.save_state()
 
 
+@pytest.mark.parametrize("dtype,opt,lr,batch", [("bf16", "adam", 1e-3, 512), ("f32", "sgd", 0.01, 512),
+                                                ("f32", "adam", 1e-3, 512), ("bf16", "adam", 1e-3, 2048)])
+def test_fused_update_equals_separate_update(gpu, monkeypatch, dtype, opt, lr, batch):
+    # On one device the optimiser runs inside the dW GEMMs' epilogues (dX
+    # first, then dW + update); RTGPU_FUSED_OPT=0 runs the dW GEMMs plain and
+    # the update as its own kernels on a side stream.  Same arithmetic, same
+    # GEMMs: three steps agree bit for bit (weights, gradients, moments, loss).
+    # f32 at batch 512 and bf16 at 2048 split the narrow layers' dW GEMMs over
+    # k; there the split-K reduce kernel applies the update.
+    dims = [256, 512, 384, 10]
+    model, x, labels = baseline_inputs(dims, batch, 77)
+    gx, gy = gpu.upload(x), rgpu_b200.upload_labels(gpu, labels)
+    runs = {}
+    for fused in ("0", "1"):
+        monkeypatch.setenv("RTGPU_FUSED_OPT", fused)
+        mlp = rgpu_b200.GpuMlp.from_params(gpu, model.params(), batch, lr, dtype=dtype, optimizer=opt)
+        mlp.enable_timing(True)
+        for _ in range(3):
+            mlp.step(gx, gy)
+        gpu.sync()
+        labels_seen = [o[0] for o in mlp.op_times()]
+        runs[fused] = (mlp.weights(), mlp.grads(), mlp.save_state(), mlp.last_loss(), labels_seen)
+        mlp.close()
+    assert any(lab.startswith("dw_gemm_") for lab in runs["1"][4]), runs["1"][4]
+    assert not any(lab.startswith("dw_gemm_") for lab in runs["0"][4]), runs["0"][4]
+    for i, (a, b) in enumerate(zip(runs["0"][0], runs["1"][0])):
+        assert np.array_equal(a, b), f"weights {i}"
+    for i, (a, b) in enumerate(zip(runs["0"][1], runs["1"][1])):
+        assert np.array_equal(a, b), f"grads {i}"
+    assert runs["0"][2] == runs["1"][2]
+    assert runs["0"][3] == runs["1"][3]
+
+
 def test_checkpoint_rejects_another_architecture(gpu):
     model, x, labels = baseline_inputs([64, 128, 10], 32, 1)
     a = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 32, 1e-3, optimizer="adam")
