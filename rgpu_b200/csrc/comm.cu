@@ -31,6 +31,8 @@ struct NcclApi {
                                   cudaStream_t) = nullptr;
     ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     const char* (*GetErrorString)(ncclResult_t) = nullptr;
+    // optional (NCCL >= 2.18): a second communicator over the same ranks
+    ncclResult_t (*CommSplit)(ncclComm_t, int, int, ncclComm_t*, ncclConfig_t*) = nullptr;
 };
 
 NcclApi& nccl_api() {
@@ -53,6 +55,7 @@ NcclApi& nccl_api() {
         api.ReduceScatter = (decltype(api.ReduceScatter))dlsym(h, "ncclReduceScatter");
         api.AllGather = (decltype(api.AllGather))dlsym(h, "ncclAllGather");
         api.GetErrorString = (decltype(api.GetErrorString))dlsym(h, "ncclGetErrorString");
+        api.CommSplit = (decltype(api.CommSplit))dlsym(h, "ncclCommSplit");
         if (!api.GetUniqueId || !api.CommInitRank || !api.CommDestroy || !api.AllReduce || !api.ReduceScatter ||
             !api.AllGather || !api.GetErrorString) {
             api.error = "libnccl.so.2 lacks a required symbol";
@@ -74,6 +77,7 @@ int need_nccl() {
 struct rt_comm {
     rt_ctx* ctx = nullptr;
     ncclComm_t nccl = nullptr;
+    ncclComm_t nccl2 = nullptr;  // second communicator (comm_open_second), its own queue of collectives
     int rank = 0, world = 1;
 };
 
@@ -88,6 +92,26 @@ int comm_allreduce(rt_comm* comm, float* buf, int64_t count, cudaStream_t st) {
 }
 
 int comm_rank(const rt_comm* comm) { return comm ? comm->rank : 0; }
+
+// Opens the second communicator over the same ranks (ncclCommSplit, one
+// color): collectives issued on it queue separately from the first's, so the
+// sharded optimiser's weight all-gathers do not wait behind gradient
+// reduce-scatters or hold them up.  Collective: every rank calls it.  Returns
+// false (and the caller keeps one queue) when NCCL has no ncclCommSplit.
+bool comm_open_second(rt_comm* comm, int* status) {
+    *status = RT_OK;
+    if (!comm) return false;
+    if (comm->nccl2) return true;
+    NcclApi& A = nccl_api();
+    if (!A.CommSplit) return false;
+    ncclResult_t r = A.CommSplit(comm->nccl, 0, comm->rank, &comm->nccl2, nullptr);
+    if (r != ncclSuccess) {
+        comm->nccl2 = nullptr;
+        *status = fail(RT_ERR_NCCL, "ncclCommSplit failed: %s", A.GetErrorString(r));
+        return false;
+    }
+    return true;
+}
 int comm_world(const rt_comm* comm) { return comm ? comm->world : 1; }
 
 // In place: buf holds world * count elements; rank r's slice
@@ -103,12 +127,13 @@ int comm_reduce_scatter(rt_comm* comm, float* buf, int64_t count, cudaStream_t s
 
 // In place: rank r's slice [r * count, (r + 1) * count) of buf is copied to
 // the same slice of every rank's buf (elem_bytes 2 for bf16, 4 for f32).
-int comm_all_gather(rt_comm* comm, void* buf, int64_t count, int elem_bytes, cudaStream_t st) {
+int comm_all_gather(rt_comm* comm, void* buf, int64_t count, int elem_bytes, cudaStream_t st, bool second) {
     if (!comm || count == 0) return RT_OK;
     NcclApi& A = nccl_api();
     char* b = static_cast<char*>(buf);
+    ncclComm_t nc = second && comm->nccl2 ? comm->nccl2 : comm->nccl;
     ncclResult_t r = A.AllGather(b + (int64_t)comm->rank * count * elem_bytes, b, (size_t)count,
-                                 elem_bytes == 2 ? ncclBfloat16 : ncclFloat32, comm->nccl, st);
+                                 elem_bytes == 2 ? ncclBfloat16 : ncclFloat32, nc, st);
     if (r != ncclSuccess) return fail(RT_ERR_NCCL, "ncclAllGather failed: %s", A.GetErrorString(r));
     return RT_OK;
 }
@@ -162,6 +187,7 @@ int rt_comm_init(rt_ctx* ctx, int rank, int world, const unsigned char id[128], 
 
 int rt_comm_destroy(rt_comm* c) {
     if (!c) return RT_OK;
+    if (c->nccl2) nccl_api().CommDestroy(c->nccl2);
     if (c->nccl) nccl_api().CommDestroy(c->nccl);
     delete c;
     return RT_OK;

@@ -39,7 +39,8 @@ int run_gemm(rt_ctx* ctx, GemmDesc g, cudaStream_t stream, size_t ws_bytes);
 int comm_allreduce(rt_comm* comm, float* buf, int64_t count, cudaStream_t st);
 int comm_allreduce_bf16(rt_comm* comm, __nv_bfloat16* buf, int64_t count, cudaStream_t st);
 int comm_reduce_scatter(rt_comm* comm, float* buf, int64_t count, cudaStream_t st);
-int comm_all_gather(rt_comm* comm, void* buf, int64_t count, int elem_bytes, cudaStream_t st);
+int comm_all_gather(rt_comm* comm, void* buf, int64_t count, int elem_bytes, cudaStream_t st, bool second = false);
+bool comm_open_second(rt_comm* comm, int* status);
 int comm_rank(const rt_comm* comm);
 int comm_world(const rt_comm* comm);
 }  // namespace rt
@@ -141,6 +142,9 @@ struct rt_mlp {
     // save_state, then collective).
     bool sharded = false;
     int rank = 0, world = 1;
+    // the weight all-gathers' own stream and NCCL communicator (when NCCL can
+    // split one off); otherwise they share the comm stream
+    cudaStream_t ag_stream = nullptr;
     // per-layer optimiser on a side stream, overlapping the remaining backward GEMMs
     cudaStream_t opt_stream = nullptr;
 };
@@ -189,6 +193,7 @@ void free_all(rt_mlp* m) {
         if (P.ev_dx) cudaEventDestroy(P.ev_dx);
     }
     if (m->comm_stream) cudaStreamDestroy(m->comm_stream);
+    if (m->ag_stream) cudaStreamDestroy(m->ag_stream);
     if (m->opt_stream) cudaStreamDestroy(m->opt_stream);
     if (m->copy_stream) cudaStreamDestroy(m->copy_stream);
     for (void* p : m->allocs) cudaFree(p);
@@ -348,14 +353,25 @@ struct Enqueuer {
         return launch_cast(m->ctx, h, RT_BF16, P.ld, P.g + r0 * P.ld, RT_F32, P.ld, r1 - r0, P.ld, cs);
     }
 
+    // Sharded optimiser: the all-gathers of every chunk of layer P (l > 0),
+    // each after this rank's update of its slice of the chunk.
+    int gather_layer(PlanLayer& P) {
+        if (!m->sharded || m->cfg.optimizer == RT_OPT_NONE) return RT_OK;
+        for (int c = 0; c < P.chunks; ++c)
+            RT_TRY(gather_weights(P, c, chunk_row_of(P.d + 1, P.chunks, c), chunk_row_of(P.d + 1, P.chunks, c + 1)));
+        return RT_OK;
+    }
+
     // Sharded optimiser: once this rank has updated its slice of chunk c, the
     // chunk's bf16 weights are all-gathered on the comm stream.
     int gather_weights(PlanLayer& P, int c, int64_t r0, int64_t r1) {
         if (!m->sharded) return RT_OK;
-        RT_CUDA(cudaStreamWaitEvent(m->comm_stream, P.ev_opt[c], 0));
+        if (!m->ag_stream) RT_CUDA(cudaStreamWaitEvent(m->comm_stream, P.ev_opt[c], 0));
+        cudaStream_t as = m->ag_stream ? m->ag_stream : m->comm_stream;
+        if (m->ag_stream) RT_CUDA(cudaStreamWaitEvent(as, P.ev_opt[c], 0));
         const int64_t e = shard_end(P, r1);
-        if (e > r0) RT_TRY(comm_all_gather(m->comm, P.w16 + r0 * P.ld, (e - r0) * P.ld / m->world, 2, m->comm_stream));
-        RT_CUDA(cudaEventRecord(P.ev_ag[c], m->comm_stream));
+        if (e > r0) RT_TRY(comm_all_gather(m->comm, P.w16 + r0 * P.ld, (e - r0) * P.ld / m->world, 2, as, m->ag_stream != nullptr));
+        RT_CUDA(cudaEventRecord(P.ev_ag[c], as));
         return RT_OK;
     }
 
@@ -451,6 +467,11 @@ struct Enqueuer {
                     RT_TRY(gather_weights(P, c, r0, r1));
                 }
             }
+            // Sharded optimiser: the previous layer's weight all-gathers go on
+            // the comm stream only now, behind this layer's reduce-scatters.
+            // Enqueued earlier, they would hold this layer's gradient sums
+            // until the previous layer's dX GEMM and updates were done.
+            if (l + 1 < nl && !m->ag_stream) RT_TRY(gather_layer(m->L[l + 1]));
             if (l > 0) {
                 RT_TRY(dx_gemm(l));
                 if (update) {
@@ -461,8 +482,8 @@ struct Enqueuer {
                         if (m->comm) RT_CUDA(cudaStreamWaitEvent(m->opt_stream, P.ev_comm[c], 0));
                         RT_TRY(enqueue_update_rows(m, P, r0, r1, m->opt_stream));
                         RT_CUDA(cudaEventRecord(P.ev_opt[c], m->opt_stream));
-                        RT_TRY(gather_weights(P, c, r0, r1));
                     }
+                    if (m->ag_stream) RT_TRY(gather_layer(P));  // own queue: right away
                 }
             }
         }
@@ -486,9 +507,11 @@ void set_fuse_opt(rt_mlp* m) {
 }
 
 // Chunks of each layer's dW GEMM: the first layer always (its update would
-// otherwise trail the step), every layer under data parallelism (its
-// allreduce starts a chunk after the GEMM does); 4 chunks for >= 4096 rows,
-// 2 for >= 2048.  RTGPU_FIRST_LAYER_CHUNKS / RTGPU_DW_CHUNKS override.
+// otherwise trail the step), and under data parallelism every layer with at
+// least 128 MB of gradients (its sum starts a chunk after the GEMM does;
+// smaller layers lose more to the narrower GEMMs than the overlap gains); 4
+// chunks for >= 4096 rows, 2 for >= 2048.  RTGPU_FIRST_LAYER_CHUNKS /
+// RTGPU_DW_CHUNKS override.
 int prepare_chunks(rt_mlp* m) {
     auto rule = [](int64_t rows) { return rows >= 4096 ? 4 : rows >= 2048 ? 2 : 1; };
     const char* env0 = getenv("RTGPU_FIRST_LAYER_CHUNKS");
@@ -498,7 +521,7 @@ int prepare_chunks(rt_mlp* m) {
         const int64_t rows = P.d + 1;
         int ch = 1;
         if (l == 0 && !m->fuse_opt) ch = env0 && env0[0] ? atoi(env0) : rule(rows);
-        else if (m->comm) ch = envd && envd[0] ? atoi(envd) : rule(rows);
+        else if (m->comm) ch = envd && envd[0] ? atoi(envd) : rows * P.ld * 4 >= (128ll << 20) ? rule(rows) : 1;
         if (ch < 1) ch = 1;
         if (ch > 8) ch = 8;
         while (ch > 1 && chunk_row_of(rows, ch, 1) == 0) --ch;  // every chunk non-empty
@@ -549,7 +572,7 @@ int capture_step(rt_mlp* m, int s) {
     }
     if (e != cudaSuccess) return fail(RT_ERR_CUDA, "step capture failed: %s", cudaGetErrorString(e));
     S.graph = graph;
-    RT_CUDA(cudaGraphInstantiate(&S.exec, graph, 0));
+    RT_CUDA(cudaGraphInstantiate(&S.exec, graph, cudaGraphInstantiateFlagUseNodePriority));
     m->kernels_per_step = (int)(m->ctx->launches - before);
     S.timed = m->timing;
     return RT_OK;
@@ -1024,7 +1047,14 @@ int rt_mlp_set_comm(rt_mlp* m, rt_comm* comm) {
     const char* r = getenv("RTGPU_COMM_SM_RESERVE");
     m->comm_sm_reserve = r ? (atoi(r) + 1) / 2 * 2 : 16;
     if (m->comm_sm_reserve < 0 || m->comm_sm_reserve >= m->ctx->sm_count) m->comm_sm_reserve = 0;
-    if (comm && !m->comm_stream) RT_CUDA(cudaStreamCreateWithFlags(&m->comm_stream, cudaStreamNonBlocking));
+    if (comm && !m->comm_stream) {
+        // The collectives get the highest stream priority: when SMs free up
+        // during backward, NCCL's blocks are dispatched before the update
+        // kernels' (the step graph keeps per-node priorities).
+        int least = 0, greatest = 0;
+        RT_CUDA(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+        RT_CUDA(cudaStreamCreateWithPriority(&m->comm_stream, cudaStreamNonBlocking, greatest));
+    }
     // RTGPU_GRAD_COMM=bf16: bf16 plans sum their gradients in bf16 (half the
     // NVLink bytes; the parity bar of bf16 plans is 2e-2)
     const char* gc = getenv("RTGPU_GRAD_COMM");
@@ -1053,6 +1083,16 @@ int rt_mlp_set_comm(rt_mlp* m, rt_comm* comm) {
             if (e > r0 && ((e - r0) * P.ld) % m->world) sharded = false;
         }
     m->sharded = sharded;
+    if (sharded && !m->ag_stream) {
+        // Collective: every rank reaches this with the same plan shape.
+        int st = RT_OK;
+        if (comm_open_second(comm, &st)) {
+            int least = 0, greatest = 0;
+            RT_CUDA(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+            RT_CUDA(cudaStreamCreateWithPriority(&m->ag_stream, cudaStreamNonBlocking, greatest));
+        }
+        RT_TRY(st);
+    }
     m->ops.clear();
     drop_graphs(m);
     return RT_OK;
