@@ -290,8 +290,17 @@ int rt_mlp_op_time(rt_mlp* mlp, int i, const char** label, double* flops, float*
  * sharded plan rt_mlp_weights, rt_mlp_grads and rt_mlp_save_state first
  * all-gather the f32 state, so every rank must call them together. */
 int rt_mlp_set_comm(rt_mlp* mlp, rt_comm* comm);
-/* How the attached communicator sums gradients (rt_comm_mode). */
-typedef enum { RT_COMM_NONE = 0, RT_COMM_ALLREDUCE = 1, RT_COMM_ALLREDUCE_BF16 = 2, RT_COMM_SHARDED_OPT = 3 } rt_comm_mode;
+/* How the attached communicator sums gradients (rt_comm_mode).
+ * RT_COMM_SHARDED_P2P: sharded optimiser whose dW GEMMs (some or all layers)
+ * scatter their rows to the owning ranks over NVLink peer memory from the
+ * GEMM epilogue instead of an NCCL reduce-scatter (RTGPU_P2P_RS=1). */
+typedef enum {
+    RT_COMM_NONE = 0,
+    RT_COMM_ALLREDUCE = 1,
+    RT_COMM_ALLREDUCE_BF16 = 2,
+    RT_COMM_SHARDED_OPT = 3,
+    RT_COMM_SHARDED_P2P = 4
+} rt_comm_mode;
 int rt_mlp_comm_mode(rt_mlp* mlp, int* mode);
 
 /* ------------------------------------------------------ autodiff tape */

@@ -14,6 +14,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "internal.h"
 
@@ -143,6 +144,95 @@ int comm_allreduce_bf16(rt_comm* comm, __nv_bfloat16* buf, int64_t count, cudaSt
     NcclApi& A = nccl_api();
     ncclResult_t r = A.AllReduce(buf, buf, (size_t)count, ncclBfloat16, ncclSum, comm->nccl, st);
     if (r != ncclSuccess) return fail(RT_ERR_NCCL, "ncclAllReduce (bf16) failed: %s", A.GetErrorString(r));
+    return RT_OK;
+}
+
+// Maps a local device allocation (the base of a cudaMalloc block) of every
+// rank into this process: peers[q] = rank q's block (peers[rank] = local).
+// The CUDA IPC handles travel by an in-place ncclAllGather.  Collective.
+// Fails (RT_ERR_UNSUPPORTED) when a peer's block cannot be mapped; the
+// caller then keeps NCCL for that exchange.
+int comm_share_buffer(rt_comm* comm, void* local, void** peers) {
+    RT_CHECK(comm && local && peers && comm->world <= kMaxPeers, "comm_share_buffer: bad arguments");
+    NcclApi& A = nccl_api();
+    cudaStream_t st = comm->ctx->stream;
+    const int W = comm->world;
+    // Every rank reaches the all-gather whatever happens before it, so that
+    // a local failure cannot leave the other ranks waiting in the collective.
+    cudaIpcMemHandle_t mine;
+    std::memset(&mine, 0, sizeof(mine));
+    int rc = RT_OK;
+    if (cudaIpcGetMemHandle(&mine, local) != cudaSuccess) rc = fail(RT_ERR_UNSUPPORTED, "cudaIpcGetMemHandle failed");
+    uint8_t* dev = nullptr;
+    RT_CUDA(cudaMalloc(&dev, sizeof(cudaIpcMemHandle_t) * W));
+    std::vector<cudaIpcMemHandle_t> all(W);
+    if (cudaMemcpyAsync(dev + sizeof(mine) * comm->rank, &mine, sizeof(mine), cudaMemcpyHostToDevice, st) !=
+        cudaSuccess && rc == RT_OK)
+        rc = fail(RT_ERR_CUDA, "comm_share_buffer: handle upload failed");
+    ncclResult_t r = A.AllGather(dev + sizeof(mine) * comm->rank, dev, sizeof(mine), ncclUint8, comm->nccl, st);
+    if (r != ncclSuccess && rc == RT_OK) rc = fail(RT_ERR_NCCL, "ncclAllGather (IPC handles) failed: %s", A.GetErrorString(r));
+    if ((cudaMemcpyAsync(all.data(), dev, sizeof(mine) * W, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+         cudaStreamSynchronize(st) != cudaSuccess) && rc == RT_OK)
+        rc = fail(RT_ERR_CUDA, "comm_share_buffer: handle download failed");
+    cudaFree(dev);
+    RT_TRY(rc);
+    for (int q = 0; q < W; ++q) peers[q] = nullptr;
+    peers[comm->rank] = local;
+    for (int q = 0; q < W; ++q) {
+        if (q == comm->rank) continue;
+        cudaError_t e = cudaIpcOpenMemHandle(&peers[q], all[q], cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            peers[q] = nullptr;
+            comm_unshare_buffer(comm, peers);
+            return fail(RT_ERR_UNSUPPORTED, "cannot map rank %d's buffer: %s", q, cudaGetErrorString(e));
+        }
+    }
+    return RT_OK;
+}
+
+// Closes the mappings comm_share_buffer opened (not the local block).
+void comm_unshare_buffer(rt_comm* comm, void** peers) {
+    if (!comm || !peers) return;
+    for (int q = 0; q < comm->world; ++q)
+        if (q != comm->rank && peers[q]) {
+            cudaIpcCloseMemHandle(peers[q]);
+            peers[q] = nullptr;
+        }
+}
+
+// True on every rank when `mine` is true on every rank (an in-place
+// ncclAllReduce(min) of one int on `scratch`, synchronised).  Collective.
+bool comm_all_true(rt_comm* comm, bool mine, float* scratch, int* status) {
+    *status = RT_OK;
+    NcclApi& A = nccl_api();
+    cudaStream_t st = comm->ctx->stream;
+    int v = mine ? 1 : 0;
+    int* dv = reinterpret_cast<int*>(scratch);
+    if (cudaMemcpyAsync(dv, &v, sizeof(v), cudaMemcpyHostToDevice, st) != cudaSuccess) {
+        *status = fail(RT_ERR_CUDA, "comm_all_true: upload failed");
+        v = 0;
+    }
+    ncclResult_t r = A.AllReduce(dv, dv, 1, ncclInt32, ncclMin, comm->nccl, st);
+    if (r != ncclSuccess) {
+        *status = fail(RT_ERR_NCCL, "ncclAllReduce (agreement) failed: %s", A.GetErrorString(r));
+        return false;
+    }
+    if (cudaMemcpyAsync(&v, dv, sizeof(v), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess) {
+        *status = fail(RT_ERR_CUDA, "comm_all_true: download failed");
+        return false;
+    }
+    return v == 1;
+}
+
+// A barrier in stream order: a one-float ncclAllReduce on `scratch`.  Work
+// enqueued on `st` after it runs once every rank has reached it, so device
+// writes that each rank finished before its barrier (peer-memory stores
+// included) are in place.
+int comm_barrier(rt_comm* comm, float* scratch, cudaStream_t st) {
+    NcclApi& A = nccl_api();
+    ncclResult_t r = A.AllReduce(scratch, scratch, 1, ncclFloat32, ncclSum, comm->nccl, st);
+    if (r != ncclSuccess) return fail(RT_ERR_NCCL, "ncclAllReduce (barrier) failed: %s", A.GetErrorString(r));
     return RT_OK;
 }
 

@@ -293,6 +293,31 @@ __global__ void __launch_bounds__(kOptThreads) sgd_kernel(OptBatch batch, float 
     }
 }
 
+// out[i] = in[i] + in[q_stride + i] + ... + in[(parts - 1) q_stride + i], summed
+// in that order (the owner's side of the peer-memory reduce-scatter: one
+// partial per source rank), 16-byte accesses where the buffers allow.
+__global__ void sum_partials_kernel(float* __restrict__ out, const float* __restrict__ in, int64_t q_stride,
+                                    int parts, int64_t n, bool vec) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t nv = vec ? n / 4 : 0;
+    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nv; q += stride) {
+        float4 acc = reinterpret_cast<const float4*>(in)[q];
+        for (int r = 1; r < parts; ++r) {
+            const float4 x = reinterpret_cast<const float4*>(in + r * q_stride)[q];
+            acc.x = __fadd_rn(acc.x, x.x);
+            acc.y = __fadd_rn(acc.y, x.y);
+            acc.z = __fadd_rn(acc.z, x.z);
+            acc.w = __fadd_rn(acc.w, x.w);
+        }
+        reinterpret_cast<float4*>(out)[q] = acc;
+    }
+    for (int64_t i = nv * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        float acc = in[i];
+        for (int r = 1; r < parts; ++r) acc = __fadd_rn(acc, in[r * q_stride + i]);
+        out[i] = acc;
+    }
+}
+
 __global__ void axpy_kernel(float* dst, int64_t ldd, const float* src, int64_t lds, int64_t rows, int64_t cols) {
     int64_t total = rows * cols;
     for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
@@ -458,6 +483,17 @@ int launch_axpy_inplace(rt_ctx* ctx, float* dst, int64_t ldd, const float* src, 
                         int64_t cols, cudaStream_t st) {
     if (rows * cols == 0) return RT_OK;
     axpy_kernel<<<grid_for(ctx, rows * cols), 256, 0, st>>>(dst, ldd, src, lds, rows, cols);
+    count_launch(ctx);
+    RT_CUDA(cudaGetLastError());
+    return RT_OK;
+}
+
+int launch_sum_partials(rt_ctx* ctx, float* out, const float* in, int64_t q_stride, int parts, int64_t n,
+                        cudaStream_t st) {
+    if (n == 0) return RT_OK;
+    const bool vec = ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(in)) & 15) == 0 &&
+                     (q_stride & 3) == 0;
+    sum_partials_kernel<<<grid_for(ctx, vec ? n / 4 + 1 : n), 256, 0, st>>>(out, in, q_stride, parts, n, vec);
     count_launch(ctx);
     RT_CUDA(cudaGetLastError());
     return RT_OK;

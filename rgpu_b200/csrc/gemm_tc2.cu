@@ -340,6 +340,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
                         if (row < p.m) epilogue_math<float>(p, row, col0, v);
                         stage_and_store<float>(&tmap_c, box, lane, row0, col0, v);
                     }
+                } else if (p.tma_store == 4) {
+                    // rows scattered to their owners' receive buffers (peer memory)
+                    p2p_chunk(p, reinterpret_cast<float*>(smem_epi + (warp - 4) * kStageBytes), lane, row0, col0, v);
                 } else if (p.tma_store == 3) {
                     // fused optimiser: the chunk updates theta / m / v / shadow and is stored as C
                     opt_chunk(p, reinterpret_cast<float*>(smem_epi + (warp - 4) * kStageBytes), lane, row0, col0, v);
@@ -375,6 +378,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
             raise_abort();
         }
         if ((p.tma_store == 1 || p.tma_store == 2) && lane == 0) bulk_wait_all();  // this warp's output stores are complete
+        if (p.tma_store == 4) __threadfence_system();  // peer-memory stores in place before the kernel ends
     }
 
     __syncwarp();
@@ -448,8 +452,14 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X
     p.err = ctx->dev_err;
     p.opt = g.opt;
     p.tma_store = 0;
+    p.p2p = g.p2p;
     tc = ta;  // unused unless a staged store is chosen
-    if (ctx->tma_store && splits == 1 && !g.opt.kind) {
+    if (g.p2p.world > 0) {
+        // scattered over peer memory: one k slice, f32 gradient, no fused update
+        if (splits != 1 || p.out_bf16 || g.opt.kind)
+            return fail(RT_ERR_UNSUPPORTED, "peer-scatter GEMM needs one k slice, f32 output and no fused update");
+        p.tma_store = 4;
+    } else if (ctx->tma_store && splits == 1 && !g.opt.kind) {
         p.tma_store = 1;
         RT_TRY(make_tmap_out(&tc, g.c, p.out_bf16 != 0, g.m, g.n, g.ldc));
     } else if (ctx->tma_store && splits == 1 && !p.out_bf16) {

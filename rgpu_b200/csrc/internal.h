@@ -81,6 +81,20 @@ namespace rt {
 
 // ------------------------------------------------------------- kernels
 // GEMM problem in "logical" form: C[m,n] = op(A)[m,k] * op(B)[k,n].
+constexpr int kMaxPeers = 8;
+
+// dW GEMM output scattered to its owners over peer memory (the sharded
+// optimiser's reduce-scatter done by the GEMM epilogue): launch row i < owned_end
+// belongs to rank o = i / rows_owned and is stored, as this rank's partial, at
+//   peer[o][rank * q_stride + (base_row + i - o * rows_owned) * ld + column]
+// in rank o's receive buffer; rows >= owned_end (the bias row) go to C as usual.
+// world == 0: off.
+struct P2PScatter {
+    float* peer[kMaxPeers];
+    int rank, world;
+    int64_t rows_owned, owned_end, base_row, q_stride, ld;
+};
+
 struct GemmDesc {
     rt_layout layout;
     rt_dtype in_dtype, out_dtype;
@@ -98,7 +112,15 @@ struct GemmDesc {
     float* x3_ws;      // hi/lo operand copies for the 3xTF32 GEMM (null = context scratch)
     size_t x3_ws_bytes;
     bool no_alloc;     // the call may not allocate device memory (3xTF32 then needs a ready workspace)
+    P2PScatter p2p;    // world > 0: the epilogue scatters rows to their owners (tensor-core path, one k slice)
 };
+
+// Peer memory of a communicator's ranks (comm.cu).
+int comm_share_buffer(rt_comm* comm, void* local, void** peers);
+void comm_unshare_buffer(rt_comm* comm, void** peers);
+int comm_barrier(rt_comm* comm, float* scratch, cudaStream_t st);
+bool comm_all_true(rt_comm* comm, bool mine, float* scratch, int* status);
+bool gemm_p2p_capable(const rt_ctx* ctx, const GemmDesc& g);
 
 // Kernel launchers: enqueue on `stream`, return RT_OK or an error code.
 int launch_gemm_simt(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream);
@@ -152,6 +174,9 @@ int launch_relu_bwd(rt_ctx* ctx, const void* a, void* dz, rt_dtype dt, int64_t r
                     int64_t lda, int64_t ldz, cudaStream_t stream);
 int launch_cast(rt_ctx* ctx, const void* src, rt_dtype sdt, int64_t lds, void* dst, rt_dtype ddt,
                 int64_t ldd, int64_t rows, int64_t cols, cudaStream_t stream);
+// out[i] = sum over r < parts, in order, of in[r * q_stride + i], i < n.
+int launch_sum_partials(rt_ctx* ctx, float* out, const float* in, int64_t q_stride, int parts, int64_t n,
+                        cudaStream_t stream);
 // Sets column `col` of a [rows, ld] matrix to `value` (the ones column that
 // turns the dW GEMM into a dW + db GEMM).
 int launch_fill_column(rt_ctx* ctx, void* p, rt_dtype dt, int64_t rows, int64_t ld, int64_t col, float value,

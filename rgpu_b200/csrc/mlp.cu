@@ -81,6 +81,13 @@ struct PlanLayer {
     int chunks = 1;
     std::vector<cudaEvent_t> ev_ready, ev_comm, ev_opt, ev_ag;
     cudaEvent_t ev_dx = nullptr;
+    // Peer-memory reduce-scatter (sharded optimiser, RTGPU_P2P_RS=1): the dW
+    // GEMM's epilogue stores each weight row to its owner's receive buffer
+    // `recv` ([world][d / world][ld] f32: one region per source rank), mapped
+    // into this process for every rank at peers[q].
+    bool p2p = false;
+    float* recv = nullptr;
+    void* peers[kMaxPeers] = {};
 };
 
 struct Slot {
@@ -145,6 +152,7 @@ struct rt_mlp {
     // the weight all-gathers' own stream and NCCL communicator (when NCCL can
     // split one off); otherwise they share the comm stream
     cudaStream_t ag_stream = nullptr;
+    float* scratch = nullptr;  // one word for barriers and agreement collectives
     // per-layer optimiser on a side stream, overlapping the remaining backward GEMMs
     cudaStream_t opt_stream = nullptr;
 };
@@ -177,8 +185,18 @@ void drop_graphs(rt_mlp* m) {
     }
 }
 
+// Unmaps the peers' receive buffers of every peer-scatter layer.
+void teardown_p2p(rt_mlp* m) {
+    for (PlanLayer& P : m->L)
+        if (P.p2p) {
+            comm_unshare_buffer(m->comm, P.peers);
+            P.p2p = false;
+        }
+}
+
 void free_all(rt_mlp* m) {
     drop_graphs(m);
+    teardown_p2p(m);
     for (auto& s : m->slot) {
         if (s.ready) cudaEventDestroy(s.ready);
         if (s.free_) cudaEventDestroy(s.free_);
@@ -294,6 +312,34 @@ struct Enqueuer {
     // [dW_l; db_l] rows [r0, r1) = ([A_{l-1}, 1] columns r0..r1)^T delta_l (TN, K = batch), f32.
     int dw_gemm_rows(PlanLayer& P, int l, int64_t r0, int64_t r1) {
         const int64_t rows = P.d + 1;
+        GemmDesc g = dw_desc(P, l, r0, r1);
+        if (P.p2p) {
+            // weight rows go to their owners' receive buffers, the bias row to g
+            const int64_t e = shard_end(P, r1);
+            RT_CHECK(e > r0 && (e - r0) % m->world == 0 && m->world <= kMaxPeers, "peer-scatter chunk [%lld, %lld)",
+                     (long long)r0, (long long)e);
+            for (int q = 0; q < m->world; ++q) {
+                RT_CHECK(P.peers[q] != nullptr, "peer-scatter layer without rank %d's buffer", q);
+                g.p2p.peer[q] = static_cast<float*>(P.peers[q]);
+            }
+            g.p2p.rank = m->rank;
+            g.p2p.world = m->world;
+            g.p2p.rows_owned = (e - r0) / m->world;
+            g.p2p.owned_end = e - r0;
+            g.p2p.base_row = r0 / m->world;
+            g.p2p.q_stride = P.d / m->world * P.ld;
+            g.p2p.ld = P.ld;
+        }
+        RT_TRY(run_gemm(m->ctx, g, st, P.ws_bytes));
+        // FLOPs of the weight rows (the bias row is not counted, as everywhere)
+        const char* label = !m->fuse_opt ? "dw_gemm"
+                            : m->cfg.optimizer == RT_OPT_ADAM ? "dw_gemm_adam"
+                                                              : "dw_gemm_sgd";
+        return mark(label, 2.0 * m->n * (double)(r1 - r0 - (r1 == rows ? 1 : 0)) * P.u);
+    }
+
+    // The [dW; db] rows [r0, r1) GEMM of layer l, as dw_gemm_rows launches it.
+    GemmDesc dw_desc(PlanLayer& P, int l, int64_t r0, int64_t r1) const {
         GemmDesc g{};
         g.layout = RT_TN;
         g.in_dtype = m->adt;
@@ -327,12 +373,7 @@ struct Enqueuer {
             g.opt.beta2 = m->cfg.beta2;
             g.opt.eps = m->cfg.eps;
         }
-        RT_TRY(run_gemm(m->ctx, g, st, P.ws_bytes));
-        // FLOPs of the weight rows (the bias row is not counted, as everywhere)
-        const char* label = !m->fuse_opt ? "dw_gemm"
-                            : m->cfg.optimizer == RT_OPT_ADAM ? "dw_gemm_adam"
-                                                              : "dw_gemm_sgd";
-        return mark(label, 2.0 * m->n * (double)(r1 - r0 - (r1 == rows ? 1 : 0)) * P.u);
+        return g;
     }
 
     // Sums gradient rows [r0, r1) over the ranks on the comm stream (in bf16 when
@@ -340,6 +381,19 @@ struct Enqueuer {
     int allreduce_rows(PlanLayer& P, int64_t r0, int64_t r1) {
         cudaStream_t cs = m->comm_stream;
         const int64_t count = (r1 - r0) * P.ld;
+        if (P.p2p) {
+            // Every rank's GEMM has stored its partials of this chunk into the
+            // owners' receive buffers once all ranks pass the barrier; the
+            // owner then sums them, source rank by source rank, into its
+            // slice of g.
+            const int64_t e = shard_end(P, r1), h = (e - r0) / m->world;
+            RT_TRY(comm_barrier(m->comm, m->scratch, cs));
+            if (e > r0)
+                RT_TRY(launch_sum_partials(m->ctx, P.g + (r0 + (int64_t)m->rank * h) * P.ld,
+                                           P.recv + r0 / m->world * P.ld, P.d / m->world * P.ld, m->world, h * P.ld, cs));
+            if (r1 > P.d) RT_TRY(comm_allreduce(m->comm, P.db, P.ld, cs));
+            return RT_OK;
+        }
         if (m->sharded) {
             const int64_t e = shard_end(P, r1);
             if (e > r0) RT_TRY(comm_reduce_scatter(m->comm, P.g + r0 * P.ld, (e - r0) * P.ld / m->world, cs));
@@ -504,6 +558,40 @@ struct Enqueuer {
 void set_fuse_opt(rt_mlp* m) {
     const char* e = getenv("RTGPU_FUSED_OPT");
     m->fuse_opt = !m->comm && m->cfg.optimizer != RT_OPT_NONE && !(e && e[0] == '0');
+}
+
+// Peer-memory reduce-scatter for the sharded optimiser (RTGPU_P2P_RS=1):
+// every layer whose dW chunks take the one-slice tensor-core GEMM and split
+// into equal row ranges per rank gets a receive buffer, mapped into every
+// rank's process; its dW GEMM then scatters rows to their owners itself and
+// the layer's NCCL reduce-scatters become a barrier plus the owner's sum.
+// Collective: every rank takes the same decisions in the same order, and a
+// layer whose buffers some rank could not map stays on NCCL everywhere.
+int setup_p2p(rt_mlp* m) {
+    const char* e = getenv("RTGPU_P2P_RS");
+    if (!m->sharded || !(e && e[0] == '1') || m->world > kMaxPeers) return RT_OK;
+    Enqueuer q{m, m->ctx->stream, 0, false};
+    for (size_t l = 0; l < m->L.size(); ++l) {
+        PlanLayer& P = m->L[l];
+        bool ok = P.d % m->world == 0;
+        for (int c = 0; ok && c < P.chunks; ++c) {
+            const int64_t r0 = chunk_row_of(P.d + 1, P.chunks, c), r1 = chunk_row_of(P.d + 1, P.chunks, c + 1);
+            const int64_t end = shard_end(P, r1);
+            ok = end > r0 && (end - r0) % m->world == 0 && gemm_p2p_capable(m->ctx, q.dw_desc(P, (int)l, r0, r1));
+        }
+        if (!ok) continue;
+        if (!P.recv) RT_TRY(dalloc_t(m, &P.recv, (size_t)P.d * P.ld));
+        const int shared = comm_share_buffer(m->comm, P.recv, P.peers);
+        int st = RT_OK;
+        const bool everywhere = comm_all_true(m->comm, shared == RT_OK, m->scratch, &st);
+        RT_TRY(st);
+        if (!everywhere) {
+            if (shared == RT_OK) comm_unshare_buffer(m->comm, P.peers);
+            continue;
+        }
+        P.p2p = true;
+    }
+    return RT_OK;
 }
 
 // Chunks of each layer's dW GEMM: the first layer always (its update would
@@ -1031,7 +1119,10 @@ int rt_mlp_op_time(rt_mlp* m, int i, const char** label, double* flops, float* m
 
 int rt_mlp_comm_mode(rt_mlp* m, int* mode) {
     RT_CHECK(m && mode, "bad arguments");
+    bool p2p = false;
+    for (const PlanLayer& P : m->L) p2p = p2p || P.p2p;
     *mode = !m->comm ? RT_COMM_NONE
+            : p2p ? RT_COMM_SHARDED_P2P
             : m->sharded ? RT_COMM_SHARDED_OPT
             : m->comm_bf16 ? RT_COMM_ALLREDUCE_BF16
                            : RT_COMM_ALLREDUCE;
@@ -1040,6 +1131,8 @@ int rt_mlp_comm_mode(rt_mlp* m, int* mode) {
 
 int rt_mlp_set_comm(rt_mlp* m, rt_comm* comm) {
     RT_CHECK(m, "bad arguments");
+    RT_CUDA(cudaStreamSynchronize(m->ctx->stream));  // no step still uses the old exchange
+    teardown_p2p(m);
     m->comm = comm;
     // RTGPU_COMM_SM_RESERVE=<n>: backward GEMMs run on sm_count - n SMs so the
     // gradient allreduce has SMs of its own (an even count keeps CTA pairs whole).
@@ -1093,6 +1186,8 @@ int rt_mlp_set_comm(rt_mlp* m, rt_comm* comm) {
         }
         RT_TRY(st);
     }
+    if (sharded && !m->scratch) RT_TRY(dalloc_t(m, &m->scratch, 4));
+    RT_TRY(setup_p2p(m));
     m->ops.clear();
     drop_graphs(m);
     return RT_OK;

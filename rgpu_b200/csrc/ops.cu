@@ -92,9 +92,23 @@ bool narrow_k_on_tensor_cores(const rt_ctx* ctx, const GemmDesc& g) {
     return ctx->skinny_k_max >= 0 || (g.k >= 8 && (double)g.k * g.m * g.n >= (double)(1 << 28));
 }
 
+// Whether run_gemm takes the tensor-core path in one k slice for g, the path
+// whose epilogue can scatter rows to their owners over peer memory.
+bool gemm_p2p_capable(const rt_ctx* ctx, const GemmDesc& g) {
+    if (!ctx->fast_gemm || g.m < 1 || g.n < 1 || g.k < 1 || g.opt.kind || g.out_dtype != RT_F32) return false;
+    if (gemm_skinny_wanted(g) && !narrow_k_on_tensor_cores(ctx, g)) return false;
+    if (!gemm_tc_supported(ctx, g)) return false;
+    return g.split_k == 1;
+}
+
 int run_gemm(rt_ctx* ctx, GemmDesc g, cudaStream_t stream, size_t ws_bytes) {
     RT_TRY(check_gemm(g));
     if (g.m == 0 || g.n == 0) return RT_OK;
+    if (g.p2p.world > 0) {
+        RT_CHECK(gemm_p2p_capable(ctx, g), "peer-scatter GEMM %lldx%lldx%lld is not on the one-slice tensor-core path",
+                 (long long)g.m, (long long)g.n, (long long)g.k);
+        return launch_gemm_tc(ctx, g, stream);
+    }
     if (g.split_k <= 0) {
         g.split_k = choose_split(ctx, g);
         if ((size_t)g.split_k * g.m * g.n * 4 > ws_bytes || !g.workspace) g.split_k = 1;

@@ -201,7 +201,9 @@ struct TcParams {
     OptFuse opt;
     int kb_seg;  // 3xTF32: k blocks per product segment (the k loop runs 3 * kb_seg blocks); 0 otherwise
     int tma_store;  // epilogue: 1 = C and 2 = split-K partials through shared-memory staging and TMA stores,
-                    // 3 = fused optimiser through the staging boxes (opt_chunk), 0 = direct stores
+                    // 3 = fused optimiser through the staging boxes (opt_chunk), 4 = rows scattered to
+                    // their owners' receive buffers over peer memory (p2p_chunk), 0 = direct stores
+    P2PScatter p2p;
 };
 
 // Epilogue staging: one 32 x 32 output chunk per epilogue warp (4 KB), the
@@ -477,6 +479,48 @@ __device__ __forceinline__ void opt_chunk(const TcParams& p, float* box, int lan
         }
     }
     __syncwarp();  // the box is rewritten by the next chunk
+}
+
+// Peer-scatter epilogue (tma_store == 4) for one warp's 32 x 32 chunk of a dW
+// tile, lane = row row0 + lane: transposed through the warp's box as in
+// opt_chunk, then each lane stores four consecutive columns of one row, four
+// rows per warp instruction, to the row's owner (a peer's receive buffer, or
+// this rank's own) or, past owned_end, to C.  The caller ends the kernel's
+// epilogue with a system-scope fence, so every store is in place before the
+// rank's barrier after the GEMM.
+__device__ __forceinline__ void p2p_chunk(const TcParams& p, float* box, int lane, int64_t row0, int64_t col0,
+                                          const float (&v)[32]) {
+#pragma unroll
+    for (int c = 0; c < 32; ++c) box[lane * 32 + (c ^ lane)] = v[c];
+    __syncwarp();
+    const P2PScatter& s = p.p2p;
+    const int cq = (lane & 7) * 4;
+    const int64_t col = col0 + cq;
+    float* C = static_cast<float*>(p.c);
+#pragma unroll 2
+    for (int it = 0; it < 8; ++it) {
+        const int rr = it * 4 + (lane >> 3);
+        const int64_t i = row0 + rr;
+        if (i >= p.m) continue;
+        float* dst;
+        if (i < s.owned_end) {
+            const int64_t o = i / s.rows_owned;
+            dst = s.peer[o] + (int64_t)s.rank * s.q_stride + (s.base_row + i - o * s.rows_owned) * s.ld;
+        } else {
+            dst = C + i * p.ldc;
+        }
+        float g[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) g[j] = box[rr * 32 + ((cq + j) ^ rr)];
+        if (col + 4 <= p.n && (reinterpret_cast<uintptr_t>(dst + col) & 15) == 0) {
+            *reinterpret_cast<float4*>(dst + col) = make_float4(g[0], g[1], g[2], g[3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (col + j < p.n) dst[col + j] = g[j];
+        }
+    }
+    __syncwarp();
 }
 
 // ------------------------------------------------------------------ host

@@ -595,11 +595,13 @@ class GpuMlp:
         _check(lib().rt_mlp_set_comm(self.handle, comm.handle if comm else None))
 
     def comm_mode(self) -> str:
-        """How gradients are summed: "none", "allreduce", "allreduce_bf16" or
-        "sharded_opt" (reduce-scatter, sliced update, weight all-gather)."""
+        """How gradients are summed: "none", "allreduce", "allreduce_bf16",
+        "sharded_opt" (reduce-scatter, sliced update, weight all-gather) or
+        "sharded_p2p" (the same, the reduce-scatter done by the dW GEMMs over
+        peer memory)."""
         v = C.c_int()
         _check(lib().rt_mlp_comm_mode(self.handle, C.byref(v)))
-        return ("none", "allreduce", "allreduce_bf16", "sharded_opt")[v.value]
+        return ("none", "allreduce", "allreduce_bf16", "sharded_opt", "sharded_p2p")[v.value]
 
 
 def _is_bf16(t: GpuTensor) -> bool:

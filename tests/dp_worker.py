@@ -96,8 +96,9 @@ def main():
     # agree bit for bit.
     os.environ["RTGPU_GRAD_COMM"] = "f32"
     runs = {}
-    for sharded in ("0", "1"):
-        os.environ["RTGPU_SHARDED_OPT"] = sharded
+    for sharded in ("0", "1", "p2p"):
+        os.environ["RTGPU_SHARDED_OPT"] = "0" if sharded == "0" else "1"
+        os.environ["RTGPU_P2P_RS"] = "1" if sharded == "p2p" else "0"
         mlp = rgpu_b200.GpuMlp.from_params(gpu, params, per, 1e-3, dtype="bf16", optimizer="adam",
                                            global_batch=n_global)
         mlp.set_comm(comm)
@@ -109,17 +110,21 @@ def main():
                          np.frombuffer(mlp.save_state(), np.uint8))
         mlp.close()
     os.environ.pop("RTGPU_SHARDED_OPT")
-    (mode0, w0, g0, s0), (mode1, w1, g1, s1) = runs["0"], runs["1"]
-    wt = torch.from_numpy(w1).cuda()
-    gathered = [torch.zeros_like(wt) for _ in range(world)]
-    dist.all_gather(gathered, wt)
+    os.environ.pop("RTGPU_P2P_RS")
+    mode0, w0, g0, s0 = runs["0"]
+    rel = lambda a, b: float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))  # noqa: E731
+    hdr = 24 + 8 * len(dims)
+    for key, name in (("1", "sharded"), ("p2p", "sharded_p2p")):
+        mode1, w1, g1, s1 = runs[key]
+        wt = torch.from_numpy(w1).cuda()
+        gathered = [torch.zeros_like(wt) for _ in range(world)]
+        dist.all_gather(gathered, wt)
+        if rank == 0:
+            result[name] = {"modes": [mode0, mode1], "weights": rel(w1, w0), "grads": rel(g1, g0),
+                            "state": rel(s1[hdr:].view(np.float32), s0[hdr:].view(np.float32)),
+                            "header_equal": bool(np.array_equal(s1[:hdr], s0[:hdr])),
+                            "replicas_identical": all(torch.equal(gathered[0], g) for g in gathered[1:])}
     if rank == 0:
-        rel = lambda a, b: float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))  # noqa: E731
-        hdr = 24 + 8 * len(dims)
-        result["sharded"] = {"modes": [mode0, mode1], "weights": rel(w1, w0), "grads": rel(g1, g0),
-                             "state": rel(s1[hdr:].view(np.float32), s0[hdr:].view(np.float32)),
-                             "header_equal": bool(np.array_equal(s1[:hdr], s0[:hdr])),
-                             "replicas_identical": all(torch.equal(gathered[0], g) for g in gathered[1:])}
         json.dump(result, open(out_path, "w"))
     comm.close()
     gpu.close()

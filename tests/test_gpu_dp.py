@@ -36,8 +36,9 @@ def test_two_rank_dp_equals_single_gpu(tmp_path):
     for case in ("f32", "bf16", "f32_chunked", "bf16_gradcomm"):
         dp, single = res[case + "_loss"]
         assert abs(dp - single) <= 1e-6 * abs(single), (case, dp, single)
-    sh = res["sharded"]
-    assert sh["modes"] == ["allreduce", "sharded_opt"], sh
-    # two ranks: a + b in either collective, the same elementwise update
-    assert sh["weights"] <= 1e-6 and sh["grads"] <= 1e-6 and sh["state"] <= 1e-6, sh
-    assert sh["header_equal"] and sh["replicas_identical"], sh
+    for name, mode in (("sharded", "sharded_opt"), ("sharded_p2p", "sharded_p2p")):
+        sh = res[name]
+        assert sh["modes"] == ["allreduce", mode], sh
+        # two ranks: a + b in either exchange, the same elementwise update
+        assert sh["weights"] <= 1e-6 and sh["grads"] <= 1e-6 and sh["state"] <= 1e-6, (name, sh)
+        assert sh["header_equal"] and sh["replicas_identical"], (name, sh)
