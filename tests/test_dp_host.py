@@ -59,3 +59,48 @@ def test_gloo_two_ranks_sum_to_full_batch_gradient():
         for i, ref in enumerate(model.grads()):
             g = got[f"arr_{i}"]
             assert np.allclose(g, ref, rtol=1e-5, atol=1e-7), i
+
+
+def _chunk_row_of(rows, chunks, c):
+    # mlp.cu chunk_row_of: chunk starts on 256-row edges, the last takes the rest
+    return rows if c >= chunks else rows * c // chunks // 256 * 256
+
+
+@pytest.mark.parametrize("d,ld,world,chunks", [(4096, 8192, 8, 4), (8192, 1024, 8, 4), (1024, 512, 2, 4),
+                                               (512, 192, 2, 2), (2048, 64, 4, 2)])
+def test_peer_scatter_layout_is_the_flat_reduce_scatter(d, ld, world, chunks):
+    # The peer-memory reduce-scatter (p2p_chunk in tc_common.cuh, dw_gemm_rows
+    # and allreduce_rows in mlp.cu), restated: launch row i of chunk [r0, r1)
+    # goes to owner o = i // h at
+    #   o's buffer [src * q_stride + (r0 // world + i - o * h) * ld + col],
+    # h = (e - r0) // world, e = min(r1, d), q_stride = d // world * ld; the
+    # owner sums its [r0 // world * ld, + h * ld) window of every source region
+    # into g[(r0 + o * h) * ld, + h * ld).  Checked: every (source, row) pair
+    # lands on its own row of the owner's buffer, inside the buffer, and the
+    # owner's sums cover exactly its flat reduce-scatter slice of each chunk,
+    # (e - r0) * ld / world elements from r0 * ld + o * (e - r0) * ld / world.
+    rows = d + 1
+    q_stride = d // world * ld
+    seen = [set() for _ in range(world)]
+    for c in range(chunks):
+        r0, r1 = _chunk_row_of(rows, chunks, c), _chunk_row_of(rows, chunks, c + 1)
+        e = min(r1, d)
+        assert (e - r0) % world == 0 and r0 % world == 0
+        h = (e - r0) // world
+        for src in range(world):
+            for i in range(r1 - r0):
+                if i >= e - r0:
+                    continue  # the bias row stays in the rank's own g (allreduced)
+                o = i // h
+                off = src * q_stride + (r0 // world + i - o * h) * ld
+                assert 0 <= off and off + ld <= world * q_stride == d * ld
+                assert off not in seen[o]
+                seen[o].add(off)
+        for o in range(world):
+            # what the owner sums for chunk c, row by row, is rows r0 + o*h ...
+            window = [(r0 // world + k) * ld for k in range(h)]
+            got_rows = [r0 + o * h + k for k in range(h)]
+            flat0 = r0 * ld + o * ((e - r0) * ld // world)
+            assert got_rows[0] * ld == flat0 and len(window) * ld == (e - r0) * ld // world
+    for o in range(world):
+        assert len(seen[o]) == world * d // world  # every source's every owned row, once
