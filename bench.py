@@ -473,6 +473,8 @@ def main():
     dims = cfg["dims"]
 
     gpu = rgpu_b200.Gpu(local)
+    if args.l2_group:
+        gpu.set_grupo_l2(args.l2_group)
     params, x, labels = make_inputs(cfg, batch, 1234 + rank)
     mlp = rgpu_b200.GpuMlp.from_params(gpu, params, batch, cfg["lr"], dtype=cfg["dtype"],
                                        optimizer=cfg["optimizer"], global_batch=global_batch)

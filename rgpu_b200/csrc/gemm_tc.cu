@@ -449,7 +449,16 @@ int gemm_tc_x3_init() {
     return RT_OK;
 }
 
+// Few output tiles: when even 128 x 128 tiles leave more than half of the SMs
+// without one, the GEMM is bound by how fast its busy SMs stream operands and
+// write C, so 128 x 64 one-CTA tiles (twice the CTAs) go first.
+static bool few_tiles(const rt_ctx* ctx, const GemmDesc& g) {
+    const int64_t splits = g.split_k > 1 ? g.split_k : 1;
+    return ((g.m + 127) / 128) * ((g.n + 127) / 128) * splits * 2 < ctx->sm_count && g.n > 64;
+}
+
 int launch_gemm_tc_x3(rt_ctx* ctx, const GemmDesc& g, const X3Planes& x3, cudaStream_t st) {
+    if (few_tiles(ctx, g)) return launch_variant<float, false, false, 64, true>(ctx, g, st, &x3);
     if (gemm_tc2_x3_wanted(ctx, g)) return launch_gemm_tc2_x3(ctx, g, x3, st);
     if (g.n <= 64) return launch_variant<float, false, false, 64, true>(ctx, g, st, &x3);
     if (g.n <= 128) return launch_variant<float, false, false, 128, true>(ctx, g, st, &x3);
@@ -458,6 +467,7 @@ int launch_gemm_tc_x3(rt_ctx* ctx, const GemmDesc& g, const X3Planes& x3, cudaSt
 
 int launch_gemm_tc(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     if (!gemm_tc_supported(ctx, g)) return fail(RT_ERR_UNSUPPORTED, "operands not eligible for the tensor-core GEMM");
+    if (few_tiles(ctx, g)) return launch_layout<__nv_bfloat16, 64>(ctx, g, st);
     if (gemm_tc2_wanted(ctx, g)) return launch_gemm_tc2(ctx, g, st);
     if (g.n <= 64) return launch_layout<__nv_bfloat16, 64>(ctx, g, st);
     if (g.n <= 128) return launch_layout<__nv_bfloat16, 128>(ctx, g, st);

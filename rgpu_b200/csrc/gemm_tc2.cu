@@ -529,8 +529,11 @@ bool gemm_tc2_wanted(const rt_ctx* ctx, const GemmDesc& g) {
     return ctx->pair_gemm && g.in_dtype == RT_BF16 && g.m >= 256 && g.n > 64;
 }
 
+// 256-wide column tiles unless they leave more than half of the SM pairs
+// idle, then 128-wide ones (as the 3xTF32 form below).
 int launch_gemm_tc2(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
-    if (g.n <= 128) return launch_pair_layout<128>(ctx, g, st);
+    const int64_t tiles256 = ((g.m + BM2 - 1) / BM2) * ((g.n + 255) / 256) * (g.split_k > 1 ? g.split_k : 1);
+    if (g.n <= 128 || tiles256 * 4 < ctx->sm_count) return launch_pair_layout<128>(ctx, g, st);
     return launch_pair_layout<256>(ctx, g, st);
 }
 
