@@ -38,7 +38,7 @@ CONFIGS = {
     # update fused into its epilogue), 1.6 GB on the device
     "probe_dw": dict(dims=[8192, 8192], batch=8192, dtype="bf16", optimizer="adam", lr=1e-3),
 }
-CPU_SAMPLE_ROWS = {"wide": 64, "small": 256, "probe_dw": 64}
+CPU_SAMPLE_ROWS = {"wide": 64, "small": 2048, "probe_dw": 64}
 # DRAM bytes (read + write) of one 8192 x 8192 x 8192 dW GEMM launch (the
 # two-CTA kernel), from an ncu capture (dram__bytes_read.sum +
 # dram__bytes_write.sum) of `bench.py --gemm TN --mnk 8192 8192 8192`; scaled
@@ -165,47 +165,88 @@ class ClockSampler:
                 "samples": len(sm), "window": window}
 
 
-def cpu_baseline(cfg_name, cfg, warm=1, reps=1, rows=None):
-    """rtensor's CPU train step (oracle restatement) on a bounded sample."""
-    import oracle
+class CpuStep:
+    """rtensor's CPU train step (the oracle's C++ restatement, all host
+    threads) on a bounded sample of the config's batch.
 
-    rows = rows or CPU_SAMPLE_ROWS[cfg_name]
-    threads = os.cpu_count() or 1
-    params, x, labels = make_inputs(cfg, rows, 99)
-    m = oracle.Mlp(cfg["dims"])
-    m.set_params(params)
-    opt = oracle.OPT_ADAM if cfg["optimizer"] == "adam" else oracle.OPT_SGD
-    for _ in range(warm):
-        m.train_step(x, labels, opt, cfg["lr"], threads=threads)
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        m.train_step(x, labels, opt, cfg["lr"], threads=threads)
-    dt = (time.perf_counter() - t0) / reps
-    return rows / dt, threads, dt, rows
+    A timed step runs `rows` rows with the optimiser.  Below the full batch,
+    the step's cost is extrapolated: forward+backward grows linearly in the
+    rows past a fixed part (the weight-sized passes), so its slope b is fitted
+    once from forward+backward passes on FIT_ROWS[0] and FIT_ROWS[1] rows, and
+        t_full_batch = t_step(rows) + (batch - rows) * b."""
+
+    FIT_ROWS = (256, 512)
+
+    def __init__(self, cfg, rows):
+        import oracle
+
+        self.O = oracle
+        self.cfg = cfg
+        self.batch = cfg["batch"]
+        self.rows = min(rows, self.batch)
+        self.threads = os.cpu_count() or 1
+        nmax = max(self.rows, self.FIT_ROWS[1]) if self.rows < self.batch else self.rows
+        params, self.x, self.labels = make_inputs(cfg, nmax, 99)
+        self.nparams = sum(p.size for p in params)
+        self.m = oracle.Mlp(cfg["dims"])
+        self.m.set_params(params)
+        self.opt = oracle.OPT_ADAM if cfg["optimizer"] == "adam" else oracle.OPT_SGD
+        self.b = 0.0
+
+    def _run(self, n, opt, lr):
+        t0 = time.perf_counter()
+        self.m.train_step(self.x[:n], self.labels[:n], opt, lr, threads=self.threads)
+        return time.perf_counter() - t0
+
+    def fit(self):
+        """Seconds per extra row of forward+backward (0 when a step is the full batch)."""
+        if self.rows >= self.batch:
+            return 0.0
+        r1, r2 = self.FIT_ROWS
+        self._run(r1, self.O.OPT_NONE, 0.0)  # warm caches and pages
+        t1 = self._run(r1, self.O.OPT_NONE, 0.0)
+        t2 = self._run(r2, self.O.OPT_NONE, 0.0)
+        self.b = max(t2 - t1, 0.0) / (r2 - r1)
+        return self.b
+
+    def time_step(self):
+        return self._run(self.rows, self.opt, self.cfg["lr"])
+
+    def full_batch_seconds(self, t_step):
+        return t_step + (self.batch - self.rows) * self.b
+
+    def sample(self):
+        if self.rows >= self.batch:
+            return f"the full {self.batch}-row step on {self.threads} threads"
+        return (f"{self.rows} of the {self.batch} rows per step with the {self.cfg['optimizer']} pass over all "
+                f"{self.nparams} parameters, on {self.threads} threads; the other rows' forward+backward "
+                f"extrapolated at {self.b * 1e3:.1f} ms per row (slope between {self.FIT_ROWS[0]} and "
+                f"{self.FIT_ROWS[1]} rows)")
+
+
+def cpu_baseline(cfg_name, cfg, rows=None):
+    """The CPU reference step's throughput at the full batch, from a bounded sample."""
+    c = CpuStep(cfg, rows or CPU_SAMPLE_ROWS[cfg_name])
+    c.time_step()  # warm-up: the first optimiser pass pages in the moments
+    c.fit()
+    sec = c.full_batch_seconds(c.time_step())
+    return cfg["batch"] / sec, c.threads, sec, c.sample()
 
 
 def run_reference(args, cfg_name, cfg, rank):
     if rank != 0:
         return
-    cores = os.cpu_count() or 1
-    rows = CPU_SAMPLE_ROWS[cfg_name]
-    import oracle  # noqa: F401
-
+    c = CpuStep(cfg, CPU_SAMPLE_ROWS[cfg_name])
     per_step = []
-    params, x, labels = make_inputs(cfg, rows, 99)
-    import oracle as O
-
-    m = O.Mlp(cfg["dims"])
-    m.set_params(params)
-    opt = O.OPT_ADAM if cfg["optimizer"] == "adam" else O.OPT_SGD
+    c.time_step()  # the first optimiser pass pages in the moments
+    c.fit()
     for i in range(args.warmup + args.steps):
-        t0 = time.perf_counter()
-        m.train_step(x, labels, opt, cfg["lr"], threads=cores)
-        dt = time.perf_counter() - t0
+        t = c.time_step()
         if i >= args.warmup:
-            per_step.append(dt)
+            per_step.append(c.full_batch_seconds(t))
     sec = sum(per_step) / len(per_step)
-    value = rows / sec
+    value = cfg["batch"] / sec
+    cores = c.threads
     line = {
         "impl": "reference", "metric": "train samples/sec (fwd+bwd+update)", "value": value,
         "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -213,7 +254,7 @@ def run_reference(args, cfg_name, cfg, rank):
         "dtype": "f32", "data": "synthetic",
         "config": config_dict(cfg_name, cfg, args.gpus, cfg["batch"] * args.gpus),
         "cpu_baseline": {"value": value, "unit": "samples/s", "cores": cores, "kind": "port",
-                         "sample": f"{rows} rows of the {cfg['batch']}-row step per timed step, full model"},
+                         "sample": c.sample()},
         "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -608,9 +649,9 @@ def main():
         cpu = None
         if world == 1 and not args.no_cpu:
             try:
-                v, cores, dt, rows = cpu_baseline(args.config, cfg)
+                v, cores, sec, sample = cpu_baseline(args.config, cfg)
                 cpu = {"value": v, "unit": "samples/s", "cores": cores, "kind": "port",
-                       "sample": f"{rows} rows of the {batch}-row step, full model, {dt:.1f} s/step"}
+                       "sample": f"{sample}; {sec:.1f} s per full-batch step"}
             except Exception as e:  # the baseline must not hide the GPU line
                 cpu = {"value": None, "unit": "samples/s", "cores": os.cpu_count(), "kind": "port",
                        "sample": f"failed: {e}"}
