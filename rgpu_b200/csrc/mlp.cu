@@ -480,14 +480,17 @@ struct Enqueuer {
         return RT_OK;
     }
 
-    // Backward and update.  Per layer, top down: the dW GEMM (in row chunks of
-    // [dW; db], contiguous rows of the parameter block), each chunk handed to
-    // the comm stream for its allreduce as soon as it is computed; then the dX
-    // GEMM, the last reader of W_l in the step; then, on the optimiser stream,
-    // each chunk's update once dX is done and the chunk is reduced.  The first
-    // layer has no dX GEMM, so its chunk updates follow the chunk GEMMs
-    // directly: its dW GEMM is the last GEMM of the step, and chunking it keeps
-    // the trailing update (and allreduce) to one chunk.
+    // Backward and update with separate update kernels (data parallelism, no
+    // optimiser, or RTGPU_FUSED_OPT=0).  Per layer, top down: the dW GEMM (in
+    // row chunks of [dW; db], contiguous rows of the parameter block), each
+    // chunk handed to the comm stream for its gradient sum as soon as it is
+    // computed (allreduce; or, sharded, a reduce-scatter or the peer-scatter
+    // barrier and owner sum); then the dX GEMM, the last reader of W_l in the
+    // step; then, on the optimiser stream, each chunk's update (of this rank's
+    // slice, when sharded) once dX is done and the chunk is summed, and the
+    // sharded weight all-gathers.  The first layer has no dX GEMM, so its chunk
+    // updates follow the chunk GEMMs directly: its dW GEMM is the last GEMM of
+    // the step, and chunking it keeps the trailing exchange to one chunk.
     int backward_and_update() {
         if (m->fuse_opt) return backward_fused();
         const int nl = (int)m->L.size();
