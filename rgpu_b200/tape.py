@@ -17,7 +17,7 @@ import ctypes as C
 
 import numpy as np
 
-from .gpu import RT_U32, Gpu, GpuTensor, _check, lib, upload_labels
+from .gpu import Gpu, GpuTensor, _check, lib, upload_labels
 
 # rt_binary_op / rt_unary_op (include/rtgpu.h)
 ADD, SUB, MUL, DIV = range(4)

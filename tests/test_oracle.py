@@ -7,7 +7,6 @@ tests and central-difference gradient checks
 Rng and optimiser arithmetic in numpy float32.
 """
 import numpy as np
-import pytest
 
 import oracle
 
