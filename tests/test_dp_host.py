@@ -104,3 +104,70 @@ def test_peer_scatter_layout_is_the_flat_reduce_scatter(d, ld, world, chunks):
             assert got_rows[0] * ld == flat0 and len(window) * ld == (e - r0) * ld // world
     for o in range(world):
         assert len(seen[o]) == world * d // world  # every source's every owned row, once
+
+
+def _sharded_rank(rank, world, port, out_dir):
+    # The sharded optimiser's slicing (mlp.cu: shard_end, enqueue_update_rows,
+    # allreduce_rows, gather_weights) on gloo ranks with the oracle's Adam:
+    # per chunk of [W; b] rows, rank r updates the flat slice
+    # [r0*u + r*piece, + piece), piece = (min(r1, d) - r0) * u / world, of the
+    # summed gradient; the bias row is summed and updated on every rank; the
+    # slices are then all-gathered.  Path A is the replicated update.
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        dims, n = [512, 384, 10], 16
+        rng = oracle.Rng(5)
+        model = oracle.Mlp(dims)
+        model.init_glorot(rng)
+        x = rng.normal(n * dims[0]).reshape(n, dims[0])
+        labels = rng.below(dims[-1], n)
+        per = n // world
+        model.train_step(x[rank * per:(rank + 1) * per], labels[rank * per:(rank + 1) * per])
+        grads = [g * (per / n) for g in model.grads()]
+        params = model.params()
+        out = {}
+        for mode in ("replicated", "sharded"):
+            thetas = []
+            for l in range(len(dims) - 1):
+                d, u = dims[l], dims[l + 1]
+                theta = np.ascontiguousarray(np.concatenate([params[2 * l], params[2 * l + 1]]).ravel(), np.float32)
+                g = torch.from_numpy(np.concatenate([grads[2 * l], grads[2 * l + 1]]).ravel().copy())
+                dist.all_reduce(g)  # the sum (a reduce-scatter keeps only this rank's slice of it)
+                g = g.numpy()
+                mm, vv = np.zeros_like(theta), np.zeros_like(theta)
+                if mode == "replicated":
+                    oracle.adam_update(theta, mm, vv, g, 1e-3, 1)
+                else:
+                    rows = d + 1
+                    chunks = 2 if rows >= 512 else 1
+                    for c in range(chunks):
+                        r0, r1 = _chunk_row_of(rows, chunks, c), _chunk_row_of(rows, chunks, c + 1)
+                        e = min(r1, d)
+                        piece = (e - r0) * u // world
+                        assert (e - r0) * u % world == 0
+                        a = r0 * u + rank * piece
+                        th, m_, v_ = theta[a:a + piece], mm[a:a + piece], vv[a:a + piece]
+                        oracle.adam_update(th, m_, v_, g[a:a + piece], 1e-3, 1)
+                        if r1 > d:  # the bias row, replicated
+                            b0 = d * u
+                            th, m_, v_ = theta[b0:b0 + u], mm[b0:b0 + u], vv[b0:b0 + u]
+                            oracle.adam_update(th, m_, v_, g[b0:b0 + u], 1e-3, 1)
+                        parts = [torch.zeros(piece) for _ in range(world)]
+                        dist.all_gather(parts, torch.from_numpy(theta[a:a + piece].copy()))
+                        theta[r0 * u:r0 * u + world * piece] = torch.cat(parts).numpy()
+                thetas.append(theta)
+            out[mode] = np.concatenate(thetas)
+        if rank == 0:
+            np.savez(os.path.join(out_dir, "sharded.npz"), **out)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_sharded_update_equals_replicated_update():
+    world = 2
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_sharded_rank, args=(world, 29618, d), nprocs=world, start_method="spawn")
+        got = np.load(os.path.join(d, "sharded.npz"))
+        assert np.array_equal(got["replicated"], got["sharded"])
