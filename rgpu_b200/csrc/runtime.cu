@@ -72,7 +72,15 @@ int rt_ctx_create(int device, rt_ctx** out) {
     c->cc_minor = prop.minor;
     snprintf(c->name, sizeof c->name, "%s (sm_%d%d, %d SMs, %.1f GB)", prop.name, prop.major, prop.minor,
              prop.multiProcessorCount, prop.totalGlobalMem / 1e9);
-    cudaError_t e1 = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking);
+    // RTGPU_MAIN_PRIORITY=1 puts the context's stream one level above the
+    // lowest priority: under data parallelism the plan's update kernels
+    // (lowest, on a side stream) then yield freed SMs to its GEMMs, and the
+    // collectives' streams sit above both.  Default: the lowest level.
+    int least = 0, greatest = 0;
+    cudaDeviceGetStreamPriorityRange(&least, &greatest);
+    const char* pr_env = getenv("RTGPU_MAIN_PRIORITY");
+    const int prio = (greatest < least && pr_env && pr_env[0] == '1') ? least - 1 : least;
+    cudaError_t e1 = cudaStreamCreateWithPriority(&c->own_stream, cudaStreamNonBlocking, prio);
     // one allocation: the device error word (16 bytes) and, 32 bytes in, the
     // Adam scalars of op-level rt_adam calls
     cudaError_t e2 = cudaMalloc(&c->dev_err, 64);
