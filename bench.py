@@ -38,7 +38,8 @@ CONFIGS = {
     # update fused into its epilogue), 1.6 GB on the device
     "probe_dw": dict(dims=[8192, 8192], batch=8192, dtype="bf16", optimizer="adam", lr=1e-3),
 }
-CPU_SAMPLE_ROWS = {"wide": 64, "small": 2048, "probe_dw": 64}
+# Rows of the one-thread CPU baseline step (the full batch where that is quick)
+CPU_SAMPLE_ROWS = {"wide": 256, "small": 2048, "probe_dw": 256}
 # DRAM bytes (read + write) of one 8192 x 8192 x 8192 dW GEMM launch (the
 # two-CTA kernel), from an ncu capture (dram__bytes_read.sum +
 # dram__bytes_write.sum) of `bench.py --gemm TN --mnk 8192 8192 8192`; scaled
@@ -165,96 +166,111 @@ class ClockSampler:
                 "samples": len(sm), "window": window}
 
 
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
 class CpuStep:
-    """rtensor's CPU train step (the oracle's C++ restatement, all host
-    threads) on a bounded sample of the config's batch.
+    """rtensor's CPU train step (the oracle's C++ restatement of the
+    reference's CPU backend: forward, tape backward, optimiser) of the
+    config's whole model on `rows` rows, on `threads` host threads.  Every
+    timed step is a real step; nothing is extrapolated."""
 
-    A timed step runs `rows` rows with the optimiser.  Below the full batch,
-    the step's cost is extrapolated: forward+backward grows linearly in the
-    rows past a fixed part (the weight-sized passes), so its slope b is fitted
-    once from forward+backward passes on FIT_ROWS[0] and FIT_ROWS[1] rows, and
-        t_full_batch = t_step(rows) + (batch - rows) * b."""
-
-    FIT_ROWS = (256, 512)
-
-    def __init__(self, cfg, rows):
+    def __init__(self, cfg, rows, threads):
         import oracle
 
         self.O = oracle
         self.cfg = cfg
-        self.batch = cfg["batch"]
-        self.rows = min(rows, self.batch)
-        self.threads = os.cpu_count() or 1
-        nmax = max(self.rows, self.FIT_ROWS[1]) if self.rows < self.batch else self.rows
-        params, self.x, self.labels = make_inputs(cfg, nmax, 99)
+        self.rows = min(rows, cfg["batch"])
+        self.threads = threads
+        params, self.x, self.labels = make_inputs(cfg, self.rows, 99)
         self.nparams = sum(p.size for p in params)
         self.m = oracle.Mlp(cfg["dims"])
         self.m.set_params(params)
         self.opt = oracle.OPT_ADAM if cfg["optimizer"] == "adam" else oracle.OPT_SGD
-        self.b = 0.0
 
-    def _run(self, n, opt, lr):
+    def step(self, rows=None):
+        n = self.rows if rows is None else rows
         t0 = time.perf_counter()
-        self.m.train_step(self.x[:n], self.labels[:n], opt, lr, threads=self.threads)
+        self.m.train_step(self.x[:n], self.labels[:n], self.opt, self.cfg["lr"], threads=self.threads)
         return time.perf_counter() - t0
 
-    def fit(self):
-        """Seconds per extra row of forward+backward (0 when a step is the full batch)."""
-        if self.rows >= self.batch:
-            return 0.0
-        r1, r2 = self.FIT_ROWS
-        self._run(r1, self.O.OPT_NONE, 0.0)  # warm caches and pages
-        t1 = self._run(r1, self.O.OPT_NONE, 0.0)
-        t2 = self._run(r2, self.O.OPT_NONE, 0.0)
-        self.b = max(t2 - t1, 0.0) / (r2 - r1)
-        return self.b
-
-    def time_step(self):
-        return self._run(self.rows, self.opt, self.cfg["lr"])
-
-    def full_batch_seconds(self, t_step):
-        return t_step + (self.batch - self.rows) * self.b
-
-    def sample(self):
-        if self.rows >= self.batch:
-            return f"the full {self.batch}-row step on {self.threads} threads"
-        return (f"{self.rows} of the {self.batch} rows per step with the {self.cfg['optimizer']} pass over all "
-                f"{self.nparams} parameters, on {self.threads} threads; the other rows' forward+backward "
-                f"extrapolated at {self.b * 1e3:.1f} ms per row (slope between {self.FIT_ROWS[0]} and "
-                f"{self.FIT_ROWS[1]} rows)")
+    def describe(self):
+        part = "the full batch" if self.rows >= self.cfg["batch"] else f"a {self.rows}-row sample of the {self.cfg['batch']}-row batch"
+        return (f"one train step of the whole model on {part} (forward, tape backward, {self.cfg['optimizer']} over all "
+                f"{self.nparams} parameters), {self.threads} thread{'s' if self.threads > 1 else ''}")
 
 
-def cpu_baseline(cfg_name, cfg, rows=None):
-    """The CPU reference step's throughput at the full batch, from a bounded sample."""
-    c = CpuStep(cfg, rows or CPU_SAMPLE_ROWS[cfg_name])
-    c.time_step()  # warm-up: the first optimiser pass pages in the moments
-    c.fit()
-    sec = c.full_batch_seconds(c.time_step())
-    return cfg["batch"] / sec, c.threads, sec, c.sample()
+def cpu_baseline(cfg_name, cfg):
+    """The reference CPU step timed on this host: the primary figure on one
+    thread (rtensor's CPU backend is single-threaded) on a bounded sample of
+    rows, and a secondary full-batch step on every host thread (the oracle
+    splits each matmul's rows; per-element summation order, and so the
+    result, is unchanged, but the threading is not the reference's)."""
+    host_threads = os.cpu_count() or 1
+    one = CpuStep(cfg, CPU_SAMPLE_ROWS[cfg_name], 1)
+    one.step(min(64, one.rows))  # warm-up: pages in weights and moments
+    t1 = min(one.step() for _ in range(2))
+    out = {"value": one.rows / t1, "unit": "samples/s", "cores": 1, "kind": "port",
+           "sample": f"{one.describe()}; {t1:.2f} s per step, best of 2 after a warm-up step",
+           "cpu_model": cpu_model(), "host_threads": host_threads}
+    del one
+    if host_threads > 1:
+        full = CpuStep(cfg, cfg["batch"], host_threads)
+        full.step(min(64, full.rows))
+        tf = full.step()
+        out["all_threads"] = {"value": full.rows / tf, "unit": "samples/s", "cores": host_threads,
+                              "label": "non-reference (multi-threaded oracle; the reference CPU backend uses 1 thread)",
+                              "sample": f"{full.describe()}; {tf:.1f} s for the step"}
+    return out
+
+
+# The reference arm's full-batch steps stop once another would end past this
+# many seconds of stepping (at least one step always runs).
+REFERENCE_BUDGET_S = 150.0
 
 
 def run_reference(args, cfg_name, cfg, rank):
+    """--impl reference: the reference's CPU implementation of the step (the
+    oracle port: the Rust crate cannot be built here) on every host thread,
+    on the arm's config.  Each timed step is a full-batch step; as many run
+    as --steps asks for or REFERENCE_BUDGET_S allows, and the line reports how
+    many did."""
     if rank != 0:
         return
-    c = CpuStep(cfg, CPU_SAMPLE_ROWS[cfg_name])
-    per_step = []
-    c.time_step()  # the first optimiser pass pages in the moments
-    c.fit()
-    for i in range(args.warmup + args.steps):
-        t = c.time_step()
-        if i >= args.warmup:
-            per_step.append(c.full_batch_seconds(t))
-    sec = sum(per_step) / len(per_step)
-    value = cfg["batch"] / sec
-    cores = c.threads
+    threads = os.cpu_count() or 1
+    c = CpuStep(cfg, cfg["batch"], threads)
+    c.step(min(64, c.rows))  # warm-up: a 64-row step pages in weights and moments
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < args.steps:
+        times.append(c.step())
+        spent = time.perf_counter() - t_start
+        if spent + times[-1] > REFERENCE_BUDGET_S:
+            break
+    sec = sum(times) / len(times)
+    value = c.rows / sec
     line = {
         "impl": "reference", "metric": "train samples/sec (fwd+bwd+update)", "value": value,
-        "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "unit": "samples/s", "n_gpus": args.gpus, "steps": len(times), "steps_requested": args.steps,
+        "warmup": 1, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
         "config": config_dict(cfg_name, cfg, args.gpus, cfg["batch"] * args.gpus),
-        "cpu_baseline": {"value": value, "unit": "samples/s", "cores": cores, "kind": "port",
-                         "sample": c.sample()},
+        "cpu_baseline": {"value": value, "unit": "samples/s", "cores": threads, "kind": "port",
+                         "sample": (f"{c.describe()}; {len(times)} timed full-batch steps "
+                                    f"({'all requested' if len(times) == args.steps else f'the {REFERENCE_BUDGET_S:.0f} s budget'}), "
+                                    "after one 64-row warm-up step"),
+                         "cpu_model": cpu_model()},
+        "timed_region_s": sum(times),
         "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -473,6 +489,8 @@ def main():
     ap.add_argument("--op-shape", type=int, nargs=2, default=[8192, 8192], metavar=("ROWS", "COLS"))
     ap.add_argument("--sweep-dtypes", default="f32,bf16")
     ap.add_argument("--sweep-k", default="", help="comma-separated K values (default: the full sweep)")
+    ap.add_argument("--activations", default="split", choices=["split", "bf16"],
+                    help="bf16 plans: hidden activations as a bf16 hi + lo pair (default) or one bf16 rounding")
     args = ap.parse_args()
     if args.sweep:
         run_dw_sweep(args)
@@ -518,7 +536,8 @@ def main():
         gpu.set_grupo_l2(args.l2_group)
     params, x, labels = make_inputs(cfg, batch, 1234 + rank)
     mlp = rgpu_b200.GpuMlp.from_params(gpu, params, batch, cfg["lr"], dtype=cfg["dtype"],
-                                       optimizer=cfg["optimizer"], global_batch=global_batch)
+                                       optimizer=cfg["optimizer"], global_batch=global_batch,
+                                       activations=args.activations)
     del params
     comm = None
     if world > 1:
@@ -649,19 +668,17 @@ def main():
         cpu = None
         if world == 1 and not args.no_cpu:
             try:
-                v, cores, sec, sample = cpu_baseline(args.config, cfg)
-                cpu = {"value": v, "unit": "samples/s", "cores": cores, "kind": "port",
-                       "sample": f"{sample}; {sec:.1f} s per full-batch step"}
+                cpu = cpu_baseline(args.config, cfg)
             except Exception as e:  # the baseline must not hide the GPU line
-                cpu = {"value": None, "unit": "samples/s", "cores": os.cpu_count(), "kind": "port",
-                       "sample": f"failed: {e}"}
+                cpu = {"value": None, "unit": "samples/s", "cores": 1, "kind": "port", "sample": f"failed: {e}"}
         in_bytes = xh.nbytes + labels.nbytes
         line = {
             "metric": "train samples/sec (fwd+bwd+update)", "value": value, "unit": "samples/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": cfg["dtype"],
             "data": "synthetic (seeded N(0,1) inputs, uniform labels, Kaiming-uniform weights)",
-            "config": dict(config_dict(args.config, cfg, world, global_batch), grad_sync=mlp.comm_mode()),
+            "config": dict(config_dict(args.config, cfg, world, global_batch), grad_sync=mlp.comm_mode(),
+                           activations=(args.activations if cfg["dtype"] == "bf16" else "f32")),
             "roofline": roof,
             "ms_per_step_with_kernel_events": ms_events / args.steps,
             "step_tensor_frac": {"achieved_tflops": step_tflops, "peak": pk["bf16"], "frac": step_tflops / pk["bf16"],

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define RTGPU_ABI_VERSION 1
+#define RTGPU_ABI_VERSION 2
 
 typedef enum {
     RT_OK = 0,
@@ -156,7 +156,14 @@ int64_t rt_split_k_static_capacity(void);
  *   RT_EPI_BIAS_RELU  C = max(acc + bias[j], 0)
  *   RT_EPI_RELU_MASK  C = acc * 1[mask[i,j] > 0]   (mask has the output dtype)
  * split_k: 0 = choose, 1 = none, >1 = that many k slices (needs workspace of
- * rt_gemm_workspace_size bytes). */
+ * rt_gemm_workspace_size bytes).
+ * Split bf16 planes (NULL = off; bf16 only, same layout and leading dimension
+ * as the plane they pair with, no counterpart in the reference):
+ *   a_lo  low-order plane of A: the GEMM computes (A + a_lo) B, two bf16
+ *         products into one f32 accumulator, so an f32 operand stored as the
+ *         pair hi = bf16(x), lo = bf16(x - hi) keeps ~16 significant bits;
+ *   c_lo  low-order plane of C: C receives bf16(v) and c_lo receives
+ *         bf16(v - bf16(v)) of every epilogue result v (split_k must be 1). */
 typedef enum { RT_NN = 0, RT_NT = 1, RT_TN = 2 } rt_layout;
 typedef enum { RT_EPI_NONE = 0, RT_EPI_BIAS = 1, RT_EPI_BIAS_RELU = 2, RT_EPI_RELU_MASK = 3 } rt_epilogue;
 typedef struct {
@@ -172,6 +179,8 @@ typedef struct {
     const void* mask; int64_t ldmask;
     int split_k;
     void* workspace; size_t workspace_bytes;
+    const void* a_lo;
+    void* c_lo;
 } rt_gemm_args;
 int rt_gemm(rt_ctx* ctx, const rt_gemm_args* args);
 size_t rt_gemm_workspace_size(rt_ctx* ctx, const rt_gemm_args* args);
@@ -203,15 +212,29 @@ int rt_cast(rt_ctx* ctx, const rt_tensor* src, rt_tensor* dst);
 
 /* ------------------------------------------------------------ MLP plan */
 typedef enum { RT_OPT_NONE = 0, RT_OPT_SGD = 1, RT_OPT_ADAM = 2 } rt_optimizer;
+/* How a bf16 plan stores its hidden activations (f32 plans ignore it):
+ *   RT_ACT_SPLIT  (default) each activation that feeds another hidden layer
+ *                 as the bf16 pair hi + lo; that layer's forward GEMM reads
+ *                 both planes (two bf16 products), the dW GEMM, the ReLU
+ *                 mask and the output layer read hi.  Gradients stay within
+ *                 the 2e-2 relative-L2 bar of the f32 CPU backend.
+ *   RT_ACT_BF16   one bf16 rounding per activation: the forward GEMMs of the
+ *                 hidden layers do half the tensor work, but the rounding
+ *                 moves pre-activations by ~1e-3 of their spread, which flips
+ *                 ReLU masks near zero and puts hidden-layer gradients
+ *                 2e-2 .. 8e-2 away from the f32 CPU backend. */
+typedef enum { RT_ACT_SPLIT = 0, RT_ACT_BF16 = 1 } rt_activations;
 typedef struct {
     int n_layers;          /* Dense layers; dims has n_layers + 1 entries */
     const int64_t* dims;   /* d_0 (inputs) .. d_L (classes) */
     int64_t batch;         /* rows per step on this device */
     int64_t global_batch;  /* rows per step over all ranks (0 = batch) */
-    rt_dtype dtype;        /* RT_F32, or RT_BF16: bf16 operands/activations,
-                              f32 accumulate, f32 master weights + bf16 shadow */
+    rt_dtype dtype;        /* RT_F32, or RT_BF16: bf16 operands and activations
+                              (see rt_activations), f32 accumulate, f32 master
+                              weights + bf16 shadow */
     rt_optimizer optimizer;
     float lr, beta1, beta2, eps;
+    rt_activations activations; /* bf16 plans: RT_ACT_SPLIT (0, default) or RT_ACT_BF16 */
 } rt_mlp_config;
 
 /* GpuMlp::from_params (gpu/mod.rs:1341-1482): hidden layers ReLU, output

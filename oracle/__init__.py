@@ -67,6 +67,7 @@ def lib():
         L.or_mlp_train_step.argtypes = [C.c_void_p, _f32p, _u32p, C.c_size_t, C.c_int,
                                         C.c_float, C.c_int, C.c_int]
         L.or_mlp_set_bf16_emulation.argtypes = [C.c_void_p, C.c_int]
+        L.or_mlp_set_rounding.argtypes = [C.c_void_p, C.c_int]
         L.or_mlp_forward.restype = C.c_float
         L.or_mlp_forward.argtypes = [C.c_void_p, _f32p, _u32p, C.c_size_t, C.c_int]
         L.or_adam_update.argtypes = [_f32p, _f32p, _f32p, _f32p, C.c_size_t, C.c_float,
@@ -177,6 +178,12 @@ def sgd_update(theta, g, lr):
 
 OPT_NONE, OPT_SGD, OPT_ADAM = 0, 1, 2
 
+# bf16 rounding points of the GPU plan, for Mlp.set_rounding (rtensor_cpu.h).
+ROUND_X, ROUND_W, ROUND_ACT, ROUND_DELTA, SPLIT_ACT = 1, 2, 4, 8, 16
+# The bf16 plan with single-bf16 activations, and with split (hi + lo) ones.
+BF16_PLAIN = ROUND_X | ROUND_W | ROUND_ACT | ROUND_DELTA
+BF16_SPLIT = ROUND_X | ROUND_W | ROUND_DELTA | SPLIT_ACT
+
 
 class Mlp:
     """Sequential of Dense layers (ReLU hidden, Linear output) trained with
@@ -197,6 +204,11 @@ class Mlp:
         """Round at the bf16 GPU plan's storage points (test-only option, not
         the reference algorithm; see rtensor_cpu.h)."""
         lib().or_mlp_set_bf16_emulation(self._h, int(bool(on)))
+
+    def set_rounding(self, flags: int):
+        """Round to bf16 at the chosen storage points (ROUND_* / SPLIT_ACT
+        flags; 0 = the plain reference).  Test-only, see rtensor_cpu.h."""
+        lib().or_mlp_set_rounding(self._h, int(flags))
 
     def init_glorot(self, rng: Rng):
         lib().or_mlp_init_glorot(self._h, C.byref(rng.state))

@@ -240,8 +240,9 @@ struct or_mlp {
     std::vector<std::vector<float>> act;  // act[0] = x, act[l+1] = output of layer l
     size_t n = 0;
     int t = 0;
-    bool bf16 = false;
-    std::vector<std::vector<float>> Wq;  // bf16-rounded weights (bf16 emulation)
+    int round = 0;                       // OR_ROUND_* / OR_SPLIT_ACT flags (bf16 emulation)
+    std::vector<std::vector<float>> Wq;  // bf16-rounded weights (OR_ROUND_W)
+    std::vector<std::vector<float>> fwd_in;  // OR_SPLIT_ACT: hi + lo of act[l], the next forward's input
 };
 
 extern "C" {
@@ -302,36 +303,59 @@ void or_mlp_init_kaiming(or_mlp* m, uint64_t* s) {
 // Sequential::forward (nn.rs:179-181) of Dense layers (nn.rs:143-149):
 // Z = x.matmul(W).add(b) (zip with b tiled over rows, tensor.rs:196-200),
 // then relu (ops.rs:190-194) on hidden layers; the last layer is Linear.
-static const float* gemm_weights(or_mlp* m, int l) { return m->bf16 ? m->Wq[l].data() : m->W[l].data(); }
+static const float* gemm_weights(or_mlp* m, int l) {
+    return (m->round & OR_ROUND_W) ? m->Wq[l].data() : m->W[l].data();
+}
+
+// Input of layer l's forward GEMM: x, the previous activation, or (split
+// activations, hidden layer l) its hi + lo pair summed in f32, which is exact.
+static const float* forward_input(or_mlp* m, int l) {
+    return (l > 0 && l + 1 < m->L && (m->round & OR_SPLIT_ACT)) ? m->fwd_in[l].data() : m->act[l].data();
+}
 
 static void forward_impl(or_mlp* m, const float* x, size_t n, int threads) {
     m->n = n;
     m->act.resize(m->L + 1);
     m->act[0].assign(x, x + n * m->dims[0]);
-    if (m->bf16) {
-        round_bf16(m->act[0]);
+    if (m->round & OR_ROUND_X) round_bf16(m->act[0]);
+    if (m->round & OR_ROUND_W) {
         m->Wq.resize(m->L);
         for (int l = 0; l < m->L; ++l) {
             m->Wq[l] = m->W[l];
             round_bf16(m->Wq[l]);
         }
     }
+    if (m->round & OR_SPLIT_ACT) m->fwd_in.resize(m->L);
     for (int l = 0; l < m->L; ++l) {
         size_t d = m->dims[l], u = m->dims[l + 1];
         auto& out = m->act[l + 1];
         out.resize(n * u);
-        matmul(m->act[l].data(), gemm_weights(m, l), out.data(), n, d, u, threads);
+        matmul(forward_input(m, l), gemm_weights(m, l), out.data(), n, d, u, threads);
         const float* bb = m->b[l].data();
         for (size_t i = 0; i < n; ++i)
             for (size_t j = 0; j < u; ++j) out[i * u + j] = out[i * u + j] + bb[j];
         if (l + 1 < m->L) {
             for (auto& v : out) v = std::fmax(v, 0.0f);
-            if (m->bf16) round_bf16(out);
+            if (m->round & OR_SPLIT_ACT) {
+                auto& in = m->fwd_in[l + 1];
+                in.resize(n * u);
+                for (size_t i = 0; i < n * u; ++i) {
+                    const float hi = round_bf16(out[i]);
+                    in[i] = hi + round_bf16(out[i] - hi);
+                    out[i] = hi;
+                }
+            } else if (m->round & OR_ROUND_ACT) {
+                round_bf16(out);
+            }
         }
     }
 }
 
-void or_mlp_set_bf16_emulation(or_mlp* m, int on) { m->bf16 = on != 0; }
+void or_mlp_set_rounding(or_mlp* m, int flags) { m->round = flags; }
+
+void or_mlp_set_bf16_emulation(or_mlp* m, int on) {
+    m->round = on ? (OR_ROUND_X | OR_ROUND_W | OR_ROUND_ACT | OR_ROUND_DELTA) : 0;
+}
 
 float or_mlp_forward(or_mlp* m, const float* x, const uint32_t* labels, size_t n, int threads) {
     forward_impl(m, x, n, threads);
@@ -359,7 +383,8 @@ float or_mlp_train_step(or_mlp* m, const float* x, const uint32_t* labels, size_
     or_one_hot(labels, n, c, y.data());
     std::vector<float> g(n * c);
     float loss = softmax_xent(m->act[L].data(), y.data(), n, c, g.data());
-    if (m->bf16) round_bf16(g);
+    const bool round_delta = (m->round & OR_ROUND_DELTA) != 0;
+    if (round_delta) round_bf16(g);
 
     std::vector<float> wt, at, gin;
     for (int l = L - 1; l >= 0; --l) {
@@ -368,7 +393,7 @@ float or_mlp_train_step(or_mlp* m, const float* x, const uint32_t* labels, size_
             // relu node of layer l: mask from the relu input; A > 0 <=> Z > 0.
             const auto& a = m->act[l + 1];
             for (size_t i = 0; i < n * u; ++i) g[i] = g[i] * (a[i] > 0.0f ? 1.0f : 0.0f);
-            if (m->bf16) round_bf16(g);
+            if (round_delta) round_bf16(g);
         }
         // add node: adjoint of b.
         reduce_rows(g.data(), m->db[l].data(), n, u);

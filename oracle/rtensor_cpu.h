@@ -86,14 +86,27 @@ enum { OR_OPT_NONE = 0, OR_OPT_SGD = 1, OR_OPT_ADAM = 2 };
  * computes the adjoint of x, which the tape always does (ops.rs:128). */
 float or_mlp_train_step(or_mlp* m, const float* x, const uint32_t* labels, size_t n,
                         int optimizer, float lr, int threads, int input_grad);
-/* bf16 emulation (NOT part of the reference algorithm; test-only): when on,
- * the step rounds to bf16 (nearest even) exactly where the bf16 GPU plan
- * stores bf16 -- the input x, the weights used by the GEMMs (the f32 master
- * copy is what the optimiser updates), every hidden activation after
- * bias+ReLU, and every adjoint delta_l before it feeds a GEMM or the bias
- * reduction.  Arithmetic between those points stays f32, in the reference's
- * loop order.  This isolates the bf16 kernels' arithmetic from the rounding
- * policy itself; with it off the oracle is the plain reference. */
+/* bf16 rounding emulation (NOT part of the reference algorithm; test-only).
+ * Each flag rounds to bf16 (nearest even) at one storage point of the bf16
+ * GPU plan; arithmetic between those points stays f32, in the reference's
+ * loop order:
+ *   OR_ROUND_X      the input x;
+ *   OR_ROUND_W      the weights the GEMMs read (the optimiser still updates
+ *                   the f32 masters);
+ *   OR_ROUND_ACT    every hidden activation after bias+ReLU, wherever it is
+ *                   read (next layer's forward, dW, ReLU mask);
+ *   OR_ROUND_DELTA  every adjoint delta_l before it feeds a GEMM or the bias
+ *                   reduction;
+ *   OR_SPLIT_ACT    every hidden activation a is rounded to hi = bf16(a) and,
+ *                   where it feeds another hidden layer, that layer's forward
+ *                   reads hi + bf16(a - hi); the dW product, the ReLU mask
+ *                   and the output layer's forward read hi (the
+ *                   split-activation plan; overrides OR_ROUND_ACT).
+ * With no flag set the oracle is the plain reference. */
+enum { OR_ROUND_X = 1, OR_ROUND_W = 2, OR_ROUND_ACT = 4, OR_ROUND_DELTA = 8, OR_SPLIT_ACT = 16 };
+void or_mlp_set_rounding(or_mlp* m, int flags);
+/* Shorthand: on = OR_ROUND_X | OR_ROUND_W | OR_ROUND_ACT | OR_ROUND_DELTA
+ * (the plan with single-bf16 activations), off = plain reference. */
 void or_mlp_set_bf16_emulation(or_mlp* m, int on);
 
 /* Forward only (Sequential::predict, nn.rs:184-188); returns the loss of the

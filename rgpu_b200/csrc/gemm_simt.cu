@@ -39,8 +39,10 @@ __device__ __forceinline__ float load_mask(const void* mask, int64_t idx) {
 
 struct SimtParams {
     const void* a;
+    const void* a2;  // A's low-order bf16 plane (null = none): A(i,k) = a + a2, exact in f32
     const void* b;
     void* c;
+    void* c_lo;      // bf16 output's low-order plane (null = none)
     float* ws;
     const float* bias;
     const void* mask;
@@ -58,6 +60,8 @@ __device__ __forceinline__ void finish(const SimtParams& p, int64_t i, int64_t j
     if (p.epi == RT_EPI_BIAS_RELU) v = fmaxf(v, 0.0f);
     if (p.epi == RT_EPI_RELU_MASK) v = v * (load_mask<TOut>(p.mask, i * p.ldmask + j) > 0.0f ? 1.0f : 0.0f);
     store_out<TOut>(p.c, i * p.ldc + j, v);
+    if (sizeof(TOut) == 2 && p.c_lo)
+        store_out<TOut>(p.c_lo, i * p.ldc + j, v - __bfloat162float(__float2bfloat16_rn(v)));
 }
 
 // A_KMAJOR: A(i,k) = a[i*lda + k], else a[k*lda + i].
@@ -68,6 +72,7 @@ __global__ void __launch_bounds__(THREADS) gemm_simt_kernel(SimtParams p) {
     __shared__ __align__(16) float Bs[2][BK][BN];
 
     const TIn* A = static_cast<const TIn*>(p.a);
+    const TIn* A2 = static_cast<const TIn*>(p.a2);
     const TIn* B = static_cast<const TIn*>(p.b);
     const int tid = threadIdx.x;
     const int64_t m0 = (int64_t)blockIdx.y * BM;
@@ -90,7 +95,11 @@ __global__ void __launch_bounds__(THREADS) gemm_simt_kernel(SimtParams p) {
             }
             int64_t gi = m0 + row, gk = k0 + kk;
             float v = 0.0f;
-            if (gi < p.m && gk < kend) v = to_f(A_KMAJOR ? A[gi * p.lda + gk] : A[gk * p.lda + gi]);
+            if (gi < p.m && gk < kend) {
+                const int64_t ai = A_KMAJOR ? gi * p.lda + gk : gk * p.lda + gi;
+                v = to_f(A[ai]);
+                if (A2) v += to_f(A2[ai]);
+            }
             ra[q] = v;
         }
 #pragma unroll
@@ -266,8 +275,10 @@ __global__ void splitk_reduce4_kernel(SimtParams p, int slices) {
 SimtParams make_params(const GemmDesc& g) {
     SimtParams p;
     p.a = g.a;
+    p.a2 = g.a_lo;
     p.b = g.b;
     p.c = g.c;
+    p.c_lo = g.c_lo;
     p.ws = g.split_k > 1 ? g.workspace : nullptr;
     p.bias = g.bias;
     p.mask = g.mask;

@@ -41,8 +41,10 @@ __device__ __forceinline__ float4 ld4_f(const __nv_bfloat16* p) {
 
 struct SkinnyParams {
     const void* a;
+    const void* a2;  // A's low-order bf16 plane (null = none): A = a + a2, exact in f32
     const void* b;
     void* c;
+    void* c_lo;      // bf16 output's low-order plane (null = none)
     float* ws;  // [slices][m][n] partial sums (narrow-N TN with slices > 1)
     const float* bias;
     const void* mask;
@@ -65,10 +67,14 @@ __device__ __forceinline__ void finish_one(const SkinnyParams& p, int64_t i, int
         v = v * (mk > 0.0f ? 1.0f : 0.0f);
     }
     if (p.opt.kind) opt_apply_row<1>(p.opt, i * p.ldc + j, &v, 1);
-    if (p.out_bf16)
+    if (p.out_bf16) {
         static_cast<__nv_bfloat16*>(p.c)[i * p.ldc + j] = __float2bfloat16_rn(v);
-    else
+        if (p.c_lo)
+            static_cast<__nv_bfloat16*>(p.c_lo)[i * p.ldc + j] =
+                __float2bfloat16_rn(v - __bfloat162float(__float2bfloat16_rn(v)));
+    } else {
         static_cast<float*>(p.c)[i * p.ldc + j] = v;
+    }
 }
 
 // Vector epilogue of 4 consecutive columns j0..j0+3 of row i (all < n): the
@@ -107,6 +113,12 @@ __device__ __forceinline__ void finish_four(const SkinnyParams& p, int64_t i, in
         u.x = *reinterpret_cast<uint32_t*>(&lo);
         u.y = *reinterpret_cast<uint32_t*>(&hi);
         *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.c) + i * p.ldc + j0) = u;
+        if (p.c_lo) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                static_cast<__nv_bfloat16*>(p.c_lo)[i * p.ldc + j0 + c] =
+                    __float2bfloat16_rn(v[c] - __bfloat162float(__float2bfloat16_rn(v[c])));
+        }
     } else {
         *reinterpret_cast<float4*>(static_cast<float*>(p.c) + i * p.ldc + j0) = make_float4(v[0], v[1], v[2], v[3]);
     }
@@ -179,12 +191,20 @@ __global__ void __launch_bounds__(kThreads) skinny_n_kernel(SkinnyParams p) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
     const TIn* arow = A + (row_ok ? i : 0) * p.lda;
+    const TIn* arow2 = p.a2 ? static_cast<const TIn*>(p.a2) + (row_ok ? i : 0) * p.lda : nullptr;
     for (int64_t kc = 0; kc < p.k; kc += KC) {
         float a[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int64_t q = kc + lane + 32 * u;
             a[u] = (row_ok && q < p.k) ? ld_f(arow, q) : 0.0f;
+        }
+        if (arow2) {
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int64_t q = kc + lane + 32 * u;
+                if (row_ok && q < p.k) a[u] += ld_f(arow2, q);
+            }
         }
         __syncthreads();  // the previous chunk's reads of sb are done
         const int kn = (int)min((int64_t)KC, p.k - kc);
@@ -259,6 +279,11 @@ __global__ void __launch_bounds__(kThreads) skinny_n_tn_kernel(SkinnyParams p) {
                 float a[U];
 #pragma unroll
                 for (int u = 0; u < U; ++u) a[u] = r0 + u < kn ? ld_f(A, (kc + r0 + u) * p.lda + i) : 0.0f;
+                if (p.a2) {
+#pragma unroll
+                    for (int u = 0; u < U; ++u)
+                        if (r0 + u < kn) a[u] += ld_f(static_cast<const TIn*>(p.a2), (kc + r0 + u) * p.lda + i);
+                }
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
                     const float4* br = reinterpret_cast<const float4*>(&sb[r0 + u][0]);  // a broadcast
@@ -304,7 +329,13 @@ __global__ void __launch_bounds__(kThreads) skinny_k_kernel(SkinnyParams p) {
         // consecutive threads read consecutive addresses of A
         const int r = A_KMAJOR ? t / KMAX : t % TM, q = A_KMAJOR ? t % KMAX : t / TM;
         const int64_t i = m0 + r;
-        sa[r][q] = (i < p.m && q < k) ? ld_f(A, A_KMAJOR ? i * p.lda + q : (int64_t)q * p.lda + i) : 0.0f;
+        float v = 0.0f;
+        if (i < p.m && q < k) {
+            const int64_t ai = A_KMAJOR ? i * p.lda + q : (int64_t)q * p.lda + i;
+            v = ld_f(A, ai);
+            if (p.a2) v += ld_f(static_cast<const TIn*>(p.a2), ai);
+        }
+        sa[r][q] = v;
     }
     const int cg = threadIdx.x % 64;  // column group: 4 columns
     const int rg = threadIdx.x / 64;  // rows rg, rg + 4, ...
@@ -377,8 +408,10 @@ __global__ void __launch_bounds__(kThreads) skinny_k_kernel(SkinnyParams p) {
 SkinnyParams make_params(const GemmDesc& g) {
     SkinnyParams p{};
     p.a = g.a;
+    p.a2 = g.a_lo;
     p.b = g.b;
     p.c = g.c;
+    p.c_lo = g.c_lo;
     p.bias = g.bias;
     p.mask = g.mask;
     p.m = g.m;

@@ -36,10 +36,15 @@ using namespace tc;
 // planes read through 3-D maps, and the k loop runs three product segments
 // over the same k range: lo(A) hi(B), hi(A) lo(B), then hi(A) hi(B) (the
 // small terms first).
-template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false>
+// Split bf16 A (p.split_a): two segments over the same k range, A's
+// low-order plane (tmap_a2) first, then A, both against the same B tiles.
+// A bf16 output with a low-order plane (p.c_lo) is stored through tmap_c and
+// tmap_c2.
+template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false, bool SPLIT_C = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                   const __grid_constant__ CUtensorMap tmap_c, TcParams p) {
+                   const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CUtensorMap tmap_a2,
+                   const __grid_constant__ CUtensorMap tmap_c2, TcParams p) {
     static_assert(!X3 || (sizeof(TIn) == 4 && !A_MN && !B_MN), "3xTF32 planes are f32 and K-major");
     using G = Geo<TIn, BN>;
     constexpr bool kTF32 = sizeof(TIn) == 4;
@@ -81,6 +86,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tmap(&tmap_a);
         prefetch_tmap(&tmap_b);
         if (p.tma_store) prefetch_tmap(&tmap_c);
+        if (p.split_a) prefetch_tmap(&tmap_a2);
+        if (SPLIT_C && p.tma_store) prefetch_tmap(&tmap_c2);
     }
     if (warp == 2) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -116,11 +123,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 last_phase[stage] = phase + 1;
                 int k0 = kb * G::BK;
                 int plane_a = 0, plane_b = 0;
+                const CUtensorMap* map_a = &tmap_a;
                 if constexpr (X3) {
                     const int seg = kb / p.kb_seg;
                     k0 = (kb - seg * p.kb_seg) * G::BK;
                     plane_a = seg == 0;
                     plane_b = seg == 1;
+                } else {
+                    if (p.split_a) {
+                        const int seg = kb / p.kb_seg;  // 0: A's low-order plane, 1: A
+                        k0 = (kb - seg * p.kb_seg) * G::BK;
+                        if (seg == 0) map_a = &tmap_a2;
+                    }
                 }
                 const uint32_t sa = smem_u32(smem_a + stage * G::A_BYTES);
                 const uint32_t sb = smem_u32(smem_b + stage * G::B_BYTES);
@@ -131,9 +145,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (A_MN) {
 #pragma unroll
                         for (int c = 0; c < BM / G::CHUNK; ++c)
-                            tma_load_2d(sa + c * (G::BK * 128), &tmap_a, m0 + c * G::CHUNK, k0, fb);
+                            tma_load_2d(sa + c * (G::BK * 128), map_a, m0 + c * G::CHUNK, k0, fb);
                     } else {
-                        tma_load_2d(sa, &tmap_a, k0, m0, fb);
+                        tma_load_2d(sa, map_a, k0, m0, fb);
                     }
                     if (B_MN) {
 #pragma unroll
@@ -242,7 +256,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint8_t* box = smem_epi + ew * kStageBytes;
                     if (p.out_bf16) {
                         if (row < p.m) epilogue_math<__nv_bfloat16>(p, row, col0, v);
-                        stage_and_store<__nv_bfloat16>(&tmap_c, box, lane, row0, col0, v);
+                        if constexpr (SPLIT_C)
+                            stage_and_store_split(&tmap_c, &tmap_c2, box, lane, row0, col0, v);
+                        else
+                            stage_and_store<__nv_bfloat16>(&tmap_c, box, lane, row0, col0, v);
                     } else {
                         if (row < p.m) epilogue_math<float>(p, row, col0, v);
                         stage_and_store<float>(&tmap_c, box, lane, row0, col0, v);
@@ -267,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             opt_apply_row<32>(p.opt, row * p.ldc + col0, v, cnt);
                         }
                         if (p.out_bf16)
-                            epilogue_chunk<__nv_bfloat16>(p, row, col0, v);
+                            epilogue_chunk<__nv_bfloat16, SPLIT_C>(p, row, col0, v);
                         else
                             epilogue_chunk<float>(p, row, col0, v);
                     }
@@ -308,21 +325,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3>
+template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3, bool SPLIT_C = false>
 int launch_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X3Planes* x3) {
     using G = Geo<TIn, BN>;
     const bool bf16 = sizeof(TIn) == 2;
-    CUtensorMap ta, tb, tc;
+    CUtensorMap ta, tb, tc, ta2, tc2;
     if constexpr (X3) {
         // hi/lo planes of the operands, both K-major: A [2][m][k], B [2][n][k]
         RT_TRY(make_tmap_planes(&ta, x3->a, g.k, g.m, x3->lda, x3->a_plane, 2, G::BK, BM));
         RT_TRY(make_tmap_planes(&tb, x3->b, g.k, g.n, x3->ldb, x3->b_plane, 2, G::BK, BN));
+        ta2 = ta;
     } else {
         // A: logical [m,k].  K-major storage [m][lda]; MN-major storage [k][lda].
         if (A_MN)
             RT_TRY(make_tmap(&ta, g.a, bf16, g.m, g.k, g.lda, G::CHUNK, G::BK));
         else
             RT_TRY(make_tmap(&ta, g.a, bf16, g.k, g.m, g.lda, G::BK, BM));
+        ta2 = ta;
+        if (g.a_lo) {  // A's low-order plane: the same geometry
+            if (A_MN)
+                RT_TRY(make_tmap(&ta2, g.a_lo, bf16, g.m, g.k, g.lda, G::CHUNK, G::BK));
+            else
+                RT_TRY(make_tmap(&ta2, g.a_lo, bf16, g.k, g.m, g.lda, G::BK, BM));
+        }
         // B: logical [k,n].  K-major storage [n][ldb]; MN-major storage [k][ldb].
         if (B_MN)
             RT_TRY(make_tmap(&tb, g.b, bf16, g.n, g.k, g.ldb, G::CHUNK, G::BK));
@@ -342,7 +367,14 @@ int launch_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X3Plan
     if constexpr (X3) {
         p.kb_seg = p.kblocks;
         p.kblocks *= 3;
+    } else {
+        if (g.a_lo) {
+            p.split_a = 1;
+            p.kb_seg = p.kblocks;
+            p.kblocks *= 2;
+        }
     }
+    p.c_lo = g.c_lo;
     int splits = g.split_k > 1 ? g.split_k : 1;
     if (splits > p.kblocks) splits = p.kblocks;
     p.kb_per_split = (p.kblocks + splits - 1) / splits;
@@ -363,6 +395,7 @@ int launch_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X3Plan
     p.tma_store = 0;
     p.p2p = g.p2p;
     tc = ta;  // unused unless a staged store is chosen
+    tc2 = ta;
     if (g.p2p.world > 0) {
         // scattered over peer memory: one k slice, f32 gradient, no fused update
         if (splits != 1 || p.out_bf16 || g.opt.kind)
@@ -371,6 +404,7 @@ int launch_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X3Plan
     } else if (ctx->tma_store && splits == 1 && !g.opt.kind) {
         p.tma_store = 1;
         RT_TRY(make_tmap_out(&tc, g.c, p.out_bf16 != 0, g.m, g.n, g.ldc));
+        if (g.c_lo) RT_TRY(make_tmap_out(&tc2, g.c_lo, true, g.m, g.n, g.ldc));
     } else if (ctx->tma_store && splits == 1 && !p.out_bf16) {
         p.tma_store = 3;  // fused optimiser through the epilogue boxes
     } else if (ctx->tma_store && splits > 1 && g.n % 4 == 0 && (reinterpret_cast<uintptr_t>(g.workspace) & 15) == 0) {
@@ -381,16 +415,16 @@ int launch_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X3Plan
     int64_t tiles = (int64_t)p.tiles_m * p.tiles_n * p.splits;
     int sms = g.max_sms > 0 && g.max_sms < ctx->sm_count ? g.max_sms : ctx->sm_count;
     int grid = (int)(tiles < sms ? tiles : sms);
-    gemm_tc_kernel<TIn, A_MN, B_MN, BN, X3><<<grid, kThreads, G::SMEM, st>>>(ta, tb, tc, p);
+    gemm_tc_kernel<TIn, A_MN, B_MN, BN, X3, SPLIT_C><<<grid, kThreads, G::SMEM, st>>>(ta, tb, tc, ta2, tc2, p);
     count_launch(ctx);
     RT_CUDA(cudaGetLastError());
     if (splits > 1) return launch_splitk_reduce(ctx, gr, st);
     return RT_OK;
 }
 
-template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3>
+template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3, bool SPLIT_C = false>
 int set_smem_attr() {
-    RT_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<TIn, A_MN, B_MN, BN, X3>,
+    RT_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<TIn, A_MN, B_MN, BN, X3, SPLIT_C>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<TIn, BN>::SMEM));
     return RT_OK;
 }
@@ -400,11 +434,20 @@ int set_smem_attrs_bn() {
     RT_TRY((set_smem_attr<TIn, false, true, BN, X3>()));
     RT_TRY((set_smem_attr<TIn, false, false, BN, X3>()));
     RT_TRY((set_smem_attr<TIn, true, true, BN, X3>()));
+    if constexpr (!X3) RT_TRY((set_smem_attr<TIn, false, true, BN, X3, true>()));  // forward with c_lo
     return RT_OK;
 }
 
+// The forward (NN) layout with a low-order output plane has its own
+// instantiation (SPLIT_C), so the other kernels carry none of its epilogue.
 template <typename TIn, int BN, bool X3 = false>
 int launch_layout(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X3Planes* x3 = nullptr) {
+    if constexpr (!X3) {
+        if (g.c_lo) {
+            if (g.layout != RT_NN) return fail(RT_ERR_UNSUPPORTED, "c_lo is supported for the NN layout only");
+            return launch_variant<TIn, false, true, BN, X3, true>(ctx, g, st, x3);
+        }
+    }
     switch (g.layout) {
         case RT_NN: return launch_variant<TIn, false, true, BN, X3>(ctx, g, st, x3);
         case RT_NT: return launch_variant<TIn, false, false, BN, X3>(ctx, g, st, x3);
@@ -434,6 +477,7 @@ bool gemm_tc_supported(const rt_ctx* ctx, const GemmDesc& g) {
     if (g.m >= (1ll << 31) || g.n >= (1ll << 31) || g.k >= (1ll << 31)) return false;
     const int64_t es = 2, os = g.out_dtype == RT_BF16 ? 2 : 4;
     if (!aligned16(g.a) || !aligned16(g.b) || !aligned16(g.c)) return false;
+    if ((g.a_lo && !aligned16(g.a_lo)) || (g.c_lo && !aligned16(g.c_lo))) return false;
     if ((g.lda * es) % 16 || (g.ldb * es) % 16 || (g.ldc * os) % 16) return false;
     if (g.epi == RT_EPI_RELU_MASK && (!aligned16(g.mask) || (g.ldmask * os) % 16)) return false;
     return true;

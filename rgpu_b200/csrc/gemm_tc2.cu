@@ -121,10 +121,13 @@ struct Geo2 {
     static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
 };
 
-template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false>
+// Split bf16 A (p.split_a) and a bf16 output's low-order plane (p.c_lo): as
+// in the one-CTA kernel, through tmap_a2 and tmap_c2.
+template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false, bool SPLIT_C = false>
 __global__ void __launch_bounds__(kThreads2, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                    const __grid_constant__ CUtensorMap tmap_c, TcParams p) {
+                    const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CUtensorMap tmap_a2,
+                    const __grid_constant__ CUtensorMap tmap_c2, TcParams p) {
     static_assert(!X3 || (sizeof(TIn) == 4 && !A_MN && !B_MN), "3xTF32 planes are f32 and K-major");
     using G = Geo2<TIn, BN>;
     constexpr bool kTF32 = sizeof(TIn) == 4;
@@ -169,6 +172,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
         prefetch_tmap(&tmap_a);
         prefetch_tmap(&tmap_b);
         if (p.tma_store) prefetch_tmap(&tmap_c);
+        if (p.split_a) prefetch_tmap(&tmap_a2);
+        if (SPLIT_C && p.tma_store) prefetch_tmap(&tmap_c2);
     }
     if (warp == 2) {
         asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -218,13 +223,19 @@ __global__ void __launch_bounds__(kThreads2, 1)
                     tma_load_3d_pair(sa, &tmap_a, k0, m0, seg == 0 ? 1 : 0, leader_full);
                     tma_load_3d_pair(sb, &tmap_b, k0, n0, seg == 1 ? 1 : 0, leader_full);
                 } else {
-                    const int k0 = kb * G::BK;
+                    int k0 = kb * G::BK;
+                    const CUtensorMap* map_a = &tmap_a;
+                    if (p.split_a) {
+                        const int seg = kb / p.kb_seg;  // 0: A's low-order plane, 1: A
+                        k0 = (kb - seg * p.kb_seg) * G::BK;
+                        if (seg == 0) map_a = &tmap_a2;
+                    }
                     if (A_MN) {
 #pragma unroll
                         for (int c = 0; c < 128 / G::CHUNK; ++c)
-                            tma_load_2d_pair(sa + c * (G::BK * 128), &tmap_a, m0 + c * G::CHUNK, k0, leader_full);
+                            tma_load_2d_pair(sa + c * (G::BK * 128), map_a, m0 + c * G::CHUNK, k0, leader_full);
                     } else {
-                        tma_load_2d_pair(sa, &tmap_a, k0, m0, leader_full);
+                        tma_load_2d_pair(sa, map_a, k0, m0, leader_full);
                     }
                     if (B_MN) {
 #pragma unroll
@@ -335,7 +346,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
                     uint8_t* box = smem_epi + (warp - 4) * kStageBytes;
                     if (p.out_bf16) {
                         if (row < p.m) epilogue_math<__nv_bfloat16>(p, row, col0, v);
-                        stage_and_store<__nv_bfloat16>(&tmap_c, box, lane, row0, col0, v);
+                        if constexpr (SPLIT_C)
+                            stage_and_store_split(&tmap_c, &tmap_c2, box, lane, row0, col0, v);
+                        else
+                            stage_and_store<__nv_bfloat16>(&tmap_c, box, lane, row0, col0, v);
                     } else {
                         if (row < p.m) epilogue_math<float>(p, row, col0, v);
                         stage_and_store<float>(&tmap_c, box, lane, row0, col0, v);
@@ -359,7 +373,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
                             opt_apply_row<32>(p.opt, row * p.ldc + col0, v, cnt);
                         }
                         if (p.out_bf16)
-                            epilogue_chunk<__nv_bfloat16>(p, row, col0, v);
+                            epilogue_chunk<__nv_bfloat16, SPLIT_C>(p, row, col0, v);
                         else
                             epilogue_chunk<float>(p, row, col0, v);
                     }
@@ -402,19 +416,27 @@ __global__ void __launch_bounds__(kThreads2, 1)
     }
 }
 
-template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false>
+template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false, bool SPLIT_C = false>
 int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X3Planes* x3 = nullptr) {
     using G = Geo2<TIn, BN>;
     const bool bf16 = sizeof(TIn) == 2;
-    CUtensorMap ta, tb, tc;
+    CUtensorMap ta, tb, tc, ta2, tc2;
     if constexpr (X3) {
         RT_TRY(make_tmap_planes(&ta, x3->a, g.k, g.m, x3->lda, x3->a_plane, 2, G::BK, 128));
         RT_TRY(make_tmap_planes(&tb, x3->b, g.k, g.n, x3->ldb, x3->b_plane, 2, G::BK, G::BNH));
+        ta2 = ta;
     } else {
         if (A_MN)
             RT_TRY(make_tmap(&ta, g.a, bf16, g.m, g.k, g.lda, G::CHUNK, G::BK));
         else
             RT_TRY(make_tmap(&ta, g.a, bf16, g.k, g.m, g.lda, G::BK, 128));
+        ta2 = ta;
+        if (g.a_lo) {  // A's low-order plane: the same geometry
+            if (A_MN)
+                RT_TRY(make_tmap(&ta2, g.a_lo, bf16, g.m, g.k, g.lda, G::CHUNK, G::BK));
+            else
+                RT_TRY(make_tmap(&ta2, g.a_lo, bf16, g.k, g.m, g.lda, G::BK, 128));
+        }
         if (B_MN)
             RT_TRY(make_tmap(&tb, g.b, bf16, g.n, g.k, g.ldb, G::CHUNK, G::BK));
         else
@@ -433,7 +455,14 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X
     if constexpr (X3) {
         p.kb_seg = p.kblocks;
         p.kblocks *= 3;
+    } else {
+        if (g.a_lo) {
+            p.split_a = 1;
+            p.kb_seg = p.kblocks;
+            p.kblocks *= 2;
+        }
     }
+    p.c_lo = g.c_lo;
     int splits = g.split_k > 1 ? g.split_k : 1;
     if (splits > p.kblocks) splits = p.kblocks;
     p.kb_per_split = (p.kblocks + splits - 1) / splits;
@@ -454,6 +483,7 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X
     p.tma_store = 0;
     p.p2p = g.p2p;
     tc = ta;  // unused unless a staged store is chosen
+    tc2 = ta;
     if (g.p2p.world > 0) {
         // scattered over peer memory: one k slice, f32 gradient, no fused update
         if (splits != 1 || p.out_bf16 || g.opt.kind)
@@ -462,6 +492,7 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X
     } else if (ctx->tma_store && splits == 1 && !g.opt.kind) {
         p.tma_store = 1;
         RT_TRY(make_tmap_out(&tc, g.c, p.out_bf16 != 0, g.m, g.n, g.ldc));
+        if (g.c_lo) RT_TRY(make_tmap_out(&tc2, g.c_lo, true, g.m, g.n, g.ldc));
     } else if (ctx->tma_store && splits == 1 && !p.out_bf16) {
         p.tma_store = 3;  // fused optimiser through the epilogue boxes
     } else if (ctx->tma_store && splits > 1 && g.n % 4 == 0 && (reinterpret_cast<uintptr_t>(g.workspace) & 15) == 0) {
@@ -485,14 +516,20 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    RT_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3>, ta, tb, tc, p));
+    RT_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3, SPLIT_C>, ta, tb, tc, ta2, tc2, p));
     count_launch(ctx);
     if (splits > 1) return launch_splitk_reduce(ctx, gr, st);
     return RT_OK;
 }
 
+// The forward (NN) layout with a low-order output plane has its own
+// instantiation (SPLIT_C), so the other kernels carry none of its epilogue.
 template <int BN>
 int launch_pair_layout(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
+    if (g.c_lo) {
+        if (g.layout != RT_NN) return fail(RT_ERR_UNSUPPORTED, "c_lo is supported for the NN layout only");
+        return launch_pair_variant<__nv_bfloat16, false, true, BN, false, true>(ctx, g, st);
+    }
     switch (g.layout) {
         case RT_NN: return launch_pair_variant<__nv_bfloat16, false, true, BN>(ctx, g, st);
         case RT_NT: return launch_pair_variant<__nv_bfloat16, false, false, BN>(ctx, g, st);
@@ -501,9 +538,9 @@ int launch_pair_layout(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     return fail(RT_ERR_INVALID, "unknown layout");
 }
 
-template <bool A_MN, bool B_MN, int BN, typename TIn = __nv_bfloat16, bool X3 = false>
+template <bool A_MN, bool B_MN, int BN, typename TIn = __nv_bfloat16, bool X3 = false, bool SPLIT_C = false>
 int set_attr_pair() {
-    RT_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3>,
+    RT_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3, SPLIT_C>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, Geo2<TIn, BN>::SMEM));
     return RT_OK;
 }
@@ -520,6 +557,8 @@ int gemm_tc2_init(rt_ctx* ctx) {
     RT_TRY((set_attr_pair<true, true, 256>()));
     RT_TRY((set_attr_pair<false, false, 128, float, true>()));
     RT_TRY((set_attr_pair<false, false, 256, float, true>()));
+    RT_TRY((set_attr_pair<false, true, 128, __nv_bfloat16, false, true>()));  // forward with c_lo
+    RT_TRY((set_attr_pair<false, true, 256, __nv_bfloat16, false, true>()));
     return RT_OK;
 }
 

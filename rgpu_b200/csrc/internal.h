@@ -113,6 +113,11 @@ struct GemmDesc {
     size_t x3_ws_bytes;
     bool no_alloc;     // the call may not allocate device memory (3xTF32 then needs a ready workspace)
     P2PScatter p2p;    // world > 0: the epilogue scatters rows to their owners (tensor-core path, one k slice)
+    // Split bf16 planes (bf16 only; same layout and leading dimension as the
+    // plane they pair with): C = (A + a_lo) B, and the epilogue result v is
+    // stored as bf16(v) in c plus bf16(v - bf16(v)) in c_lo.
+    const void* a_lo;
+    void* c_lo;
 };
 
 // Peer memory of a communicator's ranks (comm.cu).

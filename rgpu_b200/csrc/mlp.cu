@@ -71,6 +71,7 @@ struct PlanLayer {
     float* g = nullptr;              // gradient [d+1, ld]: dW rows 0..d-1, db row d
     float* db = nullptr;             // = g + d*ld
     void* act = nullptr;    // hidden: A_l [n, ld_act] (operand dtype); last: logits f32 [n, ld]
+    void* act_lo = nullptr; // split-activation bf16 plans, layers feeding a hidden layer: A_l's low-order plane
     void* delta = nullptr;  // delta_l [n, ld] (operand dtype)
     int split_dw = 1;
     float* ws = nullptr;    // split-K partials for the dW GEMM
@@ -114,6 +115,13 @@ struct rt_mlp {
     std::vector<int64_t> dims;
     std::vector<PlanLayer> L;
     rt_dtype adt = RT_F32;
+    // bf16 plans with RT_ACT_SPLIT: every hidden activation that feeds another
+    // hidden layer is stored as the pair hi = bf16(a) (act) and lo =
+    // bf16(a - hi) (act_lo); that layer's forward GEMM reads both, the dW
+    // GEMMs and the ReLU masks read hi.  The output layer's input needs no lo
+    // plane: its rounding moves the logits by ~1e-3 of their spread and flips
+    // no ReLU mask.
+    bool split_act = false;
     int64_t n = 0, ldx = 0;
     Slot slot[2];
     int next_slot = 0;
@@ -301,6 +309,10 @@ struct Enqueuer {
             g.epi = last ? RT_EPI_BIAS : RT_EPI_BIAS_RELU;
             g.bias = P.b;
             g.split_k = 1;
+            if (m->split_act) {
+                if (l > 0 && !last) g.a_lo = m->L[l - 1].act_lo;  // hidden layer: (A_hi + A_lo) W
+                if (l + 2 < nl) g.c_lo = P.act_lo;                // A_l feeds a hidden layer: hi and lo planes
+            }
             g.x3_ws = m->x3_ws;
             g.x3_ws_bytes = m->x3_ws_bytes;
             RT_TRY(run_gemm(m->ctx, g, st, 0));
@@ -755,6 +767,8 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
     RT_CHECK(cfg->batch >= 1, "rt_mlp_create: batch must be >= 1");
     RT_CHECK(cfg->dtype == RT_F32 || cfg->dtype == RT_BF16, "rt_mlp_create: dtype must be RT_F32 or RT_BF16");
     RT_CHECK(cfg->optimizer >= RT_OPT_NONE && cfg->optimizer <= RT_OPT_ADAM, "rt_mlp_create: unknown optimizer");
+    RT_CHECK(cfg->activations == RT_ACT_SPLIT || cfg->activations == RT_ACT_BF16,
+             "rt_mlp_create: unknown activations mode %d", (int)cfg->activations);
     for (int l = 0; l <= cfg->n_layers; ++l) RT_CHECK(cfg->dims[l] >= 1, "rt_mlp_create: dims[%d] < 1", l);
     for (int l = 0; l < cfg->n_layers; ++l) RT_CHECK(weights[l] != nullptr, "rt_mlp_create: weights[%d] is NULL", l);
     RT_CUDA(cudaSetDevice(ctx->device));
@@ -764,6 +778,7 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
     m->dims.assign(cfg->dims, cfg->dims + cfg->n_layers + 1);
     m->cfg.dims = m->dims.data();
     m->adt = cfg->dtype;
+    m->split_act = m->adt == RT_BF16 && cfg->activations == RT_ACT_SPLIT;
     m->n = cfg->batch;
     const size_t es = dtype_size(m->adt);
     const int nl = cfg->n_layers;
@@ -808,6 +823,8 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
         }
         if (m->adt == RT_BF16 && (s = dalloc_t(m, &P.w16, pn))) return bail(s);
         if ((s = dalloc(m, &P.act, (size_t)m->n * P.ld_act * (last ? 4 : es)))) return bail(s);
+        if (l + 2 < nl && m->split_act && (s = dalloc(m, &P.act_lo, (size_t)m->n * P.ld_act * es)))
+            return bail(s);
         if (!last && (s = launch_fill_column(ctx, P.act, m->adt, m->n, P.ld_act, P.u, 1.0f, ctx->stream)))
             return bail(s);
         if ((s = dalloc(m, &P.delta, (size_t)m->n * P.ld * es))) return bail(s);

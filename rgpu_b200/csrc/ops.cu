@@ -27,6 +27,12 @@ static int check_gemm(const GemmDesc& g) {
         RT_CHECK(g.mask, "relu-mask epilogue without a mask");
         RT_CHECK(g.ldmask >= g.n, "ldmask too small");
     }
+    if (g.a_lo) RT_CHECK(g.in_dtype == RT_BF16, "a_lo (low-order plane of A) needs bf16 operands");
+    if (g.c_lo) {
+        RT_CHECK(g.out_dtype == RT_BF16, "c_lo (low-order plane of C) needs a bf16 output");
+        RT_CHECK(g.split_k <= 1 && !g.opt.kind && g.p2p.world == 0,
+                 "c_lo needs one k slice and no fused update or peer scatter");
+    }
     return RT_OK;
 }
 
@@ -110,7 +116,7 @@ int run_gemm(rt_ctx* ctx, GemmDesc g, cudaStream_t stream, size_t ws_bytes) {
         return launch_gemm_tc(ctx, g, stream);
     }
     if (g.split_k <= 0) {
-        g.split_k = choose_split(ctx, g);
+        g.split_k = g.c_lo ? 1 : choose_split(ctx, g);
         if ((size_t)g.split_k * g.m * g.n * 4 > ws_bytes || !g.workspace) g.split_k = 1;
     }
     if (g.k == 0) g.split_k = 1;
@@ -188,6 +194,8 @@ int rt_gemm(rt_ctx* ctx, const rt_gemm_args* a) {
     g.ldmask = a->ldmask;
     g.split_k = a->split_k;
     g.workspace = (float*)a->workspace;
+    g.a_lo = a->a_lo;
+    g.c_lo = a->c_lo;
     return run_gemm(ctx, g, ctx->stream, a->workspace ? a->workspace_bytes : 0);
 }
 
@@ -198,7 +206,7 @@ size_t rt_gemm_workspace_size(rt_ctx* ctx, const rt_gemm_args* a) {
     g.m = a->m;
     g.n = a->n;
     g.k = a->k;
-    int s = a->split_k > 0 ? a->split_k : choose_split(ctx, g);
+    int s = a->split_k > 0 ? a->split_k : a->c_lo ? 1 : choose_split(ctx, g);
     return s > 1 ? (size_t)s * (size_t)a->m * (size_t)a->n * 4 : 0;
 }
 

@@ -204,6 +204,10 @@ struct TcParams {
                     // 3 = fused optimiser through the staging boxes (opt_chunk), 4 = rows scattered to
                     // their owners' receive buffers over peer memory (p2p_chunk), 0 = direct stores
     P2PScatter p2p;
+    // Split bf16 A (a_lo): the k loop runs two segments of kb_seg blocks over the same k
+    // range, A's low-order plane (tmap_a2) first, then A itself; B is the same in both.
+    int split_a;
+    void* c_lo;  // bf16 output's low-order plane (same ldc): bf16(v - bf16(v)); null = none
 };
 
 // Epilogue staging: one 32 x 32 output chunk per epilogue warp (4 KB), the
@@ -295,21 +299,27 @@ __device__ __forceinline__ void epilogue_math(const TcParams& p, int64_t row, in
     }
 }
 
-// Direct stores of one row's 32 columns (the thread's own row).
-template <typename TOut>
-__device__ __forceinline__ void store_chunk(const TcParams& p, int64_t row, int64_t col0, const float (&v)[32]) {
-    const int64_t n = p.n;
+// Low-order part of an epilogue result: v - bf16(v), exact in f32 (v and its
+// bf16 rounding share the exponent range), rounded to bf16 where it is stored.
+__device__ __forceinline__ float lo_part(float v) { return v - __bfloat162float(__float2bfloat16_rn(v)); }
+
+// Direct stores of one row's 32 columns (the thread's own row) to `base`
+// (row stride ldc); LO stores the low-order parts of the bf16 rounding.
+template <typename TOut, bool LO = false>
+__device__ __forceinline__ void store_chunk_to(void* base, int64_t ldc, int64_t n, int64_t row, int64_t col0,
+                                               const float (&v)[32]) {
     const bool full = col0 + 32 <= n;
     if constexpr (sizeof(TOut) == 2) {
-        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.c) + row * p.ldc + col0;
+        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(base) + row * ldc + col0;
+        auto val = [&](int j) { return LO ? lo_part(v[j]) : v[j]; };
         if (full) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 uint4 u;
-                __nv_bfloat162 h0 = __floats2bfloat162_rn(v[q * 8 + 0], v[q * 8 + 1]);
-                __nv_bfloat162 h1 = __floats2bfloat162_rn(v[q * 8 + 2], v[q * 8 + 3]);
-                __nv_bfloat162 h2 = __floats2bfloat162_rn(v[q * 8 + 4], v[q * 8 + 5]);
-                __nv_bfloat162 h3 = __floats2bfloat162_rn(v[q * 8 + 6], v[q * 8 + 7]);
+                __nv_bfloat162 h0 = __floats2bfloat162_rn(val(q * 8 + 0), val(q * 8 + 1));
+                __nv_bfloat162 h1 = __floats2bfloat162_rn(val(q * 8 + 2), val(q * 8 + 3));
+                __nv_bfloat162 h2 = __floats2bfloat162_rn(val(q * 8 + 4), val(q * 8 + 5));
+                __nv_bfloat162 h3 = __floats2bfloat162_rn(val(q * 8 + 6), val(q * 8 + 7));
                 u.x = *reinterpret_cast<uint32_t*>(&h0);
                 u.y = *reinterpret_cast<uint32_t*>(&h1);
                 u.z = *reinterpret_cast<uint32_t*>(&h2);
@@ -319,10 +329,10 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, int64_t row, int6
         } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-                if (col0 + j < n) dst[j] = __float2bfloat16_rn(v[j]);
+                if (col0 + j < n) dst[j] = __float2bfloat16_rn(val(j));
         }
     } else {
-        float* dst = static_cast<float*>(p.c) + row * p.ldc + col0;
+        float* dst = static_cast<float*>(base) + row * ldc + col0;
         if (full) {
 #pragma unroll
             for (int q = 0; q < 8; ++q)
@@ -335,10 +345,12 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, int64_t row, int6
     }
 }
 
-template <typename TOut>
+// SPLIT_C: the kernel instantiation that also stores the low-order plane c_lo.
+template <typename TOut, bool SPLIT_C = false>
 __device__ __forceinline__ void epilogue_chunk(const TcParams& p, int64_t row, int64_t col0, float (&v)[32]) {
     epilogue_math<TOut>(p, row, col0, v);
-    store_chunk<TOut>(p, row, col0, v);
+    store_chunk_to<TOut>(p.c, p.ldc, p.n, row, col0, v);
+    if constexpr (SPLIT_C && sizeof(TOut) == 2) store_chunk_to<TOut, true>(p.c_lo, p.ldc, p.n, row, col0, v);
 }
 
 // Writes lane `lane`'s row of a 32 x 32 chunk into the warp's staging box,
@@ -346,17 +358,18 @@ __device__ __forceinline__ void epilogue_chunk(const TcParams& p, int64_t row, i
 // unit q of row r at q ^ (r & 7)), bf16 rows 64 bytes (unit q at
 // q ^ ((r >> 1) & 3)).  Each 8-lane phase of a 16-byte store then covers all
 // 32 banks once.
-template <typename TOut>
+template <typename TOut, bool LO = false>
 __device__ __forceinline__ void stage_row(uint8_t* box, int lane, const float (&v)[32]) {
     if constexpr (sizeof(TOut) == 2) {
         uint8_t* row = box + lane * 64;
+        auto val = [&](int j) { return LO ? lo_part(v[j]) : v[j]; };
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             uint4 u;
-            __nv_bfloat162 h0 = __floats2bfloat162_rn(v[q * 8 + 0], v[q * 8 + 1]);
-            __nv_bfloat162 h1 = __floats2bfloat162_rn(v[q * 8 + 2], v[q * 8 + 3]);
-            __nv_bfloat162 h2 = __floats2bfloat162_rn(v[q * 8 + 4], v[q * 8 + 5]);
-            __nv_bfloat162 h3 = __floats2bfloat162_rn(v[q * 8 + 6], v[q * 8 + 7]);
+            __nv_bfloat162 h0 = __floats2bfloat162_rn(val(q * 8 + 0), val(q * 8 + 1));
+            __nv_bfloat162 h1 = __floats2bfloat162_rn(val(q * 8 + 2), val(q * 8 + 3));
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(val(q * 8 + 4), val(q * 8 + 5));
+            __nv_bfloat162 h3 = __floats2bfloat162_rn(val(q * 8 + 6), val(q * 8 + 7));
             u.x = *reinterpret_cast<uint32_t*>(&h0);
             u.y = *reinterpret_cast<uint32_t*>(&h1);
             u.z = *reinterpret_cast<uint32_t*>(&h2);
@@ -389,6 +402,25 @@ __device__ __forceinline__ void stage_and_store(const CUtensorMap* tmap_c, uint8
             tma_store_2d(tmap_c, smem_u32(box), (int32_t)col0, (int32_t)row0);
         else
             tma_store_3d(tmap_c, smem_u32(box), (int32_t)col0, (int32_t)row0, split);
+        bulk_commit();
+    }
+}
+
+// The same for a bf16 chunk with a low-order plane: the warp's 4 KB box holds
+// the chunk's bf16(v) in its first 2 KB and bf16(v - bf16(v)) in its second,
+// stored through the C map and the c_lo map in one bulk group.
+__device__ __forceinline__ void stage_and_store_split(const CUtensorMap* tmap_hi, const CUtensorMap* tmap_lo,
+                                                      uint8_t* box, int lane, int64_t row0, int64_t col0,
+                                                      const float (&v)[32]) {
+    if (lane == 0) bulk_wait_read_all();
+    __syncwarp();
+    stage_row<__nv_bfloat16>(box, lane, v);
+    stage_row<__nv_bfloat16, true>(box + kStageBytes / 2, lane, v);
+    fence_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(tmap_hi, smem_u32(box), (int32_t)col0, (int32_t)row0);
+        tma_store_2d(tmap_lo, smem_u32(box + kStageBytes / 2), (int32_t)col0, (int32_t)row0);
         bulk_commit();
     }
 }

@@ -24,9 +24,11 @@ RT_F32, RT_BF16, RT_U32 = 0, 1, 2
 RT_NN, RT_NT, RT_TN = 0, 1, 2
 RT_EPI_NONE, RT_EPI_BIAS, RT_EPI_BIAS_RELU, RT_EPI_RELU_MASK = 0, 1, 2, 3
 RT_OPT_NONE, RT_OPT_SGD, RT_OPT_ADAM = 0, 1, 2
+RT_ACT_SPLIT, RT_ACT_BF16 = 0, 1
 
 _DTYPES = {"f32": RT_F32, "float32": RT_F32, "bf16": RT_BF16, "bfloat16": RT_BF16, "u32": RT_U32}
 _OPTS = {"none": RT_OPT_NONE, "sgd": RT_OPT_SGD, "adam": RT_OPT_ADAM}
+_ACTS = {"split": RT_ACT_SPLIT, "bf16": RT_ACT_BF16}
 
 
 class RtError(RuntimeError):
@@ -45,6 +47,7 @@ class GemmArgs(C.Structure):
         ("epilogue", C.c_int), ("bias", C.c_void_p),
         ("mask", C.c_void_p), ("ldmask", C.c_int64),
         ("split_k", C.c_int), ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
+        ("a_lo", C.c_void_p), ("c_lo", C.c_void_p),
     ]
 
 
@@ -53,6 +56,7 @@ class MlpConfig(C.Structure):
         ("n_layers", C.c_int), ("dims", C.POINTER(C.c_int64)), ("batch", C.c_int64),
         ("global_batch", C.c_int64), ("dtype", C.c_int), ("optimizer", C.c_int),
         ("lr", C.c_float), ("beta1", C.c_float), ("beta2", C.c_float), ("eps", C.c_float),
+        ("activations", C.c_int),
     ]
 
 
@@ -446,9 +450,14 @@ class GpuMlp:
 
     @classmethod
     def from_params(cls, gpu: Gpu, params, batch: int, lr: float, *, dtype="f32", optimizer="adam",
-                    global_batch: int | None = None, beta1=0.9, beta2=0.999, eps=1e-8) -> "GpuMlp":
+                    global_batch: int | None = None, beta1=0.9, beta2=0.999, eps=1e-8,
+                    activations="split") -> "GpuMlp":
         """params = [W1, b1, W2, b2, ...] as Sequential::params() returns them
-        (nn.rs:190-192); W_l is [d_l, d_{l+1}], b_l is [1, d_{l+1}]."""
+        (nn.rs:190-192); W_l is [d_l, d_{l+1}], b_l is [1, d_{l+1}].
+        ``activations`` (bf16 plans): "split" keeps each hidden activation as a
+        bf16 hi + lo pair for the next forward GEMM (the default, within the
+        2e-2 parity bar), "bf16" rounds it once (faster forward, hidden-layer
+        gradients 2e-2 .. 8e-2 from the f32 reference)."""
         assert len(params) % 2 == 0 and params, "expected (W, b) pairs"
         ws = [np.ascontiguousarray(params[i], np.float32) for i in range(0, len(params), 2)]
         bs = [np.ascontiguousarray(params[i], np.float32).ravel() for i in range(1, len(params), 2)]
@@ -457,7 +466,7 @@ class GpuMlp:
             assert w.shape == (dims[l], dims[l + 1]), "inconsistent layer shapes"
         dims_arr = (C.c_int64 * len(dims))(*dims)
         cfg = MlpConfig(len(ws), dims_arr, batch, global_batch or 0, _dt(dtype), _OPTS[optimizer], lr, beta1,
-                        beta2, eps)
+                        beta2, eps, _ACTS[activations])
         wp = (C.c_void_p * len(ws))(*[w.ctypes.data for w in ws])
         bp = (C.c_void_p * len(bs))(*[b.ctypes.data for b in bs])
         h = C.c_void_p()

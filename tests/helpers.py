@@ -47,3 +47,24 @@ def baseline_inputs(dims, batch, seed):
     x = rng.normal(batch * dims[0]).reshape(batch, dims[0])
     labels = rng.below(dims[-1], batch)
     return m, x, labels
+
+
+def bf16_round(a) -> np.ndarray:
+    """Nearest-even bf16 value of each f32 element, widened back to f32."""
+    a = np.ascontiguousarray(a, np.float32)
+    u = a.view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+    return r.astype(np.uint32).view(np.float32).reshape(a.shape)
+
+
+def bf16_baseline_inputs(dims, batch, seed):
+    """baseline_inputs for the bf16 configs ("bf16 inputs/weights with fp32
+    accumulate and fp32 master weights"): x and W are rounded to bf16 values,
+    so the CPU reference and the GPU plan start from identical inputs and
+    weights, and the f32 masters begin equal to their bf16 shadows."""
+    m, x, labels = baseline_inputs(dims, batch, seed)
+    params = m.params()
+    for l in range(0, len(params), 2):
+        params[l] = bf16_round(params[l])
+    m.set_params(params)
+    return m, bf16_round(x), labels

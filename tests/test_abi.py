@@ -30,7 +30,32 @@ def test_python_mirror_binds_every_declared_symbol():
 
 
 def test_abi_version():
-    assert G.lib().rt_abi_version() == 1
+    assert G.lib().rt_abi_version() == 2
+
+
+def test_python_structs_match_the_header_layout(tmp_path):
+    # The ctypes mirrors of rt_gemm_args and rt_mlp_config must have the C
+    # structs' size and field offsets (compiled from include/rtgpu.h by gcc).
+    import ctypes as C
+    import subprocess
+
+    structs = {"rt_gemm_args": G.GemmArgs, "rt_mlp_config": G.MlpConfig}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "rtgpu.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
+        for f, _ in py._fields_:
+            lines.append(f'printf("{cname} {f} %zu\\n", offsetof({cname}, {f}));')
+    lines.append("return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    got = {tuple(l.split()[:2]): int(l.split()[2]) for l in out if l}
+    for cname, py in structs.items():
+        assert got[(cname, "size")] == C.sizeof(py), cname
+        for f, _ in py._fields_:
+            assert got[(cname, f)] == getattr(py, f).offset, (cname, f)
 
 
 def test_no_device_is_reported_not_faked():

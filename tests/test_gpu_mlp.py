@@ -1,16 +1,18 @@
 """Whole-step parity of GpuMlp (the captured CUDA-graph train step) against the
 CPU oracle's tape-driven step, on identical seeded inputs and weights.
 
-Mirrors crates/rtensor/tests/gpu.rs:62-213 and adds the BASELINE configs at
-sizes the oracle finishes in seconds, with the north-star tolerances:
-relative L2 <= 1e-4 per gradient for f32, <= 2e-2 for bf16 operands.
+Mirrors crates/rtensor/tests/gpu.rs:62-213 and adds the BASELINE configs
+(config 3 at its full batch of 8192 too), with the north-star tolerances:
+relative L2 <= 1e-4 per gradient for f32, <= 2e-2 for bf16 operands.  The
+bf16 configs take bf16 inputs and weights, so the plain f32 CPU reference is
+given exactly the values the GPU plan starts from.
 """
 import numpy as np
 import pytest
 
 import oracle
 import rgpu_b200
-from tests.helpers import baseline_inputs, erro_rel, glorot_model, quadrant_data, rel_l2
+from tests.helpers import baseline_inputs, bf16_baseline_inputs, erro_rel, glorot_model, quadrant_data, rel_l2
 
 pytestmark = pytest.mark.gpu
 
@@ -130,70 +132,91 @@ def test_config2_f32_batch2048(gpu):
     assert abs(loss_cpu - loss_gpu) < 1e-4
 
 
-def _wide_bf16_grads(gpu, dims, n, seed, fast):
-    model, x, labels = baseline_inputs(dims, n, seed)
+def _wide_bf16_grads(gpu, dims, n, seed, fast, activations="split", optimizer="none", lr=0.0):
+    model, x, labels = bf16_baseline_inputs(dims, n, seed)
     gpu.set_fast_gemm(fast)
     try:
-        mlp = rgpu_b200.GpuMlp.from_params(gpu, model.params(), n, 0.0, dtype="bf16", optimizer="none")
-        mlp.step(gpu.upload(x), rgpu_b200.upload_labels(gpu, labels))
+        mlp = rgpu_b200.GpuMlp.from_params(gpu, model.params(), n, lr, dtype="bf16", optimizer=optimizer,
+                                           activations=activations)
+        mlp.step(gpu.upload(x, "bf16"), rgpu_b200.upload_labels(gpu, labels))
         grads = mlp.grads()
+        loss = mlp.last_loss()
         mlp.close()
     finally:
         gpu.set_fast_gemm(True)
-    return model, x, labels, grads
+    return model, x, labels, grads, loss
 
 
-def test_bf16_step_logic_matches_bf16_oracle_exactly(gpu):
-    # The bf16 plan's rounding points (x, W shadow, activations, deltas) and
-    # step logic, isolated from accumulation order: the SIMT kernels sum k in
-    # the oracle's order and bf16 x bf16 products are exact in f32, so the
-    # only differences left are the xent's lane-parallel sums.
+@pytest.mark.parametrize("activations,flags", [("split", oracle.BF16_SPLIT), ("bf16", oracle.BF16_PLAIN)])
+def test_bf16_step_logic_tracks_the_rounding_point_oracle(gpu, activations, flags):
+    # The bf16 plan's rounding points and step logic, isolated from the
+    # tensor cores' accumulation order: the SIMT kernels sum k in the
+    # oracle's order, and bf16 x bf16 (or (hi + lo) x bf16) products are exact
+    # in f32, so what is left is the softmax-CE kernel's lane-parallel sums,
+    # which can move a delta across a bf16 rounding boundary.  Measured
+    # <= 4e-4; bound 1e-3.
     dims = [512, 1024, 1024, 1024, 100]
-    model, x, labels, grads = _wide_bf16_grads(gpu, dims, 256, 2027, fast=False)
-    model.set_bf16_emulation(True)
+    model, x, labels, grads, _ = _wide_bf16_grads(gpu, dims, 256, 2027, fast=False, activations=activations)
+    model.set_rounding(flags)
     model.train_step(x, labels, threads=8, input_grad=False)
     for i, (gc, gg) in enumerate(zip(model.grads(), grads)):
         assert rel_l2(gg, gc) <= 1e-3, f"param {i}: {rel_l2(gg, gc):.3e}"
 
 
-def test_bf16_wide_mlp_reduced_batch(gpu):
-    # BASELINE config 3 architecture (4096 -> 8192 x3 -> 1000) with bf16
-    # operands on the tensor-core path, f32 accumulate, f32 master weights, at
-    # a batch the oracle finishes in seconds.
-    #
-    # The tensor cores sum k in another order (and truncate), so each layer's
-    # output differs from the oracle's by ~1e-5 relative; bf16 rounding of the
-    # activations turns that into independent rounding noise (~2^-9), and
-    # hidden-layer gradients pick up ReLU-mask flips from it.  Measured on
-    # B200: output layer 1.6e-3 / 5e-4, hidden layers 2.1e-2 .. 2.5e-2 against
-    # the bf16-point oracle; 4.4e-3 (output) and 4.7e-2 .. 7.9e-2 (hidden)
-    # against the plain f32 reference.
+def test_bf16_wide_mlp_meets_the_bar_at_reduced_batch(gpu):
+    # BASELINE config 3's architecture (4096 -> 8192 x3 -> 1000), bf16 inputs
+    # and weights, f32 accumulate, on the tensor-core path with split
+    # activations (the default), against the plain f32 CPU reference given
+    # the same bf16 inputs and weights: every gradient within the north-star
+    # 2e-2 (measured <= 5e-3).  With single-bf16 activations the hidden-layer
+    # gradients are 2e-2 .. 8e-2 away (ReLU masks flipped by the activation
+    # rounding), which is why split activations are the default.
     dims = [4096, 8192, 8192, 8192, 1000]
-    model, x, labels, grads_gpu = _wide_bf16_grads(gpu, dims, 64, 2027, fast=True)
-    L = len(grads_gpu)
-    model.set_bf16_emulation(True)
-    model.train_step(x, labels, threads=8, input_grad=False)
-    for i, (gc, gg) in enumerate(zip(model.grads(), grads_gpu)):
-        bound = 2e-2 if i >= L - 2 else 4e-2
-        assert rel_l2(gg, gc) <= bound, f"param {i} vs bf16-point oracle: {rel_l2(gg, gc):.3e} > {bound}"
-    model.set_bf16_emulation(False)
-    model.train_step(x, labels, threads=8, input_grad=False)
+    model, x, labels, grads_split, loss_split = _wide_bf16_grads(gpu, dims, 64, 2027, fast=True)
+    _, _, _, grads_plain, _ = _wide_bf16_grads(gpu, dims, 64, 2027, fast=True, activations="bf16")
+    loss_cpu = model.train_step(x, labels, threads=8, input_grad=False)
     gref = model.grads()
-    for i in (L - 2, L - 1):
-        assert rel_l2(grads_gpu[i], gref[i]) <= 2e-2, f"output param {i}: {rel_l2(grads_gpu[i], gref[i]):.3e}"
-    for i, (gc, gg) in enumerate(zip(gref, grads_gpu)):
-        a, b = gg.ravel().astype(np.float64), gc.ravel().astype(np.float64)
-        cos = float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
-        assert cos >= 0.99, f"param {i}: cosine {cos:.4f}"
-        assert rel_l2(gg, gc) <= 0.12, f"param {i} vs f32: {rel_l2(gg, gc):.3e}"
+    errs = [rel_l2(g, r) for g, r in zip(grads_split, gref)]
+    for i, e in enumerate(errs):
+        assert e <= 2e-2, f"param {i}: rel L2 {e:.3e} > 2e-2 (all: {[f'{v:.2e}' for v in errs]})"
+    assert abs(loss_split - loss_cpu) < 1e-3
+    plain = [rel_l2(g, r) for g, r in zip(grads_plain, gref)]
+    assert max(plain[:6]) > 2 * max(errs[:6]), (plain, errs)
+
+
+def test_config3_full_batch_meets_the_bar(gpu):
+    # BASELINE config 3 exactly: 4096 -> 8192 -> 8192 -> 8192 -> 1000, bf16
+    # inputs/weights with f32 accumulate and f32 masters, Adam(1e-3), batch
+    # 8192, X ~ N(0,1), uniform labels, Kaiming init.  One step of the
+    # production plan (tensor cores, split activations, Adam fused into the
+    # dW GEMMs); its gradients against the plain f32 CPU reference on the
+    # same inputs and weights (crates/rtensor/tests/gpu.rs:62-97 is the
+    # reference's own GPU-vs-CPU gradient check), all host threads, with the
+    # north-star bar of 2e-2 relative L2 for every W and b.
+    import os
+
+    dims = [4096, 8192, 8192, 8192, 1000]
+    n = 8192
+    model, x, labels, grads, loss_gpu = _wide_bf16_grads(gpu, dims, n, 2024 + 3, fast=True, optimizer="adam",
+                                                         lr=1e-3)
+    loss_cpu = model.train_step(x, labels, threads=os.cpu_count() or 8, input_grad=False)
+    errs = [rel_l2(g, r) for g, r in zip(grads, model.grads())]
+    print("config 3, batch 8192: grad rel L2 " + " ".join(f"{e:.3e}" for e in errs) +
+          f"; loss GPU {loss_gpu:.6f} CPU {loss_cpu:.6f}")
+    for i, e in enumerate(errs):
+        assert e <= 2e-2, f"param {i} ({'W' if i % 2 == 0 else 'b'}{i // 2}): rel L2 {e:.3e} > 2e-2"
+    assert abs(loss_gpu - loss_cpu) < 1e-3
 
 
 def test_bf16_adam_step_updates_master_and_shadow(gpu):
+    # Five Adam steps: after the first, the GEMMs read the bf16 shadow of the
+    # updated f32 masters, so the oracle rounds its weights at use as well
+    # (the split-activation plan's rounding points).
     dims = [256, 512, 512, 100]
-    model, x, labels = baseline_inputs(dims, 256, 2028)
+    model, x, labels = bf16_baseline_inputs(dims, 256, 2028)
     mlp = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 256, 1e-3, dtype="bf16", optimizer="adam")
     gx, gy = gpu.upload(x), rgpu_b200.upload_labels(gpu, labels)
-    model.set_bf16_emulation(True)
+    model.set_rounding(oracle.BF16_SPLIT)
     loss_cpu = None
     for _ in range(5):
         loss_cpu = model.train_step(x, labels, oracle.OPT_ADAM, 1e-3, threads=4)
