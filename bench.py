@@ -38,21 +38,27 @@ CONFIGS = {
     # update fused into its epilogue), 1.6 GB on the device
     "probe_dw": dict(dims=[8192, 8192], batch=8192, dtype="bf16", optimizer="adam", lr=1e-3),
 }
+# the fixed global batch of the strong-scaling leg
+STRONG_GLOBAL_BATCH = 65536
 # Rows of the one-thread CPU baseline step (the full batch where that is quick)
 CPU_SAMPLE_ROWS = {"wide": 256, "small": 2048, "probe_dw": 256}
-# DRAM bytes (read + write) of one 8192 x 8192 x 8192 dW GEMM launch (the
-# two-CTA kernel), from an ncu capture (dram__bytes_read.sum +
-# dram__bytes_write.sum) of `bench.py --gemm TN --mnk 8192 8192 8192`; scaled
-# to other dW launches by their FLOPs.
-DW_GEMM_TRAFFIC_BYTES = 1.099e9 + 0.251e9
-DW_GEMM_TRAFFIC_FLOPS = 2.0 * 8192 ** 3
-# The same for the dW launch with the fused Adam update (the [W; b] block of
-# an 8192 -> 8192 layer at batch 8192: the dW GEMM of `bench.py --config
-# probe_dw`, 2 * 8192^3 FLOPs as the plan counts them, the bias row aside);
-# every dW launch of the wide step has k = 8192, so its bytes scale with its
-# FLOPs there too.
-DW_ADAM_TRAFFIC_BYTES = 2.187e9 + 1.183e9
-DW_ADAM_TRAFFIC_FLOPS = 2.0 * 8192 ** 3
+# DRAM bytes (read + write) per launch of the step's dominant kernels, each
+# from one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of an
+# 8192 x 8192 x 8192 launch (2 * 8192^3 algorithmic FLOPs), scaled to the
+# step's launches of that label by their FLOPs (every such launch of the wide
+# step has k = 8192, so its bytes grow with its FLOPs):
+#   dw_gemm       `bench.py --gemm TN --mnk 8192 8192 8192` (plain dW GEMM)
+#   dw_gemm_adam  the dW GEMM of `bench.py --config probe_dw` (Adam fused in
+#                 the epilogue; the [W; b] block of one 8192 -> 8192 layer)
+#   fwd_gemm_bias_relu_split  `bench.py --gemm NN --split --mnk 8192 8192 8192`
+#                 (A as bf16 hi + lo planes, bias + ReLU, bf16 output with its
+#                 lo plane: the forward GEMM of a hidden layer that feeds another)
+TRAFFIC_PER_LAUNCH = {
+    "dw_gemm": (1.099e9 + 0.251e9, "bench.py --gemm TN --mnk 8192 8192 8192"),
+    "dw_gemm_adam": (2.187e9 + 1.183e9, "the dW launch of bench.py --config probe_dw"),
+    "fwd_gemm_bias_relu_split": (2.605e9 + 0.259e9, "bench.py --gemm NN --split --mnk 8192 8192 8192"),
+}
+TRAFFIC_FLOPS = 2.0 * 8192 ** 3
 
 
 def peaks():
@@ -75,17 +81,42 @@ def exact_flops(dims, n):
     return float(f)
 
 
-def make_inputs(cfg, rows, seed):
+def make_weights(cfg, seed):
+    """Kaiming-uniform W, zero b (bf16 configs: W rounded to bf16 values, the
+    configs' bf16 weights; the f32 masters start equal to their shadows)."""
     rng = np.random.default_rng(seed)
     dims = cfg["dims"]
     params = []
     for l in range(len(dims) - 1):
         lim = np.float32(np.sqrt(6.0 / dims[l]))
-        params.append(rng.uniform(-lim, lim, size=(dims[l], dims[l + 1])).astype(np.float32))
+        w = rng.uniform(-lim, lim, size=(dims[l], dims[l + 1])).astype(np.float32)
+        if cfg["dtype"] == "bf16":
+            w = bf16_values(w)
+        params.append(w)
         params.append(np.zeros((1, dims[l + 1]), np.float32))
+    return params
+
+
+def make_data(cfg, rows, seed):
+    """X ~ N(0,1) (bf16 values for bf16 configs), labels uniform in [0, classes)."""
+    rng = np.random.default_rng(seed)
+    dims = cfg["dims"]
     x = rng.standard_normal((rows, dims[0]), dtype=np.float32)
+    if cfg["dtype"] == "bf16":
+        x = bf16_values(x)
     labels = rng.integers(0, dims[-1], size=rows, dtype=np.uint32)
-    return params, x, labels
+    return x, labels
+
+
+def make_inputs(cfg, rows, seed):
+    x, labels = make_data(cfg, rows, seed + 1)
+    return make_weights(cfg, seed), x, labels
+
+
+def bf16_values(a):
+    """Nearest-even bf16 value of each f32 element, as f32."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    return (((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16).astype(np.uint32).view(np.float32).reshape(a.shape)
 
 
 class ClockSampler:
@@ -292,10 +323,29 @@ def run_gemm_only(args):
     rng = np.random.default_rng(0)
     shape_a = (k, m) if args.gemm == "TN" else (m, k)
     shape_b = (n, k) if args.gemm == "NT" else (k, n)
-    a = gpu.upload(rng.standard_normal(shape_a, dtype=np.float32), args.gemm_dtype)
-    b = gpu.upload(rng.standard_normal(shape_b, dtype=np.float32), args.gemm_dtype)
-    c = gpu.zeros((m, n), "f32" if args.gemm == "TN" or args.gemm_dtype == "f32" else "bf16")
-    fn = {"NN": gpu.matmul, "NT": gpu.matmul_a_bt, "TN": gpu.matmul_at_b}[args.gemm]
+    if args.split:
+        # the split-activation forward GEMM of a hidden layer: A as bf16 hi
+        # and lo planes, bias + ReLU, bf16 output with its lo plane
+        from rgpu_b200 import gpu as G
+
+        assert args.gemm == "NN" and args.gemm_dtype == "bf16", "--split profiles the NN bf16 forward GEMM"
+        xa = np.maximum(rng.standard_normal(shape_a, dtype=np.float32), 0)
+        hi = rgpu_b200.bf16_to_f32(rgpu_b200.f32_to_bf16(xa))
+        a, a_lo = gpu.upload(hi, "bf16"), gpu.upload(xa - hi, "bf16")
+        b = gpu.upload(rng.standard_normal(shape_b, dtype=np.float32) * np.float32(0.01), "bf16")
+        bias = gpu.upload(np.zeros((1, n), np.float32))
+        c, c_lo = gpu.zeros((m, n), "bf16"), gpu.zeros((m, n), "bf16")
+        args_g = G.GemmArgs(G.RT_NN, G.RT_BF16, G.RT_BF16, m, n, k, a.ptr, a.ld, b.ptr, b.ld, c.ptr, c.ld,
+                            G.RT_EPI_BIAS_RELU, bias.ptr, None, 0, 1, None, 0)
+        args_g.a_lo, args_g.c_lo = a_lo.ptr, c_lo.ptr
+
+        def fn(*_):
+            gpu.gemm(args_g)
+    else:
+        a = gpu.upload(rng.standard_normal(shape_a, dtype=np.float32), args.gemm_dtype)
+        b = gpu.upload(rng.standard_normal(shape_b, dtype=np.float32), args.gemm_dtype)
+        c = gpu.zeros((m, n), "f32" if args.gemm == "TN" or args.gemm_dtype == "f32" else "bf16")
+        fn = {"NN": gpu.matmul, "NT": gpu.matmul_a_bt, "TN": gpu.matmul_at_b}[args.gemm]
     fn(a, b, c)
     gpu.sync()
     st = torch.cuda.ExternalStream(gpu.stream())
@@ -308,8 +358,10 @@ def run_gemm_only(args):
     e1.record(st)
     gpu.sync()
     ms = e0.elapsed_time(e1) / args.reps
-    print(json.dumps({"gemm": args.gemm, "dtype": args.gemm_dtype, "m": m, "n": n, "k": k, "ms": ms,
-                      "tflops": 2.0 * m * n * k / (ms / 1e3) / 1e12}), flush=True)
+    mma_flops = 2.0 * m * n * k * (2 if args.split else 1)
+    print(json.dumps({"gemm": args.gemm, "dtype": args.gemm_dtype, "split": bool(args.split), "m": m, "n": n, "k": k,
+                      "ms": ms, "tflops": 2.0 * m * n * k / (ms / 1e3) / 1e12,
+                      "tensor_tflops": mma_flops / (ms / 1e3) / 1e12}), flush=True)
     gpu.close()
 
 
@@ -461,6 +513,94 @@ def run_op(args):
     gpu.close()
 
 
+INFER_BATCHES = (1, 32, 512, 4096)
+
+
+def glorot_weights(dims, seed):
+    """Dense::new's Glorot-uniform W (limit sqrt(6 / (in + out))), zero b."""
+    rng = np.random.default_rng(seed)
+    params = []
+    for l in range(len(dims) - 1):
+        lim = np.float32(np.sqrt(6.0 / (dims[l] + dims[l + 1])))
+        params.append(rng.uniform(-lim, lim, size=(dims[l], dims[l + 1])).astype(np.float32))
+        params.append(np.zeros((1, dims[l + 1]), np.float32))
+    return params
+
+
+def suite_data(n, d):
+    """examples/suite.rs:27-32: x[i, j] = sin(0.01 i + 0.03 j)."""
+    i = np.arange(n, dtype=np.float32).reshape(n, 1)
+    j = np.arange(d, dtype=np.float32).reshape(1, d)
+    return np.sin(i * np.float32(0.01) + j * np.float32(0.03)).astype(np.float32)
+
+
+def run_infer(args):
+    """Inference (the forward pass alone) as examples/suite.rs:204-240 times
+    it: the MLP 512 -> 1024 -> 1024 -> 10, f32, Glorot weights, suite.rs's
+    sin data, at batch 1 / 32 / 512 / 4096.  Per batch: GpuMlp.forward_only
+    on a device-resident input (the captured forward graph) timed with CUDA
+    events over --steps calls; the same through rt_mlp_forward_host (H2D of
+    x and D2H of the logits inside the timed span); and the CPU reference's
+    Sequential::predict (the oracle port, 1 thread as rtensor's CPU backend)
+    on the same batch.  One JSON line per batch."""
+    import torch
+
+    import oracle
+    import rgpu_b200
+
+    dims = [512, 1024, 1024, 10]
+    params = glorot_weights(dims, 7)
+    gpu = rgpu_b200.Gpu(0)
+    st = torch.cuda.ExternalStream(gpu.stream())
+    cpu_model_ = oracle.Mlp(dims)
+    cpu_model_.set_params(params)
+    for batch in INFER_BATCHES:
+        x = suite_data(batch, dims[0])
+        mlp = rgpu_b200.GpuMlp.from_params(gpu, params, batch, 0.0, optimizer="none")
+        x_dev = gpu.upload(x)
+        x_pin = torch.from_numpy(x).pin_memory()
+        out_pin = torch.zeros((batch, dims[-1]), dtype=torch.float32).pin_memory()
+        for _ in range(max(3, args.warmup)):
+            mlp.forward_only(x_dev)
+            mlp.forward_host_ptr(x_pin.data_ptr(), "f32", out_pin.data_ptr())
+        gpu.sync()
+
+        def span(fn):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            gpu.sync()
+            e0.record(st)
+            for _ in range(args.steps):
+                fn()
+            e1.record(st)
+            gpu.sync()
+            return e0.elapsed_time(e1) / args.steps
+
+        l0 = gpu.launch_count()
+        ms_dev = span(lambda: mlp.forward_only(x_dev))
+        launches = (gpu.launch_count() - l0) // args.steps
+        ms_e2e = span(lambda: mlp.forward_host_ptr(x_pin.data_ptr(), "f32", out_pin.data_ptr()))
+        reps = 20 if batch < 512 else 5
+        cpu_model_.forward(x, threads=1)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            cpu_model_.forward(x, threads=1)
+        t_cpu = (time.perf_counter() - t0) / reps
+        line = {"mode": "infer", "metric": "inference samples/sec (forward_only)", "batch": batch,
+                "value": batch / (ms_dev / 1e3), "unit": "samples/s", "ms_per_forward": ms_dev, "steps": args.steps,
+                "higher_is_better": True, "dtype": "f32", "data": "synthetic (examples/suite.rs sin data)",
+                "config": {"workload": "MLP " + "->".join(map(str, dims)), "batch": batch,
+                           "weights": "Glorot-uniform, zero bias", "reference": "examples/suite.rs:204-240"},
+                "e2e": {"value": batch / (ms_e2e / 1e3), "unit": "samples/s", "ms_per_forward": ms_e2e,
+                        "h2d_bytes_per_step": x.nbytes, "d2h_bytes_per_step": batch * dims[-1] * 4},
+                "gpu_launches": int(launches),
+                "cpu_baseline": {"value": batch / t_cpu, "unit": "samples/s", "cores": 1, "kind": "port",
+                                 "ms_per_forward": t_cpu * 1e3, "cpu_model": cpu_model(),
+                                 "sample": f"Sequential::predict on the same {batch} rows, 1 thread, mean of {reps}"}}
+        print(json.dumps(line), flush=True)
+        mlp.close()
+    gpu.close()
+
+
 def config_dict(cfg_name, cfg, n, global_batch):
     d = cfg["dims"]
     return {"workload": ("wide MLP " if cfg_name == "wide" else "MLP ") + "->".join(map(str, d)),
@@ -479,12 +619,15 @@ def main():
     ap.add_argument("--config", default="wide", choices=sorted(CONFIGS))
     ap.add_argument("--global-batch", type=int, default=0, help="strong scaling: fixed global batch")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-strong", action="store_true", help="skip the fixed-global-batch (65536) leg")
     ap.add_argument("--gemm", choices=["NN", "NT", "TN"], help="profile one bf16 GEMM instead of the step")
     ap.add_argument("--mnk", type=int, nargs=3, default=[8192, 8192, 8192], metavar=("M", "N", "K"))
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--l2-group", type=int, default=0, help="GEMM raster group (tile rows), 0 = library default")
     ap.add_argument("--gemm-dtype", default="bf16", choices=["bf16", "f32"], help="operand dtype of --gemm")
+    ap.add_argument("--split", action="store_true", help="--gemm NN with split (hi + lo) A and C planes")
     ap.add_argument("--sweep", action="store_true", help="dW = X^T dY sweep (BASELINE configs[3])")
+    ap.add_argument("--infer", action="store_true", help="inference at batch 1/32/512/4096 (examples/suite.rs)")
     ap.add_argument("--op", choices=["adam", "xent"], help="time one HBM-bound kernel alone")
     ap.add_argument("--op-shape", type=int, nargs=2, default=[8192, 8192], metavar=("ROWS", "COLS"))
     ap.add_argument("--sweep-dtypes", default="f32,bf16")
@@ -494,6 +637,9 @@ def main():
     args = ap.parse_args()
     if args.sweep:
         run_dw_sweep(args)
+        return
+    if args.infer:
+        run_infer(args)
         return
     if args.op:
         run_op(args)
@@ -534,11 +680,13 @@ def main():
     gpu = rgpu_b200.Gpu(local)
     if args.l2_group:
         gpu.set_grupo_l2(args.l2_group)
-    params, x, labels = make_inputs(cfg, batch, 1234 + rank)
+    # Data parallelism: every rank starts from the same weights (one seed)
+    # and takes its own rows of the global batch (seeded per rank).
+    params = make_weights(cfg, 1234)
+    x, labels = make_data(cfg, batch, 5678 + rank)
     mlp = rgpu_b200.GpuMlp.from_params(gpu, params, batch, cfg["lr"], dtype=cfg["dtype"],
                                        optimizer=cfg["optimizer"], global_batch=global_batch,
                                        activations=args.activations)
-    del params
     comm = None
     if world > 1:
         uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
@@ -611,14 +759,60 @@ def main():
 
     # ---- second timed region of the same steps with a CUDA event between
     # consecutive kernels of the captured step (the per-kernel times behind
-    # the roofline); the events cost a little, so `value` comes from the
-    # region above
+    # the roofline), read back after every step and averaged over the steps;
+    # the events cost a little, so `value` comes from the region above
     mlp.enable_timing(True)
     for _ in range(2):
         step_dev()
     gpu.sync()
-    ms_events = timed(step_dev, args.steps)
-    ops = mlp.op_times()  # the last timed step's per-kernel device times
+    barrier()
+    op_sum = None
+    for _ in range(args.steps):
+        step_dev()
+        gpu.sync()
+        ops_i = mlp.op_times()
+        if op_sum is None:
+            op_sum = [[lab, fl, 0.0] for lab, fl, _ in ops_i]
+        for acc_op, (lab, fl, t) in zip(op_sum, ops_i):
+            acc_op[2] += t
+    barrier()
+    ops = [(lab, fl, t / args.steps) for lab, fl, t in op_sum]  # mean device ms per kernel
+    ms_events = sum(t for _, _, t in ops) * args.steps
+
+    # ---- the same model at a fixed global batch of
+    # 65536 rows split over the ranks (strong scaling), device-resident
+    # inputs, timed like the main region; the 1-GPU run gives the baseline
+    # of the scaling efficiency at the same global batch.
+    grad_sync = mlp.comm_mode()
+    strong = None
+    if args.config == "wide" and not args.global_batch and not args.no_strong:
+        mlp.close()
+        sb = STRONG_GLOBAL_BATCH // world
+        smlp = rgpu_b200.GpuMlp.from_params(gpu, params, sb, cfg["lr"], dtype=cfg["dtype"],
+                                            optimizer=cfg["optimizer"], global_batch=sb * world,
+                                            activations=args.activations)
+        if comm:
+            smlp.set_comm(comm)
+        gen = torch.Generator(device=torch.device("cuda", local))
+        gen.manual_seed(91 + rank)
+        sx = torch.randn((sb, dims[0]), generator=gen, device=torch.device("cuda", local)).to(torch.bfloat16)
+        sl = torch.randint(0, dims[-1], (sb,), generator=gen, device=torch.device("cuda", local), dtype=torch.int32)
+        torch.cuda.synchronize()
+
+        def step_strong():
+            smlp.step_ptr(sx.data_ptr(), "bf16", sl.data_ptr())
+
+        for _ in range(max(3, args.warmup)):
+            step_strong()
+        gpu.sync()
+        ms_s = timed(step_strong, args.steps)
+        strong = {"global_batch": sb * world, "batch_per_gpu": sb, "n_gpus": world, "steps": args.steps,
+                  "ms_per_step": ms_s / args.steps, "value": sb * world / (ms_s / args.steps / 1e3),
+                  "unit": "samples/s", "scaling": "strong",
+                  "note": "BASELINE configs[4]: fixed global batch over the ranks; device-resident N(0,1) bf16 inputs"}
+        smlp.close()
+        mlp = None
+        del sx, sl
 
     ms_step = ms / args.steps
     value = global_batch / (ms_step / 1e3)
@@ -646,17 +840,18 @@ def main():
         scale = 1.0 if cfg["dtype"] == "bf16" else 1.0 / 6.0
         burst = pk["bf16"] * scale
         peak = (pk["bf16_sus"] if sustained else pk["bf16"]) * scale
-        traffic = None
-        if lab == "dw_gemm" and cfg["dtype"] == "bf16":  # plain dW launch, as captured
-            traffic = DW_GEMM_TRAFFIC_BYTES * (fl / cnt) / DW_GEMM_TRAFFIC_FLOPS
-        elif lab == "dw_gemm_adam" and cfg["dtype"] == "bf16" and DW_ADAM_TRAFFIC_BYTES:
-            traffic = DW_ADAM_TRAFFIC_BYTES * (fl / cnt) / DW_ADAM_TRAFFIC_FLOPS
+        traffic, traffic_src = None, None
+        if cfg["dtype"] == "bf16" and lab in TRAFFIC_PER_LAUNCH:
+            tb, traffic_src = TRAFFIC_PER_LAUNCH[lab]
+            traffic = tb * (fl / cnt) / TRAFFIC_FLOPS
+        # split-activation forward GEMMs run two bf16 products per algorithmic one
+        executed = 2.0 if lab.endswith("_split") else 1.0
         roof = {"bound": "tensor", "kernel": lab, "launches_per_step": cnt, "achieved": ach, "peak": peak,
                 "unit": "TFLOP/s", "frac": ach / peak, "peak_burst": burst, "frac_of_burst": ach / burst,
+                "executed_tensor_tflops": ach * executed, "executed_frac_of_burst": ach * executed / burst,
                 "traffic": traffic,
-                "traffic_note": "bytes per launch, ncu capture of the 8192^3 dW GEMM" + (
-                    " with fused Adam (bench.py --config probe_dw)" if lab == "dw_gemm_adam" else "")
-                + " scaled by FLOPs",
+                "traffic_note": (f"DRAM bytes per launch: ncu capture of {traffic_src}, scaled by FLOPs"
+                                 if traffic_src else "no ncu capture for this kernel"),
                 "peak_source": pk["source"] + (" bf16 dense sustained (cuBLAS back to back under the power cap)"
                                                if sustained else
                                                " bf16 dense burst / 2 (tf32 rate) / 3 (3xTF32 products)")}
@@ -677,26 +872,30 @@ def main():
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": cfg["dtype"],
             "data": "synthetic (seeded N(0,1) inputs, uniform labels, Kaiming-uniform weights)",
-            "config": dict(config_dict(args.config, cfg, world, global_batch), grad_sync=mlp.comm_mode(),
+            "config": dict(config_dict(args.config, cfg, world, global_batch), grad_sync=grad_sync,
                            activations=(args.activations if cfg["dtype"] == "bf16" else "f32")),
             "roofline": roof,
             "ms_per_step_with_kernel_events": ms_events / args.steps,
+            "roofline_window": f"per-kernel CUDA events, mean over {args.steps} timed steps",
             "step_tensor_frac": {"achieved_tflops": step_tflops, "peak": pk["bf16"], "frac": step_tflops / pk["bf16"],
                                  "peak_sustained": pk["bf16_sus"],
                                  "frac_of_sustained": step_tflops / pk["bf16_sus"] if pk["bf16_sus"] else None,
                                  "flops_per_step_per_gpu": step_flops,
                                  "gemm_tflops": gemm_f / (gemm_t / 1e3) / 1e12 if gemm_t > 0 else None},
             "cpu_baseline": cpu,
+            "strong_scaling": strong,
             "e2e": {"value": e2e_value, "unit": "samples/s", "h2d_bytes_per_step": in_bytes,
                     "d2h_bytes_per_step": batch * 4},
             "gpu_launches": int(launches),
             "clocks": clk,
-            "kernels_last_step": [{"label": lab, "ms": round(t, 4), "tflops": round(fl / (t / 1e3) / 1e12, 1) if fl and t
-                                   else None} for lab, fl, t in ops],
+            "kernels_mean_over_steps": [{"label": lab, "ms": round(t, 4),
+                                         "tflops": round(fl / (t / 1e3) / 1e12, 1) if fl and t else None}
+                                        for lab, fl, t in ops],
         }
         print(json.dumps(line), flush=True)
 
-    mlp.close()
+    if mlp:
+        mlp.close()
     if comm:
         comm.close()
     gpu.close()

@@ -132,15 +132,14 @@ int rt_split_k_suggest(int64_t m, int64_t n, int64_t k);
 int64_t rt_split_k_workspace(int64_t m, int64_t n, int slices);
 /* No counterpart in the reference.  The same split-K GEMM as
  * rt_matmul_split_k, for callers that cannot allocate device memory when they
- * call (inside a CUDA graph capture, under a host runtime whose allocator
- * owns the device memory, in loops that forbid allocation after start-up):
- * the partial sums live in a fixed 16 MiB array built into the library
- * (rt_split_k_static_capacity() floats per device, held until the process
- * exits).  Calls needing slices*m*n above that capacity fail with
- * RT_ERR_INVALID.  All calls on a device share the array, so calls whose
- * kernels overlap on the GPU race and must be serialised; the first call on
- * a device looks up the array's device address and should happen outside
- * any stream capture. */
+ * call (a host runtime whose own allocator owns the device memory, a loop
+ * that forbids allocation after start-up): the partial sums live in a fixed
+ * 16 MiB array built into the library (rt_split_k_static_capacity() floats
+ * per device, held until the process exits).  Calls needing slices*m*n above
+ * that capacity fail with RT_ERR_INVALID.  All calls on a device share the
+ * array, so calls whose kernels overlap on the GPU race and must be
+ * serialised.  The first call on a context looks up the array's device
+ * address (cudaGetSymbolAddress) and keeps it in the context. */
 int rt_matmul_split_k_noalloc(rt_ctx* ctx, const rt_tensor* a, const rt_tensor* b, rt_tensor* c,
                               int slices, int transposed);
 int64_t rt_split_k_static_capacity(void);
@@ -255,8 +254,16 @@ int rt_mlp_step(rt_mlp* mlp, const void* x_dev, rt_dtype x_dtype, const uint32_t
  * enqueued; the loss buffer is valid after rt_ctx_sync. */
 int rt_mlp_step_host(rt_mlp* mlp, const void* x_host, rt_dtype x_dtype, const uint32_t* labels_host,
                      float* loss_rows_host);
-/* GpuMlp::forward_only (gpu/mod.rs:1514-1521). */
+/* GpuMlp::forward_only (gpu/mod.rs:1514-1521): the input is copied into the
+ * plan and the forward GEMMs run as a CUDA graph captured on first use. */
 int rt_mlp_forward_only(rt_mlp* mlp, const void* x_dev, rt_dtype x_dtype);
+/* GpuMlp::forward_only followed by GpuMlp::logits (gpu/mod.rs:1514-1526) from
+ * page-locked or pageable HOST memory: the host->device copy of x (on a copy
+ * stream, overlapping the previous call's forward), the captured forward and,
+ * when logits_host != NULL, the device->host copy of the [batch, classes] f32
+ * logits are enqueued.  Returns once enqueued; logits are valid after
+ * rt_ctx_sync. */
+int rt_mlp_forward_host(rt_mlp* mlp, const void* x_host, rt_dtype x_dtype, float* logits_host);
 /* GpuMlp::logits (gpu/mod.rs:1524-1526): [batch, classes] f32, blocking. */
 int rt_mlp_logits(rt_mlp* mlp, float* host);
 /* GpuMlp::last_loss (gpu/mod.rs:1529-1531): mean row loss, blocking. */
@@ -316,13 +323,19 @@ int rt_mlp_set_comm(rt_mlp* mlp, rt_comm* comm);
 /* How the attached communicator sums gradients (rt_comm_mode).
  * RT_COMM_SHARDED_P2P: sharded optimiser whose dW GEMMs (some or all layers)
  * scatter their rows to the owning ranks over NVLink peer memory from the
- * GEMM epilogue instead of an NCCL reduce-scatter (RTGPU_P2P_RS=1). */
+ * GEMM epilogue instead of an NCCL reduce-scatter (RTGPU_P2P_RS=1).
+ * RT_COMM_SHARDED_CE: sharded optimiser whose gradient pieces and updated
+ * bf16 weights move between the ranks' mapped buffers by copy-engine copies
+ * over NVLink (no SM moves them), with one-float NCCL barriers; the default
+ * for sharded plans where every rank maps every other rank's buffers
+ * (RTGPU_CE_EXCHANGE=0 keeps NCCL's reduce-scatter and all-gather). */
 typedef enum {
     RT_COMM_NONE = 0,
     RT_COMM_ALLREDUCE = 1,
     RT_COMM_ALLREDUCE_BF16 = 2,
     RT_COMM_SHARDED_OPT = 3,
-    RT_COMM_SHARDED_P2P = 4
+    RT_COMM_SHARDED_P2P = 4,
+    RT_COMM_SHARDED_CE = 5
 } rt_comm_mode;
 int rt_mlp_comm_mode(rt_mlp* mlp, int* mode);
 

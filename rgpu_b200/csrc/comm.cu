@@ -80,6 +80,10 @@ struct rt_comm {
     ncclComm_t nccl = nullptr;
     ncclComm_t nccl2 = nullptr;  // second communicator (comm_open_second), its own queue of collectives
     int rank = 0, world = 1;
+    // device staging for the IPC handles comm_share_buffer all-gathers
+    // (allocated with the communicator, so that call allocates nothing
+    // before its collective)
+    uint8_t* handles = nullptr;
 };
 
 namespace rt {
@@ -163,8 +167,7 @@ int comm_share_buffer(rt_comm* comm, void* local, void** peers) {
     std::memset(&mine, 0, sizeof(mine));
     int rc = RT_OK;
     if (cudaIpcGetMemHandle(&mine, local) != cudaSuccess) rc = fail(RT_ERR_UNSUPPORTED, "cudaIpcGetMemHandle failed");
-    uint8_t* dev = nullptr;
-    RT_CUDA(cudaMalloc(&dev, sizeof(cudaIpcMemHandle_t) * W));
+    uint8_t* dev = comm->handles;
     std::vector<cudaIpcMemHandle_t> all(W);
     if (cudaMemcpyAsync(dev + sizeof(mine) * comm->rank, &mine, sizeof(mine), cudaMemcpyHostToDevice, st) !=
         cudaSuccess && rc == RT_OK)
@@ -174,7 +177,6 @@ int comm_share_buffer(rt_comm* comm, void* local, void** peers) {
     if ((cudaMemcpyAsync(all.data(), dev, sizeof(mine) * W, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
          cudaStreamSynchronize(st) != cudaSuccess) && rc == RT_OK)
         rc = fail(RT_ERR_CUDA, "comm_share_buffer: handle download failed");
-    cudaFree(dev);
     RT_TRY(rc);
     for (int q = 0; q < W; ++q) peers[q] = nullptr;
     peers[comm->rank] = local;
@@ -227,11 +229,13 @@ bool comm_all_true(rt_comm* comm, bool mine, float* scratch, int* status) {
 
 // A barrier in stream order: a one-float ncclAllReduce on `scratch`.  Work
 // enqueued on `st` after it runs once every rank has reached it, so device
-// writes that each rank finished before its barrier (peer-memory stores
-// included) are in place.
-int comm_barrier(rt_comm* comm, float* scratch, cudaStream_t st) {
+// writes that each rank finished before its barrier (peer-memory stores and
+// copies included) are in place.  `second` issues it on the second
+// communicator (its own queue of collectives).
+int comm_barrier(rt_comm* comm, float* scratch, cudaStream_t st, bool second) {
     NcclApi& A = nccl_api();
-    ncclResult_t r = A.AllReduce(scratch, scratch, 1, ncclFloat32, ncclSum, comm->nccl, st);
+    ncclComm_t nc = second && comm->nccl2 ? comm->nccl2 : comm->nccl;
+    ncclResult_t r = A.AllReduce(scratch, scratch, 1, ncclFloat32, ncclSum, nc, st);
     if (r != ncclSuccess) return fail(RT_ERR_NCCL, "ncclAllReduce (barrier) failed: %s", A.GetErrorString(r));
     return RT_OK;
 }
@@ -266,8 +270,13 @@ int rt_comm_init(rt_ctx* ctx, int rank, int world, const unsigned char id[128], 
     c->ctx = ctx;
     c->rank = rank;
     c->world = world;
+    if (cudaMalloc(&c->handles, sizeof(cudaIpcMemHandle_t) * (size_t)world) != cudaSuccess) {
+        delete c;
+        return fail(RT_ERR_OOM, "rt_comm_init: handle staging allocation failed");
+    }
     ncclResult_t r = A.CommInitRank(&c->nccl, world, u, rank);
     if (r != ncclSuccess) {
+        cudaFree(c->handles);
         delete c;
         return fail(RT_ERR_NCCL, "ncclCommInitRank(rank %d of %d) failed: %s", rank, world, A.GetErrorString(r));
     }
@@ -279,6 +288,7 @@ int rt_comm_destroy(rt_comm* c) {
     if (!c) return RT_OK;
     if (c->nccl2) nccl_api().CommDestroy(c->nccl2);
     if (c->nccl) nccl_api().CommDestroy(c->nccl);
+    if (c->handles) cudaFree(c->handles);
     delete c;
     return RT_OK;
 }

@@ -318,6 +318,31 @@ __global__ void sum_partials_kernel(float* __restrict__ out, const float* __rest
     }
 }
 
+// out[i] = sum over r < parts, in order, of (r == own_rank ? own[i] : in[r * q_stride + i]);
+// out may be own (each element reads own[i] before writing out[i]).
+__global__ void sum_partials_own_kernel(float* out, const float* own, const float* __restrict__ in,
+                                        int64_t q_stride, int parts, int own_rank, int64_t n, bool vec) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t nv = vec ? n / 4 : 0;
+    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nv; q += stride) {
+        float4 acc = own_rank == 0 ? reinterpret_cast<const float4*>(own)[q] : reinterpret_cast<const float4*>(in)[q];
+        for (int r = 1; r < parts; ++r) {
+            const float4 x = r == own_rank ? reinterpret_cast<const float4*>(own)[q]
+                                           : reinterpret_cast<const float4*>(in + r * q_stride)[q];
+            acc.x = __fadd_rn(acc.x, x.x);
+            acc.y = __fadd_rn(acc.y, x.y);
+            acc.z = __fadd_rn(acc.z, x.z);
+            acc.w = __fadd_rn(acc.w, x.w);
+        }
+        reinterpret_cast<float4*>(out)[q] = acc;
+    }
+    for (int64_t i = nv * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        float acc = own_rank == 0 ? own[i] : in[i];
+        for (int r = 1; r < parts; ++r) acc = __fadd_rn(acc, r == own_rank ? own[i] : in[r * q_stride + i]);
+        out[i] = acc;
+    }
+}
+
 __global__ void axpy_kernel(float* dst, int64_t ldd, const float* src, int64_t lds, int64_t rows, int64_t cols) {
     int64_t total = rows * cols;
     for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
@@ -494,6 +519,18 @@ int launch_sum_partials(rt_ctx* ctx, float* out, const float* in, int64_t q_stri
     const bool vec = ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(in)) & 15) == 0 &&
                      (q_stride & 3) == 0;
     sum_partials_kernel<<<grid_for(ctx, vec ? n / 4 + 1 : n), 256, 0, st>>>(out, in, q_stride, parts, n, vec);
+    count_launch(ctx);
+    RT_CUDA(cudaGetLastError());
+    return RT_OK;
+}
+
+int launch_sum_partials_own(rt_ctx* ctx, float* out, const float* own, const float* in, int64_t q_stride, int parts,
+                            int own_rank, int64_t n, cudaStream_t st) {
+    if (n == 0) return RT_OK;
+    const bool vec = ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(own) |
+                       reinterpret_cast<uintptr_t>(in)) & 15) == 0 && (q_stride & 3) == 0;
+    sum_partials_own_kernel<<<grid_for(ctx, vec ? n / 4 + 1 : n), 256, 0, st>>>(out, own, in, q_stride, parts,
+                                                                              own_rank, n, vec);
     count_launch(ctx);
     RT_CUDA(cudaGetLastError());
     return RT_OK;

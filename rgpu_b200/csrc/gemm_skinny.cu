@@ -11,10 +11,14 @@
 // (or, for narrow K, over its output), with the tiny operand held in L1 or
 // shared memory.  Same epilogues as the other GEMM kernels (bias, bias+ReLU,
 // ReLU mask, fused optimiser), f32 or bf16 operands and output.
+#include <cooperative_groups.h>
+
 #include "internal.h"
 
 namespace rt {
 namespace {
+
+namespace cg = cooperative_groups;
 
 constexpr int kThreads = 256;
 constexpr int kSkinnyNSmem = 1024 * 20 * 4;  // skinny_n_kernel's staged B chunk
@@ -405,6 +409,138 @@ __global__ void __launch_bounds__(kThreads) skinny_k_kernel(SkinnyParams p) {
     }
 }
 
+// Few rows (layout NN, m <= 16, or m <= 64 for f32 operands, whose tensor-core
+// path would be three tf32 products behind an operand split: the forward
+// pass at small batch):
+// a GEMV-like pass over B.  A cluster of kClusterK CTAs owns 64 columns of C
+// (lane l of every warp holds columns 2 l and 2 l + 1) and splits k: CTA r of
+// the cluster takes the r-th k range, and its 8 warps split that range again.
+// A's rows are staged in shared memory 256 k at a time (hi + lo summed when A
+// is split), B is read once per 16-row pass with coalesced 8-byte (f32) or
+// 4-byte (bf16) loads, 16 rows' loads in flight per thread.  The warps' sums
+// are reduced in shared memory in warp order, then CTA 0 of the cluster adds
+// the CTAs' sums in rank order through distributed shared memory and runs
+// the epilogue: one launch, no workspace, a fixed summation order.
+constexpr int kClusterK = 8;
+constexpr int kSkinnyRowsMax = 64;
+constexpr int kMRows = 16;  // rows per pass
+constexpr int kKChunk = 256;
+
+template <typename TIn>
+__device__ __forceinline__ float2 ld2_f(const TIn* p);
+template <>
+__device__ __forceinline__ float2 ld2_f<float>(const float* p) {
+    return __ldg(reinterpret_cast<const float2*>(p));
+}
+template <>
+__device__ __forceinline__ float2 ld2_f<__nv_bfloat16>(const __nv_bfloat16* p) {
+    const uint32_t u = __ldg(reinterpret_cast<const unsigned int*>(p));
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+}
+
+template <typename TIn>
+__global__ void __cluster_dims__(kClusterK, 1, 1) __launch_bounds__(kThreads)
+    skinny_m_kernel(SkinnyParams p) {
+    // sa (A rows of the k chunk) during the k loop; red (the warps' sums)
+    // after it, in the same shared memory
+    __shared__ __align__(16) float buf[kThreads / 32][kMRows][64];
+    __shared__ __align__(16) float part[kMRows][64];
+    static_assert(sizeof(float) * kMRows * kKChunk <= sizeof(buf), "A chunk fits the reduction buffer");
+    float(*sa)[kKChunk] = reinterpret_cast<float(*)[kKChunk]>(&buf[0][0][0]);
+    float(*red)[kMRows][64] = buf;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    const TIn* A = static_cast<const TIn*>(p.a);
+    const TIn* A2 = static_cast<const TIn*>(p.a2);
+    const TIn* B = static_cast<const TIn*>(p.b);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t n0 = (int64_t)(blockIdx.x / kClusterK) * 64;
+    const int64_t j = n0 + 2 * lane;  // this lane's columns j, j + 1
+    // two columns per load where the row stride and base allow an aligned pair
+    const bool pair = j + 1 < p.n && (p.ldb & 1) == 0 && (reinterpret_cast<uintptr_t>(B) % (2 * sizeof(TIn))) == 0;
+    const int64_t kr = (p.k + kClusterK - 1) / kClusterK;  // this CTA's k range
+    const int64_t k_lo = (int64_t)rank * kr, k_hi = min(p.k, k_lo + kr);
+    for (int64_t m0 = 0; m0 < p.m; m0 += kMRows) {
+        const int rows = (int)min((int64_t)kMRows, p.m - m0);
+        float acc[kMRows][2];
+#pragma unroll
+        for (int i = 0; i < kMRows; ++i) acc[i][0] = acc[i][1] = 0.0f;
+        for (int64_t kc = k_lo; kc < k_hi; kc += kKChunk) {
+            const int kn = (int)min((int64_t)kKChunk, k_hi - kc);
+            __syncthreads();  // the previous chunk's reads of sa are done
+            for (int t = threadIdx.x; t < kMRows * kKChunk; t += kThreads) {
+                const int i = t / kKChunk, q = t % kKChunk;
+                float v = 0.0f;
+                if (i < rows && q < kn) {
+                    const int64_t ai = (m0 + i) * p.lda + kc + q;
+                    v = ld_f(A, ai);
+                    if (A2) v += ld_f(A2, ai);
+                }
+                sa[i][q] = v;
+            }
+            __syncthreads();
+            // warp w takes k rows w, w + 8, ... of the chunk, 16 at a time
+            for (int q0 = warp; q0 < kn; q0 += 16 * (kThreads / 32)) {
+                float2 b[16];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    const int q = q0 + u * (kThreads / 32);
+                    b[u] = make_float2(0.0f, 0.0f);
+                    if (q < kn && j < p.n) {
+                        const TIn* br = B + (kc + q) * p.ldb + j;
+                        if (pair)
+                            b[u] = ld2_f(br);
+                        else
+                            b[u] = make_float2(ld_f(br, 0), j + 1 < p.n ? ld_f(br, 1) : 0.0f);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    const int q = q0 + u * (kThreads / 32);
+                    if (q >= kn) break;
+#pragma unroll
+                    for (int i = 0; i < kMRows; ++i) {
+                        const float a = sa[i][q];
+                        acc[i][0] = fmaf(a, b[u].x, acc[i][0]);
+                        acc[i][1] = fmaf(a, b[u].y, acc[i][1]);
+                    }
+                }
+            }
+        }
+        __syncthreads();  // every warp is done reading sa, which red overwrites
+#pragma unroll
+        for (int i = 0; i < kMRows; ++i) {
+            red[warp][i][2 * lane] = acc[i][0];
+            red[warp][i][2 * lane + 1] = acc[i][1];
+        }
+        __syncthreads();
+        for (int t = threadIdx.x; t < kMRows * 64; t += kThreads) {
+            const int i = t / 64, c = t % 64;
+            float v = 0.0f;
+            for (int w = 0; w < kThreads / 32; ++w) v += red[w][i][c];
+            part[i][c] = v;
+        }
+        cluster.sync();  // every CTA's part is complete
+        if (rank == 0) {
+            for (int t = threadIdx.x; t < kMRows * 64; t += kThreads) {
+                const int i = t / 64, c = t % 64;
+                if (i >= rows || n0 + c >= p.n) continue;
+                float v = 0.0f;
+                for (int r = 0; r < kClusterK; ++r) v += cluster.map_shared_rank(&part[0][0], r)[i * 64 + c];
+                finish_one(p, m0 + i, n0 + c, v);
+            }
+        }
+        cluster.sync();  // CTA 0 has read every part before they are rewritten (or the CTAs exit)
+    }
+}
+
+// The few-row kernel's GEMMs (n and k wider than the skinny limit).
+bool few_rows(const GemmDesc& g) {
+    if (g.layout != RT_NN || g.n <= kSkinnyMax || g.k <= kSkinnyMax || g.opt.kind || g.split_k > 1 || g.p2p.world)
+        return false;
+    return g.m <= kSkinnyMax || (g.in_dtype == RT_F32 && g.m <= kSkinnyRowsMax);
+}
+
 SkinnyParams make_params(const GemmDesc& g) {
     SkinnyParams p{};
     p.a = g.a;
@@ -439,6 +575,14 @@ void launch_narrow_k(const GemmDesc& g, const SkinnyParams& p, dim3 grid, cudaSt
 template <typename TIn>
 int launch_typed(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     SkinnyParams p = make_params(g);
+    if (few_rows(g)) {
+        const int64_t groups = (g.n + 63) / 64;
+        if (groups * kClusterK > (int64_t)INT32_MAX) return fail(RT_ERR_INVALID, "few-row GEMM n too large");
+        skinny_m_kernel<TIn><<<(unsigned)(groups * kClusterK), kThreads, 0, st>>>(p);
+        count_launch(ctx);
+        RT_CUDA(cudaGetLastError());
+        return RT_OK;
+    }
     if (g.n <= kSkinnyMax) {
         if (g.layout == RT_TN) {
             int slices = g.split_k > 1 && g.workspace ? g.split_k : 1;
@@ -493,7 +637,8 @@ int gemm_skinny_init() {
 }
 
 bool gemm_skinny_wanted(const GemmDesc& g) {
-    return g.m >= 1 && g.k >= 1 && (g.n <= kSkinnyMax || g.k <= kSkinnyMax);
+    if (g.m < 1 || g.k < 1) return false;
+    return g.n <= kSkinnyMax || g.k <= kSkinnyMax || few_rows(g);
 }
 
 int launch_gemm_skinny(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {

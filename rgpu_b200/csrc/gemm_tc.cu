@@ -36,8 +36,8 @@ using namespace tc;
 // planes read through 3-D maps, and the k loop runs three product segments
 // over the same k range: lo(A) hi(B), hi(A) lo(B), then hi(A) hi(B) (the
 // small terms first).
-// Split bf16 A (p.split_a): two segments over the same k range, A's
-// low-order plane (tmap_a2) first, then A, both against the same B tiles.
+// Split bf16 A (p.split_a): twice the k blocks, alternating A's low-order
+// plane (tmap_a2) and A at each k block, both against the same B tile.
 // A bf16 output with a low-order plane (p.c_lo) is stored through tmap_c and
 // tmap_c2.
 template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false, bool SPLIT_C = false>
@@ -131,9 +131,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     plane_b = seg == 1;
                 } else {
                     if (p.split_a) {
-                        const int seg = kb / p.kb_seg;  // 0: A's low-order plane, 1: A
-                        k0 = (kb - seg * p.kb_seg) * G::BK;
-                        if (seg == 0) map_a = &tmap_a2;
+                        // k blocks alternate: A's low-order plane at k block kb / 2, then A at
+                        // the same k block, so the second load of each B tile hits L2
+                        k0 = (kb >> 1) * G::BK;
+                        if ((kb & 1) == 0) map_a = &tmap_a2;
                     }
                 }
                 const uint32_t sa = smem_u32(smem_a + stage * G::A_BYTES);
@@ -370,8 +371,7 @@ int launch_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X3Plan
     } else {
         if (g.a_lo) {
             p.split_a = 1;
-            p.kb_seg = p.kblocks;
-            p.kblocks *= 2;
+            p.kblocks *= 2;  // each k block twice: A's low-order plane, then A
         }
     }
     p.c_lo = g.c_lo;

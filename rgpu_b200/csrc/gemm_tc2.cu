@@ -226,9 +226,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
                     int k0 = kb * G::BK;
                     const CUtensorMap* map_a = &tmap_a;
                     if (p.split_a) {
-                        const int seg = kb / p.kb_seg;  // 0: A's low-order plane, 1: A
-                        k0 = (kb - seg * p.kb_seg) * G::BK;
-                        if (seg == 0) map_a = &tmap_a2;
+                        // k blocks alternate: A's low-order plane at k block kb / 2, then A at
+                        // the same k block, so the second load of each B tile hits L2
+                        k0 = (kb >> 1) * G::BK;
+                        if ((kb & 1) == 0) map_a = &tmap_a2;
                     }
                     if (A_MN) {
 #pragma unroll
@@ -458,8 +459,7 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X
     } else {
         if (g.a_lo) {
             p.split_a = 1;
-            p.kb_seg = p.kblocks;
-            p.kblocks *= 2;
+            p.kblocks *= 2;  // each k block twice: A's low-order plane, then A
         }
     }
     p.c_lo = g.c_lo;

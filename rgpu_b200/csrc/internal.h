@@ -64,6 +64,9 @@ struct rt_ctx {
     size_t x3_scratch_bytes = 0;
     std::vector<void*> x3_retired;
     int l2_group = 8;
+    // device address of rt_matmul_split_k_noalloc's built-in scratch array
+    // (looked up on that entry point's first call on this context)
+    float* splitk_static = nullptr;
     uint64_t launches = 0;
     char name[256] = {0};
 };
@@ -123,7 +126,7 @@ struct GemmDesc {
 // Peer memory of a communicator's ranks (comm.cu).
 int comm_share_buffer(rt_comm* comm, void* local, void** peers);
 void comm_unshare_buffer(rt_comm* comm, void** peers);
-int comm_barrier(rt_comm* comm, float* scratch, cudaStream_t st);
+int comm_barrier(rt_comm* comm, float* scratch, cudaStream_t st, bool second = false);
 bool comm_all_true(rt_comm* comm, bool mine, float* scratch, int* status);
 bool gemm_p2p_capable(const rt_ctx* ctx, const GemmDesc& g);
 
@@ -182,6 +185,9 @@ int launch_cast(rt_ctx* ctx, const void* src, rt_dtype sdt, int64_t lds, void* d
 // out[i] = sum over r < parts, in order, of in[r * q_stride + i], i < n.
 int launch_sum_partials(rt_ctx* ctx, float* out, const float* in, int64_t q_stride, int parts, int64_t n,
                         cudaStream_t stream);
+// The same with part `own_rank` read from `own` instead of `in` (out may be own).
+int launch_sum_partials_own(rt_ctx* ctx, float* out, const float* own, const float* in, int64_t q_stride, int parts,
+                            int own_rank, int64_t n, cudaStream_t stream);
 // Sets column `col` of a [rows, ld] matrix to `value` (the ones column that
 // turns the dW GEMM into a dW + db GEMM).
 int launch_fill_column(rt_ctx* ctx, void* p, rt_dtype dt, int64_t rows, int64_t ld, int64_t col, float value,

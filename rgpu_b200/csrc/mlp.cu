@@ -89,6 +89,19 @@ struct PlanLayer {
     bool p2p = false;
     float* recv = nullptr;
     void* peers[kMaxPeers] = {};
+    // Copy-engine exchange (sharded optimiser, the default where every rank
+    // maps every other rank's buffers): each rank copies owner q's flat piece
+    // of a finished dW chunk into ce_recv of rank q, region `this rank`, at
+    // ce_off[chunk]; ce_recv is [world][d * ld / world] f32 (per source rank,
+    // this rank's pieces of every chunk in chunk order; a rank's own region is
+    // unused, it sums its own partial in place).  After its update a
+    // rank's piece of the bf16 weights is pulled by every other rank from its
+    // w16 (w16_peers[q] maps rank q's shadow).  No SM moves these bytes.
+    bool ce = false;
+    float* ce_recv = nullptr;
+    void* ce_peers[kMaxPeers] = {};
+    void* w16_peers[kMaxPeers] = {};
+    std::vector<int64_t> ce_off;
 };
 
 struct Slot {
@@ -99,6 +112,9 @@ struct Slot {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     bool timed = false;
+    // the forward pass alone (inference), captured on first use
+    cudaGraph_t fwd_graph = nullptr;
+    cudaGraphExec_t fwd_exec = nullptr;
     cudaEvent_t ready = nullptr, free_ = nullptr;
 };
 
@@ -140,6 +156,7 @@ struct rt_mlp {
     std::vector<cudaEvent_t> events;
     std::vector<OpRecord> ops;
     int kernels_per_step = 0;
+    int kernels_per_forward = 0;
 
     rt_comm* comm = nullptr;
     int comm_sm_reserve = 0;  // SMs the backward GEMMs leave to NCCL while gradients are reduced
@@ -163,6 +180,13 @@ struct rt_mlp {
     float* scratch = nullptr;  // one word for barriers and agreement collectives
     // per-layer optimiser on a side stream, overlapping the remaining backward GEMMs
     cudaStream_t opt_stream = nullptr;
+    // Copy-engine exchange: one stream per peer for the gradient scatter and
+    // one per peer for the weight pulls, so that the copies to (or from)
+    // different ranks run on different copy engines at once; fork/join
+    // events tie them to the comm and all-gather streams.
+    cudaStream_t ce_scatter[kMaxPeers] = {}, ce_pull[kMaxPeers] = {};
+    cudaEvent_t ce_fork = nullptr, ce_fork2 = nullptr;
+    cudaEvent_t ce_join[kMaxPeers] = {}, ce_join2[kMaxPeers] = {};
 };
 
 namespace {
@@ -188,18 +212,28 @@ void drop_graphs(rt_mlp* m) {
     for (auto& s : m->slot) {
         if (s.exec) cudaGraphExecDestroy(s.exec);
         if (s.graph) cudaGraphDestroy(s.graph);
+        if (s.fwd_exec) cudaGraphExecDestroy(s.fwd_exec);
+        if (s.fwd_graph) cudaGraphDestroy(s.fwd_graph);
         s.exec = nullptr;
         s.graph = nullptr;
+        s.fwd_exec = nullptr;
+        s.fwd_graph = nullptr;
     }
 }
 
-// Unmaps the peers' receive buffers of every peer-scatter layer.
+// Unmaps the peers' buffers of every peer-scatter and copy-engine layer.
 void teardown_p2p(rt_mlp* m) {
-    for (PlanLayer& P : m->L)
+    for (PlanLayer& P : m->L) {
         if (P.p2p) {
             comm_unshare_buffer(m->comm, P.peers);
             P.p2p = false;
         }
+        if (P.ce) {
+            comm_unshare_buffer(m->comm, P.ce_peers);
+            comm_unshare_buffer(m->comm, P.w16_peers);
+            P.ce = false;
+        }
+    }
 }
 
 void free_all(rt_mlp* m) {
@@ -218,6 +252,14 @@ void free_all(rt_mlp* m) {
         for (auto e : P.ev_ag) cudaEventDestroy(e);
         if (P.ev_dx) cudaEventDestroy(P.ev_dx);
     }
+    for (int q = 0; q < kMaxPeers; ++q) {
+        if (m->ce_scatter[q]) cudaStreamDestroy(m->ce_scatter[q]);
+        if (m->ce_pull[q]) cudaStreamDestroy(m->ce_pull[q]);
+        if (m->ce_join[q]) cudaEventDestroy(m->ce_join[q]);
+        if (m->ce_join2[q]) cudaEventDestroy(m->ce_join2[q]);
+    }
+    if (m->ce_fork) cudaEventDestroy(m->ce_fork);
+    if (m->ce_fork2) cudaEventDestroy(m->ce_fork2);
     if (m->comm_stream) cudaStreamDestroy(m->comm_stream);
     if (m->ag_stream) cudaStreamDestroy(m->ag_stream);
     if (m->opt_stream) cudaStreamDestroy(m->opt_stream);
@@ -316,7 +358,9 @@ struct Enqueuer {
             g.x3_ws = m->x3_ws;
             g.x3_ws_bytes = m->x3_ws_bytes;
             RT_TRY(run_gemm(m->ctx, g, st, 0));
-            RT_TRY(mark(last ? "fwd_gemm_bias" : "fwd_gemm_bias_relu", 2.0 * m->n * P.d * P.u));
+            // FLOPs are the algorithmic 2 n d u; a split-A GEMM runs twice that on the tensor cores
+            const char* label = last ? "fwd_gemm_bias" : g.a_lo ? "fwd_gemm_bias_relu_split" : "fwd_gemm_bias_relu";
+            RT_TRY(mark(label, 2.0 * m->n * P.d * P.u));
         }
         return RT_OK;
     }
@@ -388,11 +432,38 @@ struct Enqueuer {
         return g;
     }
 
-    // Sums gradient rows [r0, r1) over the ranks on the comm stream (in bf16 when
-    // the plan reduces in bf16: cast, allreduce, cast back into g).
-    int allreduce_rows(PlanLayer& P, int64_t r0, int64_t r1) {
+    // Sums gradient rows [r0, r1) (chunk c) over the ranks on the comm stream
+    // (in bf16 when the plan reduces in bf16: cast, allreduce, cast back into g).
+    int allreduce_rows(PlanLayer& P, int c, int64_t r0, int64_t r1) {
         cudaStream_t cs = m->comm_stream;
         const int64_t count = (r1 - r0) * P.ld;
+        if (P.ce) {
+            // copy-engine reduce-scatter: this rank's partial of every owner's
+            // piece goes to that owner's receive region for this rank; once
+            // every rank has passed the barrier, the owner sums the world
+            // partials, source rank by source rank, into its piece of g
+            const int64_t e = shard_end(P, r1);
+            if (e > r0) {
+                const int64_t piece = (e - r0) * P.ld / m->world, region = P.d * P.ld / m->world;
+                RT_CUDA(cudaEventRecord(m->ce_fork, cs));
+                for (int q = 0; q < m->world; ++q) {
+                    if (q == m->rank) continue;  // the owner reads its own partial in place
+                    cudaStream_t sq = m->ce_scatter[q];
+                    RT_CUDA(cudaStreamWaitEvent(sq, m->ce_fork, 0));
+                    float* dst = static_cast<float*>(P.ce_peers[q]) + (int64_t)m->rank * region + P.ce_off[c];
+                    RT_CUDA(cudaMemcpyAsync(dst, P.g + r0 * P.ld + (int64_t)q * piece, (size_t)piece * 4,
+                                            cudaMemcpyDeviceToDevice, sq));
+                    RT_CUDA(cudaEventRecord(m->ce_join[q], sq));
+                    RT_CUDA(cudaStreamWaitEvent(cs, m->ce_join[q], 0));
+                }
+                RT_TRY(comm_barrier(m->comm, m->scratch, cs));
+                float* own = P.g + r0 * P.ld + (int64_t)m->rank * piece;
+                RT_TRY(launch_sum_partials_own(m->ctx, own, own, P.ce_recv + P.ce_off[c], region, m->world, m->rank,
+                                               piece, cs));
+            }
+            if (r1 > P.d) RT_TRY(comm_allreduce(m->comm, P.db, P.ld, cs));
+            return RT_OK;
+        }
         if (P.p2p) {
             // Every rank's GEMM has stored its partials of this chunk into the
             // owners' receive buffers once all ranks pass the barrier; the
@@ -432,6 +503,31 @@ struct Enqueuer {
     // chunk's bf16 weights are all-gathered on the comm stream.
     int gather_weights(PlanLayer& P, int c, int64_t r0, int64_t r1) {
         if (!m->sharded) return RT_OK;
+        if (P.ce) {
+            // once every rank has updated its piece of chunk c (the barrier on
+            // the second communicator), pull the other ranks' pieces of the
+            // bf16 weights into this rank's shadow
+            cudaStream_t as = m->ag_stream;
+            RT_CUDA(cudaStreamWaitEvent(as, P.ev_opt[c], 0));
+            const int64_t e = shard_end(P, r1);
+            if (e > r0) {
+                RT_TRY(comm_barrier(m->comm, m->scratch + 1, as, true));
+                const int64_t piece = (e - r0) * P.ld / m->world;
+                RT_CUDA(cudaEventRecord(m->ce_fork2, as));
+                for (int q = 0; q < m->world; ++q) {
+                    if (q == m->rank) continue;
+                    cudaStream_t sq = m->ce_pull[q];
+                    RT_CUDA(cudaStreamWaitEvent(sq, m->ce_fork2, 0));
+                    const int64_t o = r0 * P.ld + (int64_t)q * piece;
+                    RT_CUDA(cudaMemcpyAsync(P.w16 + o, static_cast<const __nv_bfloat16*>(P.w16_peers[q]) + o,
+                                            (size_t)piece * 2, cudaMemcpyDeviceToDevice, sq));
+                    RT_CUDA(cudaEventRecord(m->ce_join2[q], sq));
+                    RT_CUDA(cudaStreamWaitEvent(as, m->ce_join2[q], 0));
+                }
+            }
+            RT_CUDA(cudaEventRecord(P.ev_ag[c], as));
+            return RT_OK;
+        }
         if (!m->ag_stream) RT_CUDA(cudaStreamWaitEvent(m->comm_stream, P.ev_opt[c], 0));
         cudaStream_t as = m->ag_stream ? m->ag_stream : m->comm_stream;
         if (m->ag_stream) RT_CUDA(cudaStreamWaitEvent(as, P.ev_opt[c], 0));
@@ -525,7 +621,7 @@ struct Enqueuer {
                 RT_CUDA(cudaEventRecord(P.ev_ready[c], st));
                 if (m->comm) {
                     RT_CUDA(cudaStreamWaitEvent(m->comm_stream, P.ev_ready[c], 0));
-                    RT_TRY(allreduce_rows(P, r0, r1));
+                    RT_TRY(allreduce_rows(P, c, r0, r1));
                     RT_CUDA(cudaEventRecord(P.ev_comm[c], m->comm_stream));
                 }
                 if (update && l == 0) {
@@ -609,6 +705,56 @@ int setup_p2p(rt_mlp* m) {
     return RT_OK;
 }
 
+// Copy-engine exchange for the sharded optimiser (the default; RTGPU_CE_EXCHANGE=0
+// keeps NCCL's reduce-scatter and all-gather): every layer whose chunks split
+// into equal flat pieces per rank gets a receive buffer, and that buffer and
+// the layer's bf16 shadow are mapped into every rank's process.  Collective:
+// every rank takes the same decisions in the same order, and a layer that
+// some rank could not map stays on NCCL everywhere.
+int setup_ce(rt_mlp* m) {
+    const char* e = getenv("RTGPU_CE_EXCHANGE");
+    if (!m->sharded || !m->ag_stream || (e && e[0] == '0') || m->world > kMaxPeers) return RT_OK;
+    for (PlanLayer& P : m->L) {
+        if (P.p2p || !P.w16) continue;
+        bool ok = (P.d * P.ld) % m->world == 0;
+        P.ce_off.assign(P.chunks, 0);
+        int64_t off = 0;
+        for (int c = 0; ok && c < P.chunks; ++c) {
+            const int64_t r0 = chunk_row_of(P.d + 1, P.chunks, c), end = shard_end(P, chunk_row_of(P.d + 1, P.chunks, c + 1));
+            if (end <= r0) continue;
+            ok = ((end - r0) * P.ld) % m->world == 0;
+            P.ce_off[c] = off;
+            off += (end - r0) * P.ld / m->world;
+        }
+        if (!ok) continue;
+        if (!P.ce_recv) RT_TRY(dalloc_t(m, &P.ce_recv, (size_t)P.d * P.ld));
+        const int a = comm_share_buffer(m->comm, P.ce_recv, P.ce_peers);
+        const int b = comm_share_buffer(m->comm, P.w16, P.w16_peers);
+        int st = RT_OK;
+        const bool everywhere = comm_all_true(m->comm, a == RT_OK && b == RT_OK, m->scratch, &st);
+        RT_TRY(st);
+        if (!everywhere) {
+            if (a == RT_OK) comm_unshare_buffer(m->comm, P.ce_peers);
+            if (b == RT_OK) comm_unshare_buffer(m->comm, P.w16_peers);
+            continue;
+        }
+        P.ce = true;
+    }
+    bool any = false;
+    for (const PlanLayer& P : m->L) any = any || P.ce;
+    if (any && !m->ce_fork) {
+        RT_CUDA(cudaEventCreateWithFlags(&m->ce_fork, cudaEventDisableTiming));
+        RT_CUDA(cudaEventCreateWithFlags(&m->ce_fork2, cudaEventDisableTiming));
+        for (int q = 0; q < m->world; ++q) {
+            RT_CUDA(cudaStreamCreateWithFlags(&m->ce_scatter[q], cudaStreamNonBlocking));
+            RT_CUDA(cudaStreamCreateWithFlags(&m->ce_pull[q], cudaStreamNonBlocking));
+            RT_CUDA(cudaEventCreateWithFlags(&m->ce_join[q], cudaEventDisableTiming));
+            RT_CUDA(cudaEventCreateWithFlags(&m->ce_join2[q], cudaEventDisableTiming));
+        }
+    }
+    return RT_OK;
+}
+
 // Chunks of each layer's dW GEMM: the first layer always (its update would
 // otherwise trail the step), and under data parallelism every layer with at
 // least 128 MB of gradients (its sum starts a chunk after the GEMM does;
@@ -687,6 +833,33 @@ int launch_slot(rt_mlp* m, int s) {
     RT_CUDA(cudaGraphLaunch(S.exec, m->ctx->stream));
     RT_CUDA(cudaEventRecord(S.free_, m->ctx->stream));
     m->ctx->launches += (uint64_t)m->kernels_per_step;
+    m->last_slot = s;
+    return RT_OK;
+}
+
+// The forward pass of slot s as a CUDA graph (captured on first use).
+int launch_forward(rt_mlp* m, int s) {
+    Slot& S = m->slot[s];
+    cudaStream_t st = m->ctx->stream;
+    if (!S.fwd_exec) {
+        uint64_t before = m->ctx->launches;
+        RT_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        Enqueuer q{m, st, s, true};
+        int rc = q.forward();
+        cudaGraph_t graph = nullptr;
+        cudaError_t e = cudaStreamEndCapture(st, &graph);
+        if (rc != RT_OK) {
+            if (graph) cudaGraphDestroy(graph);
+            return rc;
+        }
+        if (e != cudaSuccess) return fail(RT_ERR_CUDA, "forward capture failed: %s", cudaGetErrorString(e));
+        S.fwd_graph = graph;
+        RT_CUDA(cudaGraphInstantiate(&S.fwd_exec, graph, 0));
+        m->kernels_per_forward = (int)(m->ctx->launches - before);
+    }
+    RT_CUDA(cudaGraphLaunch(S.fwd_exec, st));
+    RT_CUDA(cudaEventRecord(S.free_, st));
+    m->ctx->launches += (uint64_t)m->kernels_per_forward;
     m->last_slot = s;
     return RT_OK;
 }
@@ -912,9 +1085,11 @@ int rt_mlp_step_host(rt_mlp* m, const void* x_host, rt_dtype x_dtype, const uint
 
 int rt_mlp_forward_only(rt_mlp* m, const void* x_dev, rt_dtype x_dtype) {
     RT_CHECK(m && x_dev, "rt_mlp_forward_only: bad arguments");
+    RT_CHECK(x_dtype == RT_F32 || x_dtype == RT_BF16, "x dtype must be RT_F32 or RT_BF16");
     const int64_t d0 = m->dims[0];
     cudaStream_t st = m->ctx->stream;
     int s = m->next_slot;
+    m->next_slot ^= 1;
     Slot& S = m->slot[s];
     if (x_dtype == m->adt) {
         size_t es = dtype_size(x_dtype);
@@ -922,8 +1097,44 @@ int rt_mlp_forward_only(rt_mlp* m, const void* x_dev, rt_dtype x_dtype) {
     } else {
         RT_TRY(launch_cast(m->ctx, x_dev, x_dtype, d0, S.x, m->adt, m->ldx, m->n, d0, st));
     }
-    Enqueuer q{m, st, s, true};
-    return q.forward();
+    return launch_forward(m, s);
+}
+
+int rt_mlp_forward_host(rt_mlp* m, const void* x_host, rt_dtype x_dtype, float* logits_host) {
+    RT_CHECK(m && x_host, "rt_mlp_forward_host: bad arguments");
+    RT_CHECK(x_dtype == RT_F32 || x_dtype == RT_BF16, "x dtype must be RT_F32 or RT_BF16");
+    int s = m->next_slot;
+    m->next_slot ^= 1;
+    Slot& S = m->slot[s];
+    const int64_t d0 = m->dims[0];
+    // the copy stream refills slot s once the work that last read it is done
+    RT_CUDA(cudaStreamWaitEvent(m->copy_stream, S.free_, 0));
+    if (x_dtype == m->adt) {
+        size_t es = dtype_size(x_dtype);
+        RT_CUDA(cudaMemcpy2DAsync(S.x, m->ldx * es, x_host, d0 * es, d0 * es, m->n, cudaMemcpyHostToDevice,
+                                  m->copy_stream));
+    } else {
+        size_t bytes = (size_t)m->n * d0 * dtype_size(x_dtype);
+        if (S.stage_bytes < bytes) {
+            RT_CUDA(cudaStreamSynchronize(m->copy_stream));
+            if (S.stage) cudaFree(S.stage);
+            S.stage = nullptr;
+            S.stage_bytes = 0;
+            RT_CUDA(cudaMalloc(&S.stage, bytes));
+            S.stage_bytes = bytes;
+        }
+        RT_CUDA(cudaMemcpyAsync(S.stage, x_host, bytes, cudaMemcpyHostToDevice, m->copy_stream));
+        RT_TRY(launch_cast(m->ctx, S.stage, x_dtype, d0, S.x, m->adt, m->ldx, m->n, d0, m->copy_stream));
+    }
+    RT_CUDA(cudaEventRecord(S.ready, m->copy_stream));
+    RT_CUDA(cudaStreamWaitEvent(m->ctx->stream, S.ready, 0));
+    RT_TRY(launch_forward(m, s));
+    if (logits_host) {
+        const PlanLayer& P = m->L.back();
+        RT_CUDA(cudaMemcpy2DAsync(logits_host, P.u * 4, P.act, P.ld * 4, P.u * 4, m->n, cudaMemcpyDeviceToHost,
+                                  m->ctx->stream));
+    }
+    return RT_OK;
 }
 
 int rt_mlp_logits(rt_mlp* m, float* host) {
@@ -1139,10 +1350,11 @@ int rt_mlp_op_time(rt_mlp* m, int i, const char** label, double* flops, float* m
 
 int rt_mlp_comm_mode(rt_mlp* m, int* mode) {
     RT_CHECK(m && mode, "bad arguments");
-    bool p2p = false;
-    for (const PlanLayer& P : m->L) p2p = p2p || P.p2p;
+    bool p2p = false, ce = false;
+    for (const PlanLayer& P : m->L) p2p = p2p || P.p2p, ce = ce || P.ce;
     *mode = !m->comm ? RT_COMM_NONE
             : p2p ? RT_COMM_SHARDED_P2P
+            : ce ? RT_COMM_SHARDED_CE
             : m->sharded ? RT_COMM_SHARDED_OPT
             : m->comm_bf16 ? RT_COMM_ALLREDUCE_BF16
                            : RT_COMM_ALLREDUCE;
@@ -1208,6 +1420,12 @@ int rt_mlp_set_comm(rt_mlp* m, rt_comm* comm) {
     }
     if (sharded && !m->scratch) RT_TRY(dalloc_t(m, &m->scratch, 4));
     RT_TRY(setup_p2p(m));
+    RT_TRY(setup_ce(m));
+    // With every layer on the copy-engine exchange, NCCL only runs barriers
+    // and the bias rows' allreduces: the backward GEMMs keep every SM.
+    bool all_ce = m->sharded;
+    for (const PlanLayer& P : m->L) all_ce = all_ce && P.ce;
+    if (all_ce && !getenv("RTGPU_COMM_SM_RESERVE")) m->comm_sm_reserve = 0;
     m->ops.clear();
     drop_graphs(m);
     return RT_OK;

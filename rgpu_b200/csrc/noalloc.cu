@@ -2,12 +2,13 @@
 // compiled into this library, so that a call allocates no device memory.
 //
 // Who needs this: callers that must not allocate device memory when they
-// call in.  Three common cases: code running while a CUDA graph is being
-// captured (cudaMalloc is not a stream operation and is illegal inside a
-// capture region); host runtimes whose own caching allocator owns the device
-// memory and must not be bypassed behind its back; and latency-bound loops
-// that forbid allocation after start-up.  rt_matmul_split_k needs the caller
-// to provide the partials buffer; this variant does not.
+// call in.  Two common cases: host runtimes whose own caching allocator owns
+// the device memory and must not be bypassed behind its back (a cudaMalloc
+// outside it can fail once that allocator has reserved the device, and it
+// can synchronise the device, stalling the caller's other streams); and
+// latency-bound loops that forbid allocation after start-up.
+// rt_matmul_split_k needs the caller to provide the partials buffer; this
+// variant does not.
 //
 // Limits and sharing rules:
 //   - the scratch holds kScratchFloats f32 values (16 MiB) per device, held
@@ -16,14 +17,12 @@
 //   - every call on a device uses the same array and leaves its partial sums
 //     in it.  Nothing needs clearing first: each call writes every partial it
 //     later reads.  Two calls whose kernels overlap on the GPU (different
-//     streams, or a graph replayed concurrently with a direct call) race on
-//     the array: serialise them;
+//     streams or contexts) race on the array: serialise them;
 //   - the array's host-side name is not a device address; its device address
-//     is looked up with cudaGetSymbolAddress once per device, the first time
-//     this entry point runs on that device (with the device current).  Make
-//     that first call outside any stream capture.
-#include <mutex>
-
+//     is looked up with cudaGetSymbolAddress, with the context's device
+//     current, the first time this entry point runs on a context, and kept in
+//     the context (a context created after a cudaDeviceReset looks it up
+//     again).
 #include "internal.h"
 
 namespace rt {
@@ -38,23 +37,18 @@ constexpr size_t kScratchFloats = size_t(4) << 20;  // 16 MiB of f32 partials
 
 static __device__ __align__(256) float g_splitk_scratch[kScratchFloats];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_mu;
-float* g_scratch_ptr[kMaxDevices] = {nullptr};
-
-// Device address of the scratch array for the current device (looked up once).
-int scratch_for_device(int device, float** out) {
-    if (device < 0 || device >= kMaxDevices) return fail(RT_ERR_INVALID, "device index %d out of range", device);
-    std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_scratch_ptr[device]) {
+// Device address of the scratch array for ctx's device (looked up once per
+// context, with the device current).
+int scratch_for_context(rt_ctx* ctx, float** out) {
+    if (!ctx->splitk_static) {
         void* p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_splitk_scratch);
         if (e != cudaSuccess || !p)
-            return fail(RT_ERR_CUDA, "cudaGetSymbolAddress(split-K scratch) failed on device %d: %s", device,
+            return fail(RT_ERR_CUDA, "cudaGetSymbolAddress(split-K scratch) failed on device %d: %s", ctx->device,
                         cudaGetErrorString(e));
-        g_scratch_ptr[device] = static_cast<float*>(p);
+        ctx->splitk_static = static_cast<float*>(p);
     }
-    *out = g_scratch_ptr[device];
+    *out = ctx->splitk_static;
     return RT_OK;
 }
 
@@ -82,7 +76,7 @@ int rt_matmul_split_k_noalloc(rt_ctx* ctx, const rt_tensor* a, const rt_tensor* 
                     slices, (long long)m, (long long)n, need, kScratchFloats);
     RT_CUDA(cudaSetDevice(ctx->device));
     float* scratch = nullptr;
-    RT_TRY(scratch_for_device(ctx->device, &scratch));
+    RT_TRY(scratch_for_context(ctx, &scratch));
     GemmDesc g{};
     g.layout = transposed ? RT_TN : RT_NN;
     g.in_dtype = a->dtype;

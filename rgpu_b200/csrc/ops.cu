@@ -91,7 +91,7 @@ static int x3_context_scratch(rt_ctx* ctx, cudaStream_t stream, size_t need, flo
 // (83 against 100 us) and from k = 16 at 4096 x 4096 (36 against 51 us),
 // behind below that (k = 1: 167 against 69 us).
 bool narrow_k_on_tensor_cores(const rt_ctx* ctx, const GemmDesc& g) {
-    if (g.n <= kSkinnyMax) return false;
+    if (g.n <= kSkinnyMax || g.k > kSkinnyMax) return false;
     if (ctx->skinny_k_max >= 0 && g.k <= ctx->skinny_k_max) return false;
     if (gemm_tc_supported(ctx, g)) return true;
     if (g.no_alloc || !gemm_x3_supported(ctx, g)) return false;

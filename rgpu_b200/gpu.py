@@ -113,6 +113,7 @@ _SIGS = [
     ("rt_mlp_step", C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
     ("rt_mlp_step_host", C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     ("rt_mlp_forward_only", C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
+    ("rt_mlp_forward_host", C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
     ("rt_mlp_logits", C.c_int, [C.c_void_p, C.c_void_p]),
     ("rt_mlp_last_loss", C.c_int, [C.c_void_p, C.POINTER(C.c_float)]),
     ("rt_mlp_global_loss", C.c_int, [C.c_void_p, C.POINTER(C.c_float)]),
@@ -512,6 +513,23 @@ class GpuMlp:
         dt = RT_BF16 if _is_bf16(x) else RT_F32
         _check(lib().rt_mlp_forward_only(self.handle, x.ptr, dt))
 
+    def forward_only_ptr(self, x_ptr: int, x_dtype):
+        _check(lib().rt_mlp_forward_only(self.handle, x_ptr, _dt(x_dtype)))
+
+    def forward_host(self, x: np.ndarray, logits_out: np.ndarray | None = None) -> np.ndarray | None:
+        """forward_only + logits from a host array (f32); the logits land in
+        `logits_out` ([batch, classes] f32) after the call, which syncs."""
+        xa = np.ascontiguousarray(x, np.float32)
+        assert xa.shape == (self.lote, self.dims[0])
+        out = logits_out if logits_out is not None else np.empty((self.lote, self.dims[-1]), np.float32)
+        _check(lib().rt_mlp_forward_host(self.handle, xa.ctypes.data, RT_F32, out.ctypes.data))
+        self.gpu.sync()
+        return out
+
+    def forward_host_ptr(self, x_ptr: int, x_dtype, logits_ptr: int | None):
+        """Asynchronous forward_host on raw (pinned) host pointers."""
+        _check(lib().rt_mlp_forward_host(self.handle, x_ptr, _dt(x_dtype), logits_ptr))
+
     def logits(self) -> np.ndarray:
         out = np.empty((self.lote, self.dims[-1]), np.float32)
         _check(lib().rt_mlp_logits(self.handle, out.ctypes.data))
@@ -605,12 +623,13 @@ class GpuMlp:
 
     def comm_mode(self) -> str:
         """How gradients are summed: "none", "allreduce", "allreduce_bf16",
-        "sharded_opt" (reduce-scatter, sliced update, weight all-gather) or
+        "sharded_opt" (NCCL reduce-scatter, sliced update, weight all-gather),
         "sharded_p2p" (the same, the reduce-scatter done by the dW GEMMs over
-        peer memory)."""
+        peer memory) or "sharded_ce" (gradient pieces and updated weights
+        moved by copy-engine copies between mapped buffers)."""
         v = C.c_int()
         _check(lib().rt_mlp_comm_mode(self.handle, C.byref(v)))
-        return ("none", "allreduce", "allreduce_bf16", "sharded_opt", "sharded_p2p")[v.value]
+        return ("none", "allreduce", "allreduce_bf16", "sharded_opt", "sharded_p2p", "sharded_ce")[v.value]
 
 
 def _is_bf16(t: GpuTensor) -> bool:

@@ -4,9 +4,12 @@ with torch.distributed.run, one process per GPU).
 Every rank holds the full model, takes rows [r*n/p, (r+1)*n/p) of the global
 batch, scales its softmax-CE adjoint by 1/n_global, and the plan sums dW/db
 over ranks with NCCL inside the captured step.  Rank 0 also runs the whole
-global batch on its GPU without a communicator; the summed DP gradients must
-equal that single-GPU result (and the replicas must stay identical under
-Adam).  Results go to the JSON file named by argv[1].
+global batch on its GPU without a communicator and on the CPU oracle (the
+reference's CPU step); the summed DP gradients must equal the single-GPU
+result and the oracle's within the north-star bars (and the replicas must
+stay identical under Adam).  x and W are bf16 values, so the f32 and bf16
+plans and the oracle all start from identical inputs and weights.  Results
+go to the JSON file named by argv[1].
 """
 import datetime
 import json
@@ -18,7 +21,9 @@ import torch
 import torch.distributed as dist
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+import oracle  # noqa: E402
 import rgpu_b200  # noqa: E402
+from tests.helpers import bf16_round  # noqa: E402
 
 
 def main():
@@ -43,11 +48,17 @@ def main():
     params = []
     for l in range(len(dims) - 1):
         lim = np.sqrt(6.0 / dims[l])
-        params += [rng.uniform(-lim, lim, (dims[l], dims[l + 1])).astype(np.float32),
+        params += [bf16_round(rng.uniform(-lim, lim, (dims[l], dims[l + 1])).astype(np.float32)),
                    rng.uniform(-0.1, 0.1, (1, dims[l + 1])).astype(np.float32)]
     n_global = 512
-    x = rng.standard_normal((n_global, dims[0])).astype(np.float32)
+    x = bf16_round(rng.standard_normal((n_global, dims[0])).astype(np.float32))
     labels = rng.integers(0, dims[-1], n_global).astype(np.uint32)
+    g_oracle = None
+    if rank == 0:
+        cpu = oracle.Mlp(dims)
+        cpu.set_params(params)
+        loss_oracle = cpu.train_step(x, labels, threads=os.cpu_count() or 4, input_grad=False)
+        g_oracle = cpu.grads()
     per = n_global // world
     xs, ls = x[rank * per:(rank + 1) * per], labels[rank * per:(rank + 1) * per]
     result = {}
@@ -74,7 +85,9 @@ def main():
             ref.close()
             result[dtype_name] = [float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
                                   for a, b in zip(g_dp, g_ref)]
-            result[dtype_name + "_loss"] = [loss_dp, loss_ref]
+            result[dtype_name + "_oracle"] = [float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+                                              for a, b in zip(g_dp, g_oracle)]
+            result[dtype_name + "_loss"] = [loss_dp, loss_ref, loss_oracle]
     # Adam with chunked dW GEMMs and bf16 gradient sums: replicas stay bit-identical.
     os.environ["RTGPU_FIRST_LAYER_CHUNKS"] = "4"
     os.environ["RTGPU_DW_CHUNKS"] = "2"
@@ -91,14 +104,17 @@ def main():
     dist.all_gather(gathered, wt)
     if rank == 0:
         result["replicas_identical"] = all(torch.equal(gathered[0], g) for g in gathered[1:])
-    # Sharded optimiser (bf16 + Adam, f32 gradient sums): five steps give the
+    # Sharded optimiser (bf16 + Adam, f32 gradient sums) with each exchange:
+    # NCCL reduce-scatter + all-gather, the dW GEMMs' peer scatter, and the
+    # copy-engine copies between mapped buffers.  Five steps give the
     # replicated update's weights, gradients and checkpoint, and replicas that
     # agree bit for bit.
     os.environ["RTGPU_GRAD_COMM"] = "f32"
     runs = {}
-    for sharded in ("0", "1", "p2p"):
+    for sharded in ("0", "1", "p2p", "ce"):
         os.environ["RTGPU_SHARDED_OPT"] = "0" if sharded == "0" else "1"
         os.environ["RTGPU_P2P_RS"] = "1" if sharded == "p2p" else "0"
+        os.environ["RTGPU_CE_EXCHANGE"] = "1" if sharded == "ce" else "0"
         mlp = rgpu_b200.GpuMlp.from_params(gpu, params, per, 1e-3, dtype="bf16", optimizer="adam",
                                            global_batch=n_global)
         mlp.set_comm(comm)
@@ -111,10 +127,11 @@ def main():
         mlp.close()
     os.environ.pop("RTGPU_SHARDED_OPT")
     os.environ.pop("RTGPU_P2P_RS")
+    os.environ.pop("RTGPU_CE_EXCHANGE")
     mode0, w0, g0, s0 = runs["0"]
     rel = lambda a, b: float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))  # noqa: E731
     hdr = 24 + 8 * len(dims)
-    for key, name in (("1", "sharded"), ("p2p", "sharded_p2p")):
+    for key, name in (("1", "sharded"), ("p2p", "sharded_p2p"), ("ce", "sharded_ce")):
         mode1, w1, g1, s1 = runs[key]
         wt = torch.from_numpy(w1).cuda()
         gathered = [torch.zeros_like(wt) for _ in range(world)]

@@ -14,6 +14,15 @@ import torch.multiprocessing as mp
 import oracle
 
 
+def _free_port() -> int:
+    """A port no other job holds right now (rendezvous on shared machines)."""
+    import socket
+
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
+
+
 def _rank(rank, world, port, out_dir):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -48,7 +57,7 @@ def _rank(rank, world, port, out_dir):
 def test_gloo_two_ranks_sum_to_full_batch_gradient():
     world = 2
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_rank, args=(world, 29617, d), nprocs=world, start_method="spawn")
+        mp.start_processes(_rank, args=(world, _free_port(), d), nprocs=world, start_method="spawn")
         got = np.load(os.path.join(d, "dp.npz"))
         rng = oracle.Rng(11)
         model = oracle.Mlp([6, 12, 5])
@@ -168,6 +177,6 @@ def _sharded_rank(rank, world, port, out_dir):
 def test_gloo_sharded_update_equals_replicated_update():
     world = 2
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_sharded_rank, args=(world, 29618, d), nprocs=world, start_method="spawn")
+        mp.start_processes(_sharded_rank, args=(world, _free_port(), d), nprocs=world, start_method="spawn")
         got = np.load(os.path.join(d, "sharded.npz"))
         assert np.array_equal(got["replicated"], got["sharded"])

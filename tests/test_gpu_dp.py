@@ -3,6 +3,7 @@ allreduce of dW/db inside the captured step equals the single-GPU global
 batch, and the replicas stay bit-identical under Adam."""
 import json
 import os
+import socket
 import subprocess
 import sys
 
@@ -10,6 +11,12 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _free_port() -> int:
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
 
 
 def test_two_rank_dp_equals_single_gpu(tmp_path):
@@ -20,7 +27,7 @@ def test_two_rank_dp_equals_single_gpu(tmp_path):
     out = tmp_path / "dp.json"
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29531",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            os.path.join(HERE, "dp_worker.py"), str(out)]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
@@ -29,14 +36,21 @@ def test_two_rank_dp_equals_single_gpu(tmp_path):
     assert max(res["f32_chunked"]) <= 1e-5, res["f32_chunked"]
     assert max(res["bf16_gradcomm"]) <= 2e-2, res["bf16_gradcomm"]
     assert max(res["bf16"]) <= 2e-2, res["bf16"]
+    # the summed DP gradients against the CPU oracle on the same global batch
+    # (the reference's CPU step): the north-star bars, 1e-4 for f32 plans and
+    # 2e-2 for bf16 ones
+    for case, bar in (("f32", 1e-4), ("f32_chunked", 1e-4), ("bf16", 2e-2), ("bf16_gradcomm", 2e-2)):
+        assert max(res[case + "_oracle"]) <= bar, (case, res[case + "_oracle"])
+        dp, _, cpu = res[case + "_loss"]
+        assert abs(dp - cpu) <= (1e-5 if case.startswith("f32") else 1e-3) * abs(cpu), (case, dp, cpu)
     assert res["replicas_identical"]
     # the global-batch loss from all-gathered per-row losses, summed in global
     # row order, is the single-GPU loss (rows are independent; here both runs
     # pick the same GEMM kernels, so it agrees to rounding of the last bit)
     for case in ("f32", "bf16", "f32_chunked", "bf16_gradcomm"):
-        dp, single = res[case + "_loss"]
+        dp, single, _ = res[case + "_loss"]
         assert abs(dp - single) <= 1e-6 * abs(single), (case, dp, single)
-    for name, mode in (("sharded", "sharded_opt"), ("sharded_p2p", "sharded_p2p")):
+    for name, mode in (("sharded", "sharded_opt"), ("sharded_p2p", "sharded_p2p"), ("sharded_ce", "sharded_ce")):
         sh = res[name]
         assert sh["modes"] == ["allreduce", mode], sh
         # two ranks: a + b in either exchange, the same elementwise update

@@ -254,6 +254,46 @@ def test_forward_only_and_logits(gpu):
     assert erro_rel(model.logits(64), mlp.logits()) < 1e-5
 
 
+def _suite_data(n, d, shift=0.0):
+    """examples/suite.rs:27-32: x[i, j] = sin(0.01 i + 0.03 j) (+ shift)."""
+    i = np.arange(n, dtype=np.float32).reshape(n, 1)
+    j = np.arange(d, dtype=np.float32).reshape(1, d)
+    return np.sin(i * np.float32(0.01) + j * np.float32(0.03) + np.float32(shift)).astype(np.float32)
+
+
+@pytest.mark.parametrize("batch", [1, 32, 512, 4096])
+def test_inference_at_the_reference_batches(gpu, batch):
+    # examples/suite.rs:204-240: MLP 512 -> 1024 -> 1024 -> 10 (f32, Glorot
+    # from Rng::new(7)), forward_only at batch 1 / 32 / 512 / 4096 against
+    # Sequential::predict.  The forward runs as a captured graph: replaying it
+    # on new inputs must give the new logits, and the host-buffer entry point
+    # the same logits as the device one.
+    dims = [512, 1024, 1024, 10]
+    model = glorot_model(dims, 7)
+    mlp = rgpu_b200.GpuMlp.from_params(gpu, model.params(), batch, 0.0, optimizer="none")
+    for shift in (0.0, 0.5, 1.25):
+        x = _suite_data(batch, dims[0], shift)
+        mlp.forward_only(gpu.upload(x))
+        got = mlp.logits()
+        model.forward(x, threads=4)
+        want = model.logits(batch)
+        assert erro_rel(want, got) < 1e-5, f"batch {batch} shift {shift}: {erro_rel(want, got):.2e}"
+        host = mlp.forward_host(x)
+        assert np.array_equal(host, got)
+    assert mlp.dispatches_por_passo() > 0
+
+
+def test_bf16_inference_logits_meet_the_bar(gpu):
+    # The wide bf16 model's forward alone (split activations), against the
+    # plain f32 reference on the same bf16 inputs and weights.
+    dims = [4096, 8192, 8192, 8192, 1000]
+    model, x, _ = bf16_baseline_inputs(dims, 128, 31)
+    mlp = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 128, 0.0, dtype="bf16", optimizer="none")
+    mlp.forward_only(gpu.upload(x, "bf16"))
+    model.forward(x, threads=8)
+    assert rel_l2(mlp.logits(), model.logits(128)) <= 2e-2
+
+
 def test_batch_mismatch_is_an_error(gpu):
     model = glorot_model([8, 16, 4], 3)
     mlp = rgpu_b200.GpuMlp.from_params(gpu, model.params(), 64, 0.0)

@@ -436,3 +436,46 @@ def test_cast_rounds_to_nearest_even(gpu):
     gpu.cast(src, dst)
     want = rgpu_b200.bf16_to_f32(rgpu_b200.f32_to_bf16(x))
     assert np.array_equal(gpu.download(dst).ravel(), want)
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 1024, 512), (5, 1000, 1024), (16, 130, 300), (17, 4096, 257),
+                                   (64, 1024, 1024), (32, 8192, 4096)])
+def test_few_row_gemms(gpu, m, n, k):
+    # Forward GEMMs at small batch (layout NN, m <= 16, or m <= 64 for f32):
+    # a cluster of CTAs splits k and sums in a fixed order.  Against the exact
+    # product, with the bias and bias + ReLU epilogues; bf16 operands (m <= 16)
+    # also with A as hi + lo planes and a lo output plane.
+    a, b = _ab(m, n, k)
+    bias = np.linspace(-1, 1, n, dtype=np.float32).reshape(1, n)
+    gbias = gpu.upload(bias)
+    for dtype in ("f32", "bf16"):
+        if dtype == "bf16" and m > 16:
+            continue
+        x = a if dtype == "f32" else rgpu_b200.bf16_to_f32(rgpu_b200.f32_to_bf16(a))
+        w = b if dtype == "f32" else rgpu_b200.bf16_to_f32(rgpu_b200.f32_to_bf16(b))
+        gx, gw = gpu.upload(x, dtype), gpu.upload(w, dtype)
+        for epi in (G.RT_EPI_NONE, G.RT_EPI_BIAS, G.RT_EPI_BIAS_RELU):
+            c = gpu.zeros((m, n))
+            args = G.GemmArgs(G.RT_NN, G.RT_BF16 if dtype == "bf16" else G.RT_F32, G.RT_F32, m, n, k,
+                              gx.ptr, gx.ld, gw.ptr, gw.ld, c.ptr, c.ld, epi, gbias.ptr, None, 0, 1, None, 0)
+            before = gpu.launch_count()
+            gpu.gemm(args)
+            gpu.sync()
+            assert gpu.launch_count() - before == 1
+            ref = _skinny_ref(x, w, epi, bias, None)
+            e = rel_l2(gpu.download(c), ref)
+            assert e <= 1e-5, f"{dtype} epi {epi} {m}x{n}x{k}: {e:.2e}"
+    if m <= 16:
+        # split A planes and a bf16 output with its lo plane
+        hi = rgpu_b200.bf16_to_f32(rgpu_b200.f32_to_bf16(np.abs(a)))
+        lo = rgpu_b200.bf16_to_f32(rgpu_b200.f32_to_bf16(np.abs(a) - hi))
+        w = rgpu_b200.bf16_to_f32(rgpu_b200.f32_to_bf16(b))
+        ghi, glo, gw = gpu.upload(hi, "bf16"), gpu.upload(lo, "bf16"), gpu.upload(w, "bf16")
+        chi, clo = gpu.zeros((m, n), "bf16"), gpu.zeros((m, n), "bf16")
+        args = G.GemmArgs(G.RT_NN, G.RT_BF16, G.RT_BF16, m, n, k, ghi.ptr, ghi.ld, gw.ptr, gw.ld, chi.ptr, chi.ld,
+                          G.RT_EPI_BIAS_RELU, gbias.ptr, None, 0, 1, None, 0)
+        args.a_lo, args.c_lo = glo.ptr, clo.ptr
+        gpu.gemm(args)
+        ref = _skinny_ref((hi.astype(np.float64) + lo), w, G.RT_EPI_BIAS_RELU, bias, None)
+        got = gpu.download(chi).astype(np.float64) + gpu.download(clo)
+        assert rel_l2(got, ref) <= 1e-5, f"split {m}x{n}x{k}: {rel_l2(got, ref):.2e}"

@@ -1,9 +1,10 @@
 """The allocation-free split-K entry point (rt_matmul_split_k_noalloc).
 
 Some callers cannot allocate device memory at the moment they call in (for
-example while a CUDA graph is being captured, or when a host framework's own
-allocator owns the device memory), so this variant keeps its split-K partial
-sums in a fixed scratch array inside librtgpu.so instead of a caller buffer.
+example when a host framework's own allocator owns the device memory, or in
+a loop that forbids allocation after start-up), so this variant keeps its
+split-K partial sums in a fixed scratch array inside librtgpu.so instead of a
+caller buffer.
 These tests call it through the C ABI and check it against the existing
 rt_matmul_split_k (caller-provided partials) on two calls in a row, within the
 split-K tolerance of the other GEMM tests.  This file is named to be
