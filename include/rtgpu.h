@@ -338,6 +338,24 @@ typedef enum {
     RT_COMM_SHARDED_CE = 5
 } rt_comm_mode;
 int rt_mlp_comm_mode(rt_mlp* mlp, int* mode);
+/* The plan's data-parallel layout, as host-only queries (no device or plan
+ * needed), so that a host runtime sharding the same parameter blocks can agree
+ * with the library on where every slice lives.  No counterpart in the
+ * reference (GpuMlp is single-device); they describe rt_mlp_set_comm's
+ * exchange.  A layer with d inputs and `units` outputs keeps W and b as one
+ * [d+1, rt_plan_ld(units)] f32 block (bias last).  Its dW GEMM runs in
+ * rt_plan_dw_chunks(...) row chunks (data_parallel: a communicator is
+ * attached; fused_update: one device with SGD/Adam, the update inside the dW
+ * epilogue; honours RTGPU_FIRST_LAYER_CHUNKS / RTGPU_DW_CHUNKS); chunk c holds
+ * rows [rt_plan_chunk_row(d+1, chunks, c), rt_plan_chunk_row(d+1, chunks, c+1)).
+ * Under the sharded optimiser rank r of `world` updates the flat elements
+ * [*offset, *offset + returned length) of each chunk's weight rows (the bias
+ * row stays replicated); -1 on bad arguments. */
+int64_t rt_plan_ld(int64_t units);
+int rt_plan_dw_chunks(int layer, int64_t d, int64_t units, int data_parallel, int fused_update);
+int64_t rt_plan_chunk_row(int64_t rows, int chunks, int c);
+int64_t rt_plan_shard_slice(int64_t d, int64_t units, int64_t r0, int64_t r1, int world, int rank,
+                            int64_t* offset);
 
 /* ------------------------------------------------------ autodiff tape */
 /* Reverse-mode tape on the GPU for the ops a Dense network is made of.  All

@@ -174,6 +174,18 @@ __global__ void cast_kernel(const TS* s, int64_t lds, TD* d, int64_t ldd, int64_
     }
 }
 
+// Same-dtype copy of a row-strided matrix whose rows start 16-byte aligned
+// and hold a whole number of 16-byte vectors: a block per row (grid-stride
+// over rows), 16-byte loads and stores, no index division.
+__global__ void copy_rows_v16_kernel(const uint4* s, int64_t lds16, uint4* d, int64_t ldd16, int64_t rows,
+                                     int64_t vecs) {
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const uint4* sr = s + r * lds16;
+        uint4* dr = d + r * ldd16;
+        for (int64_t v = threadIdx.x; v < vecs; v += blockDim.x) dr[v] = __ldg(sr + v);
+    }
+}
+
 // ------------------------------------------------------------ optimisers
 struct OptBatch {
     OptTensor t[kMaxOptTensors];
@@ -485,6 +497,21 @@ int launch_relu_bwd(rt_ctx* ctx, const void* a, void* dz, rt_dtype dt, int64_t r
 int launch_cast(rt_ctx* ctx, const void* src, rt_dtype sdt, int64_t lds, void* dst, rt_dtype ddt, int64_t ldd,
                 int64_t rows, int64_t cols, cudaStream_t st) {
     if (rows * cols == 0) return RT_OK;
+    if (sdt == ddt) {
+        const int64_t es = sdt == RT_BF16 ? 2 : 4;
+        const bool v16 = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0 &&
+                         (lds * es) % 16 == 0 && (ldd * es) % 16 == 0 && (cols * es) % 16 == 0;
+        if (v16) {
+            const int64_t cap = (int64_t)ctx->sm_count * 8;
+            const unsigned blocks = (unsigned)(rows < cap ? rows : cap);
+            copy_rows_v16_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint4*>(src), lds * es / 16,
+                                                         static_cast<uint4*>(dst), ldd * es / 16, rows,
+                                                         cols * es / 16);
+            count_launch(ctx);
+            RT_CUDA(cudaGetLastError());
+            return RT_OK;
+        }
+    }
     unsigned g = grid_for(ctx, rows * cols);
     if (sdt == RT_F32 && ddt == RT_BF16)
         cast_kernel<float, __nv_bfloat16><<<g, 256, 0, st>>>((const float*)src, lds, (__nv_bfloat16*)dst, ldd, rows,

@@ -409,9 +409,9 @@ __global__ void __launch_bounds__(kThreads) skinny_k_kernel(SkinnyParams p) {
     }
 }
 
-// Few rows (layout NN, m <= 16, or m <= 64 for f32 operands, whose tensor-core
-// path would be three tf32 products behind an operand split: the forward
-// pass at small batch):
+// Few rows (layouts NN and TN, m <= 16, or m <= 64 for f32 operands, whose
+// tensor-core path would be three tf32 products behind an operand split: the
+// forward pass at small batch, and dW of a layer with few inputs):
 // a GEMV-like pass over B.  A cluster of kClusterK CTAs owns 64 columns of C
 // (lane l of every warp holds columns 2 l and 2 l + 1) and splits k: CTA r of
 // the cluster takes the r-th k range, and its 8 warps split that range again.
@@ -438,9 +438,10 @@ __device__ __forceinline__ float2 ld2_f<__nv_bfloat16>(const __nv_bfloat16* p) {
     return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
 }
 
-template <typename TIn>
+template <typename TIn, bool A_KM>
 __global__ void __cluster_dims__(kClusterK, 1, 1) __launch_bounds__(kThreads)
     skinny_m_kernel(SkinnyParams p) {
+    // A_KM: A is stored [k, m] (layout TN), else [m, k] (layout NN)
     // sa (A rows of the k chunk) during the k loop; red (the warps' sums)
     // after it, in the same shared memory
     __shared__ __align__(16) float buf[kThreads / 32][kMRows][64];
@@ -469,10 +470,11 @@ __global__ void __cluster_dims__(kClusterK, 1, 1) __launch_bounds__(kThreads)
             const int kn = (int)min((int64_t)kKChunk, k_hi - kc);
             __syncthreads();  // the previous chunk's reads of sa are done
             for (int t = threadIdx.x; t < kMRows * kKChunk; t += kThreads) {
-                const int i = t / kKChunk, q = t % kKChunk;
+                // consecutive threads read consecutive elements of A's stored rows
+                const int i = A_KM ? t % kMRows : t / kKChunk, q = A_KM ? t / kMRows : t % kKChunk;
                 float v = 0.0f;
                 if (i < rows && q < kn) {
-                    const int64_t ai = (m0 + i) * p.lda + kc + q;
+                    const int64_t ai = A_KM ? (kc + q) * p.lda + m0 + i : (m0 + i) * p.lda + kc + q;
                     v = ld_f(A, ai);
                     if (A2) v += ld_f(A2, ai);
                 }
@@ -536,7 +538,7 @@ __global__ void __cluster_dims__(kClusterK, 1, 1) __launch_bounds__(kThreads)
 
 // The few-row kernel's GEMMs (n and k wider than the skinny limit).
 bool few_rows(const GemmDesc& g) {
-    if (g.layout != RT_NN || g.n <= kSkinnyMax || g.k <= kSkinnyMax || g.opt.kind || g.split_k > 1 || g.p2p.world)
+    if ((g.layout != RT_NN && g.layout != RT_TN) || g.n <= kSkinnyMax || g.k <= kSkinnyMax || g.opt.kind || g.split_k > 1 || g.p2p.world)
         return false;
     return g.m <= kSkinnyMax || (g.in_dtype == RT_F32 && g.m <= kSkinnyRowsMax);
 }
@@ -578,7 +580,10 @@ int launch_typed(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     if (few_rows(g)) {
         const int64_t groups = (g.n + 63) / 64;
         if (groups * kClusterK > (int64_t)INT32_MAX) return fail(RT_ERR_INVALID, "few-row GEMM n too large");
-        skinny_m_kernel<TIn><<<(unsigned)(groups * kClusterK), kThreads, 0, st>>>(p);
+        if (g.layout == RT_TN)
+            skinny_m_kernel<TIn, true><<<(unsigned)(groups * kClusterK), kThreads, 0, st>>>(p);
+        else
+            skinny_m_kernel<TIn, false><<<(unsigned)(groups * kClusterK), kThreads, 0, st>>>(p);
         count_launch(ctx);
         RT_CUDA(cudaGetLastError());
         return RT_OK;

@@ -3,14 +3,17 @@
 // rtensor's f32 GEMMs (crates/rtensor/src/gpu/gemm.rs MM_FAST, splitk.rs
 // MM_SPLITK) compute in full f32 and the f32 parity bar is 1e-4 relative L2
 // per gradient, which a single tf32 product (10 explicit mantissa bits) does
-// not meet.  Each operand x is split exactly into
-//     hi = x with its 13 low mantissa bits cleared   (a tf32 value)
-//     lo = x - hi                                    (exact in f32)
+// not meet.  Each operand x is split into
+//     hi = x rounded to the nearest tf32 value        (ties to even)
+//     lo = x - hi rounded to the nearest tf32 value   (x - hi is exact in f32)
 // and C = lo(A) hi(B) + hi(A) lo(B) + hi(A) hi(B), all three accumulated in
-// one TMEM accumulator.  The dropped lo*lo term and the tf32 reading of lo
-// are below 2^-20 of each product, so the result tracks an f32 GEMM to about
-// 1e-6 relative; the tensor-core accumulation adds its own rounding, which
-// grows with k as in the bf16 path.
+// one TMEM accumulator.  |x - hi| <= 2^-11 |x| and the part of x that lo
+// drops is <= 2^-22 |x|, so the dropped lo*lo term and lo's rounding are
+// about 2^-22 of each product, and with both roundings to nearest their
+// errors carry no sign bias that would add up along k (clearing low bits
+// instead gives every product an error of the product's own sign, which
+// accumulates coherently on data whose sums cancel).  The tensor-core
+// accumulation adds its own rounding, which grows with k as in the bf16 path.
 //
 // The split runs as one pass that writes both operands' hi/lo planes into a
 // workspace, K-major for both ([m][k] for A, [n][k] for B): tcgen05 reads
@@ -65,13 +68,25 @@ Operand operand_b(const GemmDesc& g) {
 
 size_t plane_floats(const Operand& o) { return (size_t)o.mn * (size_t)o.ldw; }
 
+// Rounds a finite f32 to the nearest tf32 value (10 explicit mantissa bits),
+// ties to even: add just under half a tf32 ulp plus the lowest kept bit, then
+// clear the 13 dropped bits (a carry out of the mantissa steps the exponent,
+// which is the correctly rounded result).
+__device__ __forceinline__ float tf32_round(float x) {
+    uint32_t u = __float_as_uint(x);
+    u = (u + 0xFFFu + ((u >> 13) & 1u)) & 0xFFFFE000u;
+    return __uint_as_float(u);
+}
+
 // Non-finite values go whole into the hi plane (a NaN keeps its payload);
 // the GEMM then yields a non-finite output row, NaN where the hi(A) lo(B)
-// product meets inf * 0.
+// product meets inf * 0.  A finite x within half a tf32 ulp of FLT_MAX, which
+// would round to inf, keeps its truncated hi.
 __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
     if (isfinite(x)) {
-        hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
-        lo = x - hi;  // exact: the cleared bits of x
+        hi = tf32_round(x);
+        if (!isfinite(hi)) hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+        lo = tf32_round(x - hi);  // x - hi is exact: x and hi share all but the low bits
     } else {
         hi = x;
         lo = 0.0f;

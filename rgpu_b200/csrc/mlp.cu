@@ -53,6 +53,10 @@ int64_t round8(int64_t x) { return (x + 7) / 8 * 8; }
 // Row strides of GEMM operands are kept at multiples of 64 elements so every
 // 128-byte TMA row segment starts on a 128-byte line.
 int64_t round64(int64_t x) { return (x + 63) / 64 * 64; }
+// Leading dimension (elements) of a layer's [d+1, u] blocks: 64-element
+// multiples (128-byte TMA row segments), 8 below 64 units.
+int64_t plan_ld(int64_t u) { return u >= 64 ? round64(u) : round8(u); }
+
 // Start row of chunk c of `rows` rows cut into the plan's first-layer chunks
 // (boundaries on 256-row tile edges; the last chunk takes the remainder).
 int64_t chunk_row_of(int64_t rows, int chunks, int c) {
@@ -284,15 +288,27 @@ int enqueue_update_flat(rt_mlp* m, PlanLayer& P, int64_t o, int64_t n, cudaStrea
 // epilogue reads in f32, stays replicated (allreduced, updated on every rank).
 int64_t shard_end(const PlanLayer& P, int64_t r1) { return r1 < P.d ? r1 : P.d; }
 
+// This rank's flat slice of the weight rows of chunk [r0, r1) of a [d+1, ld]
+// parameter block: its length (0 when the chunk holds only the bias row) and,
+// in *off, its first element.
+int64_t shard_slice(int64_t d, int64_t ld, int64_t r0, int64_t r1, int world, int rank, int64_t* off) {
+    const int64_t e = r1 < d ? r1 : d;
+    if (e <= r0 || world < 1) {
+        *off = r0 * ld;
+        return 0;
+    }
+    const int64_t piece = (e - r0) * ld / world;
+    *off = r0 * ld + (int64_t)rank * piece;
+    return piece;
+}
+
 // Rows [r0, r1) of the parameter block: the whole range, or under the sharded
 // optimiser this rank's slice of the weight rows plus the bias row.
 int enqueue_update_rows(rt_mlp* m, PlanLayer& P, int64_t r0, int64_t r1, cudaStream_t st) {
     if (!m->sharded) return enqueue_update_flat(m, P, r0 * P.ld, (r1 - r0) * P.ld, st);
-    const int64_t e = shard_end(P, r1);
-    if (e > r0) {
-        const int64_t piece = (e - r0) * P.ld / m->world;
-        RT_TRY(enqueue_update_flat(m, P, r0 * P.ld + (int64_t)m->rank * piece, piece, st));
-    }
+    int64_t off = 0;
+    const int64_t piece = shard_slice(P.d, P.ld, r0, r1, m->world, m->rank, &off);
+    if (piece > 0) RT_TRY(enqueue_update_flat(m, P, off, piece, st));
     if (r1 > P.d) RT_TRY(enqueue_update_flat(m, P, P.d * P.ld, P.ld, st));
     return RT_OK;
 }
@@ -761,19 +777,24 @@ int setup_ce(rt_mlp* m) {
 // smaller layers lose more to the narrower GEMMs than the overlap gains); 4
 // chunks for >= 4096 rows, 2 for >= 2048.  RTGPU_FIRST_LAYER_CHUNKS /
 // RTGPU_DW_CHUNKS override.
-int prepare_chunks(rt_mlp* m) {
+int dw_chunks(size_t layer, int64_t d, int64_t ld, bool data_parallel, bool fused_update) {
     auto rule = [](int64_t rows) { return rows >= 4096 ? 4 : rows >= 2048 ? 2 : 1; };
     const char* env0 = getenv("RTGPU_FIRST_LAYER_CHUNKS");
     const char* envd = getenv("RTGPU_DW_CHUNKS");
+    const int64_t rows = d + 1;
+    int ch = 1;
+    if (layer == 0 && !fused_update) ch = env0 && env0[0] ? atoi(env0) : rule(rows);
+    else if (data_parallel) ch = envd && envd[0] ? atoi(envd) : rows * ld * 4 >= (128ll << 20) ? rule(rows) : 1;
+    if (ch < 1) ch = 1;
+    if (ch > 8) ch = 8;
+    while (ch > 1 && chunk_row_of(rows, ch, 1) == 0) --ch;  // every chunk non-empty
+    return ch;
+}
+
+int prepare_chunks(rt_mlp* m) {
     for (size_t l = 0; l < m->L.size(); ++l) {
         PlanLayer& P = m->L[l];
-        const int64_t rows = P.d + 1;
-        int ch = 1;
-        if (l == 0 && !m->fuse_opt) ch = env0 && env0[0] ? atoi(env0) : rule(rows);
-        else if (m->comm) ch = envd && envd[0] ? atoi(envd) : rows * P.ld * 4 >= (128ll << 20) ? rule(rows) : 1;
-        if (ch < 1) ch = 1;
-        if (ch > 8) ch = 8;
-        while (ch > 1 && chunk_row_of(rows, ch, 1) == 0) --ch;  // every chunk non-empty
+        const int ch = dw_chunks(l, P.d, P.ld, m->comm != nullptr, m->fuse_opt);
         if (ch == P.chunks && !P.ev_ready.empty()) continue;
         for (auto e : P.ev_ready) cudaEventDestroy(e);
         for (auto e : P.ev_comm) cudaEventDestroy(e);
@@ -933,6 +954,23 @@ int refresh_shadow(rt_mlp* m, PlanLayer& P, cudaStream_t st) {
 
 extern "C" {
 
+int64_t rt_plan_ld(int64_t units) { return units < 1 ? 0 : plan_ld(units); }
+
+int rt_plan_dw_chunks(int layer, int64_t d, int64_t units, int data_parallel, int fused_update) {
+    if (layer < 0 || d < 1 || units < 1) return 0;
+    return dw_chunks((size_t)layer, d, plan_ld(units), data_parallel != 0, fused_update != 0);
+}
+
+int64_t rt_plan_chunk_row(int64_t rows, int chunks, int c) {
+    if (rows < 0 || chunks < 1 || c < 0) return -1;
+    return chunk_row_of(rows, chunks, c);
+}
+
+int64_t rt_plan_shard_slice(int64_t d, int64_t units, int64_t r0, int64_t r1, int world, int rank, int64_t* offset) {
+    if (!offset || d < 1 || units < 1 || world < 1 || rank < 0 || rank >= world || r0 < 0 || r1 < r0) return -1;
+    return shard_slice(d, plan_ld(units), r0, r1, world, rank, offset);
+}
+
 int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* weights, const float* const* biases,
                   rt_mlp** out) {
     RT_CHECK(ctx && cfg && out && weights, "rt_mlp_create: bad arguments");
@@ -982,7 +1020,7 @@ int rt_mlp_create(rt_ctx* ctx, const rt_mlp_config* cfg, const float* const* wei
         PlanLayer& P = m->L[l];
         P.d = m->dims[l];
         P.u = m->dims[l + 1];
-        P.ld = P.u >= 64 ? round64(P.u) : round8(P.u);
+        P.ld = plan_ld(P.u);
         bool last = l == nl - 1;
         P.ld_act = last ? P.ld : round64(P.u + 1);
         size_t pn = (size_t)(P.d + 1) * P.ld;

@@ -130,6 +130,11 @@ _SIGS = [
                                  C.POINTER(C.c_float)]),
     ("rt_mlp_set_comm", C.c_int, [C.c_void_p, C.c_void_p]),
     ("rt_mlp_comm_mode", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("rt_plan_ld", C.c_int64, [C.c_int64]),
+    ("rt_plan_dw_chunks", C.c_int, [C.c_int, C.c_int64, C.c_int64, C.c_int, C.c_int]),
+    ("rt_plan_chunk_row", C.c_int64, [C.c_int64, C.c_int, C.c_int]),
+    ("rt_plan_shard_slice", C.c_int64, [C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_int, C.c_int,
+                                        C.POINTER(C.c_int64)]),
     ("rt_param_create", C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.POINTER(C.c_void_p)]),
     ("rt_param_destroy", C.c_int, [C.c_void_p]),
     ("rt_param_read", C.c_int, [C.c_void_p, C.c_void_p]),
@@ -630,6 +635,27 @@ class GpuMlp:
         v = C.c_int()
         _check(lib().rt_mlp_comm_mode(self.handle, C.byref(v)))
         return ("none", "allreduce", "allreduce_bf16", "sharded_opt", "sharded_p2p", "sharded_ce")[v.value]
+
+
+def plan_layout(layer: int, d: int, units: int, world: int = 1, rank: int = 0, data_parallel: bool = True,
+                fused_update: bool = False):
+    """The plan's data-parallel layout of one layer, from the library's own
+    rules (host only, no device): the [d+1, ld] block's leading dimension, and
+    per dW chunk its rows [r0, r1) and this rank's flat weight slice
+    (offset, length) under the sharded optimiser."""
+    L = lib()
+    ld = int(L.rt_plan_ld(units))
+    chunks = int(L.rt_plan_dw_chunks(layer, d, units, int(data_parallel), int(fused_update)))
+    out = []
+    for c in range(chunks):
+        r0 = int(L.rt_plan_chunk_row(d + 1, chunks, c))
+        r1 = int(L.rt_plan_chunk_row(d + 1, chunks, c + 1))
+        off = C.c_int64(0)
+        n = int(L.rt_plan_shard_slice(d, units, r0, r1, world, rank, C.byref(off)))
+        if n < 0:
+            raise RtError(RT_ERR_INVALID, "rt_plan_shard_slice: bad arguments")
+        out.append((r0, r1, int(off.value), n))
+    return ld, out
 
 
 def _is_bf16(t: GpuTensor) -> bool:

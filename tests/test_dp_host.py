@@ -71,8 +71,18 @@ def test_gloo_two_ranks_sum_to_full_batch_gradient():
 
 
 def _chunk_row_of(rows, chunks, c):
-    # mlp.cu chunk_row_of: chunk starts on 256-row edges, the last takes the rest
-    return rows if c >= chunks else rows * c // chunks // 256 * 256
+    # the library's chunk edges (mlp.cu chunk_row_of: chunk starts on 256-row
+    # edges, the last chunk takes the rest)
+    from rgpu_b200.gpu import lib
+
+    return int(lib().rt_plan_chunk_row(rows, chunks, c))
+
+
+def test_chunk_edges_follow_the_256_row_rule():
+    for rows, chunks in [(8193, 4), (4097, 4), (2049, 2), (513, 2), (1001, 3)]:
+        edges = [_chunk_row_of(rows, chunks, c) for c in range(chunks + 1)]
+        assert edges[0] == 0 and edges[-1] == rows
+        assert all(e % 256 == 0 for e in edges[:-1]) and edges == sorted(edges)
 
 
 @pytest.mark.parametrize("d,ld,world,chunks", [(4096, 8192, 8, 4), (8192, 1024, 8, 4), (1024, 512, 2, 4),
@@ -111,19 +121,33 @@ def test_peer_scatter_layout_is_the_flat_reduce_scatter(d, ld, world, chunks):
             got_rows = [r0 + o * h + k for k in range(h)]
             flat0 = r0 * ld + o * ((e - r0) * ld // world)
             assert got_rows[0] * ld == flat0 and len(window) * ld == (e - r0) * ld // world
+            # ... which is the library's shard slice of owner o (ld == units here)
+            import ctypes
+
+            from rgpu_b200.gpu import lib
+
+            off = ctypes.c_int64(0)
+            assert lib().rt_plan_shard_slice(d, ld, r0, r1, world, o, ctypes.byref(off)) == len(window) * ld
+            assert off.value == flat0
     for o in range(world):
         assert len(seen[o]) == world * d // world  # every source's every owned row, once
 
 
 def _sharded_rank(rank, world, port, out_dir):
-    # The sharded optimiser's slicing (mlp.cu: shard_end, enqueue_update_rows,
-    # allreduce_rows, gather_weights) on gloo ranks with the oracle's Adam:
-    # per chunk of [W; b] rows, rank r updates the flat slice
-    # [r0*u + r*piece, + piece), piece = (min(r1, d) - r0) * u / world, of the
-    # summed gradient; the bias row is summed and updated on every rank; the
-    # slices are then all-gathered.  Path A is the replicated update.
+    # The sharded optimiser's update on gloo ranks with the oracle's Adam, on
+    # the slices the library itself computes (rgpu_b200.gpu.plan_layout: the
+    # leading dimension, the dW chunk rows and each rank's flat slice, from
+    # mlp.cu's plan_ld, dw_chunks, chunk_row_of and shard_slice): per chunk of
+    # [W; b] rows rank r updates its slice of the summed gradient, the bias row
+    # is summed and updated on every rank, and the slices are all-gathered.
+    # Path A is the replicated update; both must give the same parameters.
+    from rgpu_b200.gpu import plan_layout
+
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
+    # two chunks where the rows allow it, so that the chunk edges are exercised
+    os.environ["RTGPU_DW_CHUNKS"] = "2"
+    os.environ["RTGPU_FIRST_LAYER_CHUNKS"] = "2"
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         dims, n = [512, 384, 10], 16
@@ -137,39 +161,45 @@ def _sharded_rank(rank, world, port, out_dir):
         grads = [g * (per / n) for g in model.grads()]
         params = model.params()
         out = {}
+        n_chunks = []
         for mode in ("replicated", "sharded"):
             thetas = []
             for l in range(len(dims) - 1):
                 d, u = dims[l], dims[l + 1]
-                theta = np.ascontiguousarray(np.concatenate([params[2 * l], params[2 * l + 1]]).ravel(), np.float32)
-                g = torch.from_numpy(np.concatenate([grads[2 * l], grads[2 * l + 1]]).ravel().copy())
+                ld, chunks = plan_layout(l, d, u, world, rank, data_parallel=True)
+                # the [d+1, ld] parameter block, padding columns zero
+                block = np.zeros((d + 1, ld), np.float32)
+                block[:d, :u], block[d, :u] = params[2 * l], params[2 * l + 1].ravel()
+                theta = block.ravel()
+                gblock = np.zeros((d + 1, ld), np.float32)
+                gblock[:d, :u], gblock[d, :u] = grads[2 * l], grads[2 * l + 1].ravel()
+                g = torch.from_numpy(gblock.ravel().copy())
                 dist.all_reduce(g)  # the sum (a reduce-scatter keeps only this rank's slice of it)
                 g = g.numpy()
                 mm, vv = np.zeros_like(theta), np.zeros_like(theta)
                 if mode == "replicated":
                     oracle.adam_update(theta, mm, vv, g, 1e-3, 1)
                 else:
-                    rows = d + 1
-                    chunks = 2 if rows >= 512 else 1
-                    for c in range(chunks):
-                        r0, r1 = _chunk_row_of(rows, chunks, c), _chunk_row_of(rows, chunks, c + 1)
+                    n_chunks.append(len(chunks))
+                    covered = 0
+                    for r0, r1, a, piece in chunks:
                         e = min(r1, d)
-                        piece = (e - r0) * u // world
-                        assert (e - r0) * u % world == 0
-                        a = r0 * u + rank * piece
+                        assert piece * world == (e - r0) * ld and a == r0 * ld + rank * piece
                         th, m_, v_ = theta[a:a + piece], mm[a:a + piece], vv[a:a + piece]
                         oracle.adam_update(th, m_, v_, g[a:a + piece], 1e-3, 1)
                         if r1 > d:  # the bias row, replicated
-                            b0 = d * u
-                            th, m_, v_ = theta[b0:b0 + u], mm[b0:b0 + u], vv[b0:b0 + u]
-                            oracle.adam_update(th, m_, v_, g[b0:b0 + u], 1e-3, 1)
+                            b0 = d * ld
+                            th, m_, v_ = theta[b0:b0 + ld], mm[b0:b0 + ld], vv[b0:b0 + ld]
+                            oracle.adam_update(th, m_, v_, g[b0:b0 + ld], 1e-3, 1)
                         parts = [torch.zeros(piece) for _ in range(world)]
                         dist.all_gather(parts, torch.from_numpy(theta[a:a + piece].copy()))
-                        theta[r0 * u:r0 * u + world * piece] = torch.cat(parts).numpy()
+                        theta[r0 * ld:r0 * ld + world * piece] = torch.cat(parts).numpy()
+                        covered += world * piece
+                    assert covered == d * ld  # the slices tile the weight rows exactly
                 thetas.append(theta)
             out[mode] = np.concatenate(thetas)
         if rank == 0:
-            np.savez(os.path.join(out_dir, "sharded.npz"), **out)
+            np.savez(os.path.join(out_dir, "sharded.npz"), chunks=np.array(n_chunks), **out)
     finally:
         dist.destroy_process_group()
 
@@ -179,4 +209,5 @@ def test_gloo_sharded_update_equals_replicated_update():
     with tempfile.TemporaryDirectory() as d:
         mp.start_processes(_sharded_rank, args=(world, _free_port(), d), nprocs=world, start_method="spawn")
         got = np.load(os.path.join(d, "sharded.npz"))
+        assert list(got["chunks"]) == [2, 1]  # the first layer in two chunks; 385 rows allow one
         assert np.array_equal(got["replicated"], got["sharded"])
