@@ -105,7 +105,10 @@ __device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t adesc, uin
     }
 }
 
-template <typename TIn, int BN>
+// EB: 4 KB staging boxes per epilogue warp.  Launches with a short k loop
+// take EB = 4 (more output stores in flight per warp, which is what bounds a
+// small-k GEMM) and give up three stages of the operand ring for them.
+template <typename TIn, int BN, int EB = 1>
 struct Geo2 {
     static constexpr int ES = sizeof(TIn);
     static constexpr int BK = 128 / ES;
@@ -115,21 +118,22 @@ struct Geo2 {
     static constexpr int A_BYTES = 128 * 128;
     static constexpr int B_BYTES = BNH * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
+    static constexpr int STAGES = (192 * 1024 - (EB - 1) * kEpiWarps * kStageBytes) / STAGE_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int EPI_BYTES = kEpiWarps * kStageBytes;
+    static constexpr int EPI_BYTES = EB * kEpiWarps * kStageBytes;
+    static_assert(STAGES >= 2, "operand ring too short");
     static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
 };
 
 // Split bf16 A (p.split_a) and a bf16 output's low-order plane (p.c_lo): as
 // in the one-CTA kernel, through tmap_a2 and tmap_c2.
-template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false, bool SPLIT_C = false>
+template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false, bool SPLIT_C = false, int EB = 1>
 __global__ void __launch_bounds__(kThreads2, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CUtensorMap tmap_a2,
                     const __grid_constant__ CUtensorMap tmap_c2, TcParams p) {
     static_assert(!X3 || (sizeof(TIn) == 4 && !A_MN && !B_MN), "3xTF32 planes are f32 and K-major");
-    using G = Geo2<TIn, BN>;
+    using G = Geo2<TIn, BN, EB>;
     constexpr bool kTF32 = sizeof(TIn) == 4;
     constexpr int STAGES = G::STAGES;
     constexpr uint32_t IDESC = make_idesc(kTF32, A_MN, B_MN, BN, BM2);
@@ -320,6 +324,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
         const int half = (warp - 4) >> 2;     // column half of the tile
         int acc = 0;
         uint32_t acc_phase = 0;
+        uint32_t store_seq = 0;  // chunks this warp has staged (its slot ring position)
         bool ok = true;
         for (int t = cluster_id; t < total_tiles; t += num_clusters) {
             int split, mb, nb;
@@ -338,29 +343,37 @@ __global__ void __launch_bounds__(kThreads2, 1)
                 const int64_t col0 = (int64_t)nb * BN + c;
                 if (col0 >= p.n) break;
                 float v[32];
+                // bf16 ReLU-mask epilogue: the mask's loads go out before the TMEM load
+                const bool pre_mask = p.tma_store == 1 && p.out_bf16 && p.epi == RT_EPI_RELU_MASK && row < p.m &&
+                                      col0 + 32 <= p.n;
+                uint4 mk[4];
+                if (pre_mask) load_mask_bf16(p, row, col0, mk);
                 tmem_ld_32x32(tbase + (uint32_t)c, v);
+                uint8_t* box = smem_epi + (warp - 4) * EB * kStageBytes;  // this warp's boxes
                 if (p.tma_store == 2) {
                     // staged split-K partials: slice `split` of the [splits][m][n] workspace
-                    stage_and_store<float>(&tmap_c, smem_epi + (warp - 4) * kStageBytes, lane, row0, col0, v, split);
+                    stage_and_store_ring<float>(&tmap_c, box, EB, lane, row0, col0, v, store_seq, split);
                 } else if (p.tma_store == 1) {
                     // staged: coalesced TMA stores of the warp's 32 x 32 chunk
-                    uint8_t* box = smem_epi + (warp - 4) * kStageBytes;
                     if (p.out_bf16) {
-                        if (row < p.m) epilogue_math<__nv_bfloat16>(p, row, col0, v);
+                        if (pre_mask)
+                            apply_mask_bf16(v, mk);
+                        else if (row < p.m)
+                            epilogue_math<__nv_bfloat16>(p, row, col0, v);
                         if constexpr (SPLIT_C)
                             stage_and_store_split(&tmap_c, &tmap_c2, box, lane, row0, col0, v);
                         else
-                            stage_and_store<__nv_bfloat16>(&tmap_c, box, lane, row0, col0, v);
+                            stage_and_store_ring<__nv_bfloat16>(&tmap_c, box, EB, lane, row0, col0, v, store_seq);
                     } else {
                         if (row < p.m) epilogue_math<float>(p, row, col0, v);
-                        stage_and_store<float>(&tmap_c, box, lane, row0, col0, v);
+                        stage_and_store_ring<float>(&tmap_c, box, EB, lane, row0, col0, v, store_seq);
                     }
                 } else if (p.tma_store == 4) {
                     // rows scattered to their owners' receive buffers (peer memory)
-                    p2p_chunk(p, reinterpret_cast<float*>(smem_epi + (warp - 4) * kStageBytes), lane, row0, col0, v);
+                    p2p_chunk(p, reinterpret_cast<float*>(box), lane, row0, col0, v);
                 } else if (p.tma_store == 3) {
                     // fused optimiser: the chunk updates theta / m / v / shadow and is stored as C
-                    opt_chunk(p, reinterpret_cast<float*>(smem_epi + (warp - 4) * kStageBytes), lane, row0, col0, v);
+                    opt_chunk(p, reinterpret_cast<float*>(box), lane, row0, col0, v);
                 } else if (row < p.m) {
                     if (p.ws) {
                         float* dst = p.ws + (int64_t)split * p.m * p.n + row * p.n + col0;
@@ -417,9 +430,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
     }
 }
 
-template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false, bool SPLIT_C = false>
+template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false, bool SPLIT_C = false, int EB = 1>
 int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X3Planes* x3 = nullptr) {
-    using G = Geo2<TIn, BN>;
+    using G = Geo2<TIn, BN, EB>;
     const bool bf16 = sizeof(TIn) == 2;
     CUtensorMap ta, tb, tc, ta2, tc2;
     if constexpr (X3) {
@@ -516,7 +529,7 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    RT_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3, SPLIT_C>, ta, tb, tc, ta2, tc2, p));
+    RT_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3, SPLIT_C, EB>, ta, tb, tc, ta2, tc2, p));
     count_launch(ctx);
     if (splits > 1) return launch_splitk_reduce(ctx, gr, st);
     return RT_OK;
@@ -524,24 +537,37 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X
 
 // The forward (NN) layout with a low-order output plane has its own
 // instantiation (SPLIT_C), so the other kernels carry none of its epilogue.
-template <int BN>
+template <int BN, int EB = 1>
 int launch_pair_layout(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     if (g.c_lo) {
         if (g.layout != RT_NN) return fail(RT_ERR_UNSUPPORTED, "c_lo is supported for the NN layout only");
         return launch_pair_variant<__nv_bfloat16, false, true, BN, false, true>(ctx, g, st);
     }
     switch (g.layout) {
-        case RT_NN: return launch_pair_variant<__nv_bfloat16, false, true, BN>(ctx, g, st);
-        case RT_NT: return launch_pair_variant<__nv_bfloat16, false, false, BN>(ctx, g, st);
-        case RT_TN: return launch_pair_variant<__nv_bfloat16, true, true, BN>(ctx, g, st);
+        case RT_NN: return launch_pair_variant<__nv_bfloat16, false, true, BN, false, false, EB>(ctx, g, st);
+        case RT_NT: return launch_pair_variant<__nv_bfloat16, false, false, BN, false, false, EB>(ctx, g, st);
+        case RT_TN: return launch_pair_variant<__nv_bfloat16, true, true, BN, false, false, EB>(ctx, g, st);
     }
     return fail(RT_ERR_INVALID, "unknown layout");
 }
 
-template <bool A_MN, bool B_MN, int BN, typename TIn = __nv_bfloat16, bool X3 = false, bool SPLIT_C = false>
+// k blocks one output tile's k loop runs (per k slice; twice with a split A).
+int64_t tile_kblocks(const GemmDesc& g, int bk, int products) {
+    const int64_t kb = (g.k + bk - 1) / bk * products * (g.a_lo ? 2 : 1);
+    const int64_t s = g.split_k > 1 ? g.split_k : 1;
+    return (kb + s - 1) / s;
+}
+
+// A k loop this short is over before the tile's output is stored: such
+// launches take four staging boxes per epilogue warp (EB = 4, three operand
+// stages), so that output stores, not the k loop, set their pace.
+constexpr int64_t kShortKBlocks = 32;
+
+template <bool A_MN, bool B_MN, int BN, typename TIn = __nv_bfloat16, bool X3 = false, bool SPLIT_C = false,
+          int EB = 1>
 int set_attr_pair() {
-    RT_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3, SPLIT_C>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Geo2<TIn, BN>::SMEM));
+    RT_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3, SPLIT_C, EB>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Geo2<TIn, BN, EB>::SMEM));
     return RT_OK;
 }
 
@@ -559,6 +585,10 @@ int gemm_tc2_init(rt_ctx* ctx) {
     RT_TRY((set_attr_pair<false, false, 256, float, true>()));
     RT_TRY((set_attr_pair<false, true, 128, __nv_bfloat16, false, true>()));  // forward with c_lo
     RT_TRY((set_attr_pair<false, true, 256, __nv_bfloat16, false, true>()));
+    RT_TRY((set_attr_pair<false, true, 256, __nv_bfloat16, false, false, 4>()));  // short k loops
+    RT_TRY((set_attr_pair<false, false, 256, __nv_bfloat16, false, false, 4>()));
+    RT_TRY((set_attr_pair<true, true, 256, __nv_bfloat16, false, false, 4>()));
+    RT_TRY((set_attr_pair<false, false, 256, float, true, false, 4>()));
     return RT_OK;
 }
 
@@ -573,6 +603,8 @@ bool gemm_tc2_wanted(const rt_ctx* ctx, const GemmDesc& g) {
 int launch_gemm_tc2(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     const int64_t tiles256 = ((g.m + BM2 - 1) / BM2) * ((g.n + 255) / 256) * (g.split_k > 1 ? g.split_k : 1);
     if (g.n <= 128 || tiles256 * 4 < ctx->sm_count) return launch_pair_layout<128>(ctx, g, st);
+    if (!g.c_lo && ctx->short_k_ring && tile_kblocks(g, 64, 1) <= kShortKBlocks)
+        return launch_pair_layout<256, 4>(ctx, g, st);
     return launch_pair_layout<256>(ctx, g, st);
 }
 
@@ -586,6 +618,8 @@ int launch_gemm_tc2_x3(rt_ctx* ctx, const GemmDesc& g, const X3Planes& x3, cudaS
     const int64_t tiles256 = ((g.m + BM2 - 1) / BM2) * ((g.n + 255) / 256) * (g.split_k > 1 ? g.split_k : 1);
     if (g.n <= 128 || tiles256 * 4 < ctx->sm_count)
         return launch_pair_variant<float, false, false, 128, true>(ctx, g, st, &x3);
+    if (ctx->short_k_ring && tile_kblocks(g, 32, 3) <= kShortKBlocks)
+        return launch_pair_variant<float, false, false, 256, true, false, 4>(ctx, g, st, &x3);
     return launch_pair_variant<float, false, false, 256, true>(ctx, g, st, &x3);
 }
 

@@ -56,6 +56,7 @@ struct rt_ctx {
     bool pair_gemm = true;  // two-CTA tcgen05 tiles where the problem is large enough
     bool f32_tensor = true;  // f32 GEMMs on the tensor cores (3xTF32) when fast_gemm is on
     bool tma_store = true;   // tensor-core GEMM epilogues store C through shared memory and TMA
+    bool short_k_ring = true;  // short-k pair GEMMs stage output chunks in a 4-box ring per warp
     int skinny_k_max = -1;   // narrow-K GEMMs (n > 16) deeper than this go to the tensor cores; -1: by size
     // Grow-only workspace for the hi/lo operand copies of 3xTF32 GEMMs that
     // bring none of their own.  A replaced buffer is kept until the context

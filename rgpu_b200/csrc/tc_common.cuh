@@ -108,6 +108,16 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t sr
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until the shared-memory sources of this thread's bulk stores are read.
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// ... all but the `pending` most recent bulk groups of this thread (0, 1, 3 or
+// 7: the staging rings below hold 1, 2, 4 or 8 slots).
+__device__ __forceinline__ void bulk_wait_read_upto(int pending) {
+    switch (pending) {
+        case 1: asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); break;
+        case 3: asm volatile("cp.async.bulk.wait_group.read 3;" ::: "memory"); break;
+        case 7: asm volatile("cp.async.bulk.wait_group.read 7;" ::: "memory"); break;
+        default: asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); break;
+    }
+}
 // Wait until this thread's bulk stores are complete.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // Make this thread's generic-proxy shared-memory writes visible to the async proxy (TMA).
@@ -403,6 +413,52 @@ __device__ __forceinline__ void stage_and_store(const CUtensorMap* tmap_c, uint8
         else
             tma_store_3d(tmap_c, smem_u32(box), (int32_t)col0, (int32_t)row0, split);
         bulk_commit();
+    }
+}
+
+// A warp's staging boxes as a ring of slots: a 32 x 32 chunk takes 4 KB as
+// f32 and 2 KB as bf16, so `boxes` 4 KB boxes hold boxes (f32) or 2 * boxes
+// (bf16) slots.  seq counts the warp's chunks; a chunk waits only until the
+// store that last used its slot (nslots chunks back) has read it, so up to
+// nslots stores are in flight per warp.  split >= 0 stores into slice
+// `split` of the split-K workspace (3-D map).
+template <typename TOut>
+__device__ __forceinline__ void stage_and_store_ring(const CUtensorMap* tmap_c, uint8_t* boxes, int nboxes, int lane,
+                                                     int64_t row0, int64_t col0, const float (&v)[32],
+                                                     uint32_t& seq, int split = -1) {
+    constexpr int slot_bytes = 32 * 32 * (int)sizeof(TOut);
+    const int nslots = nboxes * (kStageBytes / slot_bytes);
+    uint8_t* box = boxes + (int)(seq % (uint32_t)nslots) * slot_bytes;
+    if (lane == 0) bulk_wait_read_upto(nslots - 1);
+    __syncwarp();
+    stage_row<TOut>(box, lane, v);
+    fence_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+        if (split < 0)
+            tma_store_2d(tmap_c, smem_u32(box), (int32_t)col0, (int32_t)row0);
+        else
+            tma_store_3d(tmap_c, smem_u32(box), (int32_t)col0, (int32_t)row0, split);
+        bulk_commit();
+    }
+    ++seq;
+}
+
+// ReLU mask of one row's 32 bf16 columns, loaded ahead of the accumulator
+// (the caller issues these loads before its TMEM load, so both latencies
+// overlap), then applied: v *= 1[mask > 0].
+__device__ __forceinline__ void load_mask_bf16(const TcParams& p, int64_t row, int64_t col0, uint4 (&mk)[4]) {
+    const uint4* src =
+        reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.mask) + row * p.ldmask + col0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) mk[q] = src[q];
+}
+__device__ __forceinline__ void apply_mask_bf16(float (&v)[32], const uint4 (&mk)[4]) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&mk[q]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[q * 8 + j] = v[q * 8 + j] * (__bfloat162float(h[j]) > 0.0f ? 1.0f : 0.0f);
     }
 }
 
