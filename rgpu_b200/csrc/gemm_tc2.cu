@@ -105,10 +105,7 @@ __device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t adesc, uin
     }
 }
 
-// EB: 4 KB staging boxes per epilogue warp.  Launches with a short k loop
-// take EB = 4 (more output stores in flight per warp, which is what bounds a
-// small-k GEMM) and give up three stages of the operand ring for them.
-template <typename TIn, int BN, int EB = 1>
+template <typename TIn, int BN>
 struct Geo2 {
     static constexpr int ES = sizeof(TIn);
     static constexpr int BK = 128 / ES;
@@ -118,22 +115,21 @@ struct Geo2 {
     static constexpr int A_BYTES = 128 * 128;
     static constexpr int B_BYTES = BNH * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (192 * 1024 - (EB - 1) * kEpiWarps * kStageBytes) / STAGE_BYTES;
+    static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int EPI_BYTES = EB * kEpiWarps * kStageBytes;
-    static_assert(STAGES >= 2, "operand ring too short");
+    static constexpr int EPI_BYTES = kEpiWarps * kStageBytes;
     static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
 };
 
 // Split bf16 A (p.split_a) and a bf16 output's low-order plane (p.c_lo): as
 // in the one-CTA kernel, through tmap_a2 and tmap_c2.
-template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false, bool SPLIT_C = false, int EB = 1>
+template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false, bool SPLIT_C = false>
 __global__ void __launch_bounds__(kThreads2, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CUtensorMap tmap_a2,
                     const __grid_constant__ CUtensorMap tmap_c2, TcParams p) {
     static_assert(!X3 || (sizeof(TIn) == 4 && !A_MN && !B_MN), "3xTF32 planes are f32 and K-major");
-    using G = Geo2<TIn, BN, EB>;
+    using G = Geo2<TIn, BN>;
     constexpr bool kTF32 = sizeof(TIn) == 4;
     constexpr int STAGES = G::STAGES;
     constexpr uint32_t IDESC = make_idesc(kTF32, A_MN, B_MN, BN, BM2);
@@ -197,6 +193,13 @@ __global__ void __launch_bounds__(kThreads2, 1)
     };
 
     const int total_tiles = p.tiles_m * p.tiles_n * p.splits;
+
+    // Programmatic dependent launch (PDL_* in internal.h).  The set-up above
+    // touched no global memory.  Dependents may launch once this CTA is past
+    // its own wait: right away unless the epilogue waits, then from the
+    // epilogue warps after their wait (and from every other thread at its end).
+    if (p.pdl == PDL_WAIT_START) pdl_wait();
+    if (p.pdl != PDL_WAIT_EPILOGUE) pdl_launch_dependents();
 
     if (warp == 0 && lane == 0) {
         // ------------------------------------------------ TMA producer (both CTAs)
@@ -320,6 +323,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
         mbar_wait(smem_u32(drain), 0, abort_flag);
     } else if (warp >= 4) {
         // ------------------------------------------------ epilogue (both CTAs)
+        if (p.pdl == PDL_WAIT_EPILOGUE) {
+            pdl_wait();  // the kernel before this one has finished reading what the epilogue writes
+            pdl_launch_dependents();
+        }
         const int ew = (warp - 4) & 3;        // TMEM lane quadrant
         const int half = (warp - 4) >> 2;     // column half of the tile
         int acc = 0;
@@ -349,10 +356,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
                 uint4 mk[4];
                 if (pre_mask) load_mask_bf16(p, row, col0, mk);
                 tmem_ld_32x32(tbase + (uint32_t)c, v);
-                uint8_t* box = smem_epi + (warp - 4) * EB * kStageBytes;  // this warp's boxes
+                uint8_t* box = smem_epi + (warp - 4) * kStageBytes;  // this warp's staging box
                 if (p.tma_store == 2) {
                     // staged split-K partials: slice `split` of the [splits][m][n] workspace
-                    stage_and_store_ring<float>(&tmap_c, box, EB, lane, row0, col0, v, store_seq, split);
+                    stage_and_store_ring<float>(&tmap_c, box, 1, lane, row0, col0, v, store_seq, split);
                 } else if (p.tma_store == 1) {
                     // staged: coalesced TMA stores of the warp's 32 x 32 chunk
                     if (p.out_bf16) {
@@ -363,10 +370,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
                         if constexpr (SPLIT_C)
                             stage_and_store_split(&tmap_c, &tmap_c2, box, lane, row0, col0, v);
                         else
-                            stage_and_store_ring<__nv_bfloat16>(&tmap_c, box, EB, lane, row0, col0, v, store_seq);
+                            stage_and_store_ring<__nv_bfloat16>(&tmap_c, box, 1, lane, row0, col0, v, store_seq);
                     } else {
                         if (row < p.m) epilogue_math<float>(p, row, col0, v);
-                        stage_and_store_ring<float>(&tmap_c, box, EB, lane, row0, col0, v, store_seq);
+                        stage_and_store_ring<float>(&tmap_c, box, 1, lane, row0, col0, v, store_seq);
                     }
                 } else if (p.tma_store == 4) {
                     // rows scattered to their owners' receive buffers (peer memory)
@@ -410,6 +417,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
     }
 
     __syncwarp();
+    if (p.pdl == PDL_WAIT_EPILOGUE && warp < 4) {
+        pdl_wait();
+        pdl_launch_dependents();
+    }
     __syncthreads();
     if (*abort_flag && rank == 0 && threadIdx.x == 0) {
         // Both CTAs' TMA loads complete on the leader's barriers: wait for the
@@ -430,9 +441,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
     }
 }
 
-template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false, bool SPLIT_C = false, int EB = 1>
+template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false, bool SPLIT_C = false>
 int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X3Planes* x3 = nullptr) {
-    using G = Geo2<TIn, BN, EB>;
+    using G = Geo2<TIn, BN>;
     const bool bf16 = sizeof(TIn) == 2;
     CUtensorMap ta, tb, tc, ta2, tc2;
     if constexpr (X3) {
@@ -495,6 +506,8 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X
     p.opt = g.opt;
     p.tma_store = 0;
     p.p2p = g.p2p;
+    // the 3xTF32 planes come from the split kernel launched just before
+    p.pdl = X3 && g.pdl != PDL_NONE ? PDL_WAIT_START : g.pdl;
     tc = ta;  // unused unless a staged store is chosen
     tc2 = ta;
     if (g.p2p.world > 0) {
@@ -522,14 +535,21 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X
     cfg.blockDim = dim3(kThreads2, 1, 1);
     cfg.dynamicSmemBytes = G::SMEM;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    RT_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3, SPLIT_C, EB>, ta, tb, tc, ta2, tc2, p));
+    if (p.pdl != PDL_NONE && ctx->pdl) {
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.numAttrs = 2;
+    } else {
+        p.pdl = PDL_NONE;  // an ordinary launch: nothing to wait for
+    }
+    RT_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3, SPLIT_C>, ta, tb, tc, ta2, tc2, p));
     count_launch(ctx);
     if (splits > 1) return launch_splitk_reduce(ctx, gr, st);
     return RT_OK;
@@ -537,37 +557,25 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X
 
 // The forward (NN) layout with a low-order output plane has its own
 // instantiation (SPLIT_C), so the other kernels carry none of its epilogue.
-template <int BN, int EB = 1>
+template <int BN>
 int launch_pair_layout(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     if (g.c_lo) {
         if (g.layout != RT_NN) return fail(RT_ERR_UNSUPPORTED, "c_lo is supported for the NN layout only");
         return launch_pair_variant<__nv_bfloat16, false, true, BN, false, true>(ctx, g, st);
     }
     switch (g.layout) {
-        case RT_NN: return launch_pair_variant<__nv_bfloat16, false, true, BN, false, false, EB>(ctx, g, st);
-        case RT_NT: return launch_pair_variant<__nv_bfloat16, false, false, BN, false, false, EB>(ctx, g, st);
-        case RT_TN: return launch_pair_variant<__nv_bfloat16, true, true, BN, false, false, EB>(ctx, g, st);
+        case RT_NN: return launch_pair_variant<__nv_bfloat16, false, true, BN>(ctx, g, st);
+        case RT_NT: return launch_pair_variant<__nv_bfloat16, false, false, BN>(ctx, g, st);
+        case RT_TN: return launch_pair_variant<__nv_bfloat16, true, true, BN>(ctx, g, st);
     }
     return fail(RT_ERR_INVALID, "unknown layout");
 }
 
-// k blocks one output tile's k loop runs (per k slice; twice with a split A).
-int64_t tile_kblocks(const GemmDesc& g, int bk, int products) {
-    const int64_t kb = (g.k + bk - 1) / bk * products * (g.a_lo ? 2 : 1);
-    const int64_t s = g.split_k > 1 ? g.split_k : 1;
-    return (kb + s - 1) / s;
-}
 
-// A k loop this short is over before the tile's output is stored: such
-// launches take four staging boxes per epilogue warp (EB = 4, three operand
-// stages), so that output stores, not the k loop, set their pace.
-constexpr int64_t kShortKBlocks = 32;
-
-template <bool A_MN, bool B_MN, int BN, typename TIn = __nv_bfloat16, bool X3 = false, bool SPLIT_C = false,
-          int EB = 1>
+template <bool A_MN, bool B_MN, int BN, typename TIn = __nv_bfloat16, bool X3 = false, bool SPLIT_C = false>
 int set_attr_pair() {
-    RT_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3, SPLIT_C, EB>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Geo2<TIn, BN, EB>::SMEM));
+    RT_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3, SPLIT_C>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Geo2<TIn, BN>::SMEM));
     return RT_OK;
 }
 
@@ -585,10 +593,6 @@ int gemm_tc2_init(rt_ctx* ctx) {
     RT_TRY((set_attr_pair<false, false, 256, float, true>()));
     RT_TRY((set_attr_pair<false, true, 128, __nv_bfloat16, false, true>()));  // forward with c_lo
     RT_TRY((set_attr_pair<false, true, 256, __nv_bfloat16, false, true>()));
-    RT_TRY((set_attr_pair<false, true, 256, __nv_bfloat16, false, false, 4>()));  // short k loops
-    RT_TRY((set_attr_pair<false, false, 256, __nv_bfloat16, false, false, 4>()));
-    RT_TRY((set_attr_pair<true, true, 256, __nv_bfloat16, false, false, 4>()));
-    RT_TRY((set_attr_pair<false, false, 256, float, true, false, 4>()));
     return RT_OK;
 }
 
@@ -603,8 +607,6 @@ bool gemm_tc2_wanted(const rt_ctx* ctx, const GemmDesc& g) {
 int launch_gemm_tc2(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     const int64_t tiles256 = ((g.m + BM2 - 1) / BM2) * ((g.n + 255) / 256) * (g.split_k > 1 ? g.split_k : 1);
     if (g.n <= 128 || tiles256 * 4 < ctx->sm_count) return launch_pair_layout<128>(ctx, g, st);
-    if (!g.c_lo && ctx->short_k_ring && tile_kblocks(g, 64, 1) <= kShortKBlocks)
-        return launch_pair_layout<256, 4>(ctx, g, st);
     return launch_pair_layout<256>(ctx, g, st);
 }
 
@@ -618,8 +620,6 @@ int launch_gemm_tc2_x3(rt_ctx* ctx, const GemmDesc& g, const X3Planes& x3, cudaS
     const int64_t tiles256 = ((g.m + BM2 - 1) / BM2) * ((g.n + 255) / 256) * (g.split_k > 1 ? g.split_k : 1);
     if (g.n <= 128 || tiles256 * 4 < ctx->sm_count)
         return launch_pair_variant<float, false, false, 128, true>(ctx, g, st, &x3);
-    if (ctx->short_k_ring && tile_kblocks(g, 32, 3) <= kShortKBlocks)
-        return launch_pair_variant<float, false, false, 256, true, false, 4>(ctx, g, st, &x3);
     return launch_pair_variant<float, false, false, 256, true>(ctx, g, st, &x3);
 }
 

@@ -56,7 +56,7 @@ struct rt_ctx {
     bool pair_gemm = true;  // two-CTA tcgen05 tiles where the problem is large enough
     bool f32_tensor = true;  // f32 GEMMs on the tensor cores (3xTF32) when fast_gemm is on
     bool tma_store = true;   // tensor-core GEMM epilogues store C through shared memory and TMA
-    bool short_k_ring = true;  // short-k pair GEMMs stage output chunks in a 4-box ring per warp
+    bool pdl = true;  // plan GEMMs may launch as programmatic dependents (GemmDesc::pdl)
     int skinny_k_max = -1;   // narrow-K GEMMs (n > 16) deeper than this go to the tensor cores; -1: by size
     // Grow-only workspace for the hi/lo operand copies of 3xTF32 GEMMs that
     // bring none of their own.  A replaced buffer is kept until the context
@@ -122,7 +122,28 @@ struct GemmDesc {
     // stored as bf16(v) in c plus bf16(v - bf16(v)) in c_lo.
     const void* a_lo;
     void* c_lo;
+    // Programmatic dependent launch of a pair-kernel GEMM on its stream
+    // (PDL_NONE: an ordinary launch).  The plan sets it from what the GEMM
+    // reads and writes relative to the kernel launched just before it.
+    int pdl;
 };
+
+// How a GEMM launched as a programmatic dependent of the previous kernel on
+// its stream waits for it (griddepcontrol.wait, which returns once that grid
+// has completed and its writes are visible):
+//   PDL_NONE          ordinary launch
+//   PDL_WAIT_START    reads the previous kernel's output: every thread waits
+//                     before its first global access
+//   PDL_WAIT_EPILOGUE the previous kernel reads what this one writes (a dW
+//                     GEMM with the update fused, after the dX GEMM that reads
+//                     the same weights): the k loop runs at once, the epilogue
+//                     waits before its first global access
+//   PDL_NO_WAIT       touches nothing the previous kernel writes or reads
+//                     while it runs, and what it reads was complete when that
+//                     kernel passed its own wait
+// A kernel lets its dependents launch only once it has passed its own wait,
+// so "complete before the previous kernel's wait" carries down the chain.
+enum { PDL_NONE = 0, PDL_WAIT_START = 1, PDL_WAIT_EPILOGUE = 2, PDL_NO_WAIT = 3 };
 
 // Peer memory of a communicator's ranks (comm.cu).
 int comm_share_buffer(rt_comm* comm, void* local, void** peers);

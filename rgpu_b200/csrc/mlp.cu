@@ -373,6 +373,7 @@ struct Enqueuer {
             }
             g.x3_ws = m->x3_ws;
             g.x3_ws_bytes = m->x3_ws_bytes;
+            g.pdl = PDL_WAIT_START;  // reads the previous layer's activations
             RT_TRY(run_gemm(m->ctx, g, st, 0));
             // FLOPs are the algorithmic 2 n d u; a split-A GEMM runs twice that on the tensor cores
             const char* label = last ? "fwd_gemm_bias" : g.a_lo ? "fwd_gemm_bias_relu_split" : "fwd_gemm_bias_relu";
@@ -382,9 +383,10 @@ struct Enqueuer {
     }
 
     // [dW_l; db_l] rows [r0, r1) = ([A_{l-1}, 1] columns r0..r1)^T delta_l (TN, K = batch), f32.
-    int dw_gemm_rows(PlanLayer& P, int l, int64_t r0, int64_t r1) {
+    int dw_gemm_rows(PlanLayer& P, int l, int64_t r0, int64_t r1, int pdl) {
         const int64_t rows = P.d + 1;
         GemmDesc g = dw_desc(P, l, r0, r1);
+        g.pdl = pdl;
         if (P.p2p) {
             // weight rows go to their owners' receive buffers, the bias row to g
             const int64_t e = shard_end(P, r1);
@@ -554,10 +556,11 @@ struct Enqueuer {
     }
 
     // delta_{l-1} = (delta_l W_l^T) * 1[A_{l-1} > 0]  (NT, fused mask)
-    int dx_gemm(int l) {
+    int dx_gemm(int l, int pdl) {
         PlanLayer& P = m->L[l];
         PlanLayer& Q = m->L[l - 1];
         GemmDesc h{};
+        h.pdl = pdl;
         h.layout = RT_NT;
         h.in_dtype = m->adt;
         h.out_dtype = m->adt;
@@ -595,11 +598,20 @@ struct Enqueuer {
         RT_TRY(launch_xent(m->ctx, (const float*)Last.act, Last.ld, m->slot[s].labels, m->n, Last.u,
                            (float)(1.0 / gb), Last.delta, m->adt, Last.ld, m->loss_rows, st));
         RT_TRY(mark("softmax_xent", 0));
+        // Launch order per layer, top down: dX_l, then dW_l.  dX_l reads delta_l
+        // (complete once the dW GEMM before it has passed its epilogue wait; after
+        // softmax-CE it waits at its start) and W_l, which no running GEMM
+        // writes.  dW_l's epilogue overwrites W_l, which dX_l reads: its k loop
+        // starts at once, its epilogue waits for dX_l (the first layer's dW has
+        // no dX before it and overwrites nothing the GEMM before it reads).
         for (int l = nl - 1; l >= 0; --l) {
             PlanLayer& P = m->L[l];
-            if (l > 0) RT_TRY(dx_gemm(l));
+            if (l > 0) RT_TRY(dx_gemm(l, l == nl - 1 ? PDL_WAIT_START : PDL_NO_WAIT));
             for (int c = 0; c < P.chunks; ++c)
-                RT_TRY(dw_gemm_rows(P, l, chunk_row_of(P.d + 1, P.chunks, c), chunk_row_of(P.d + 1, P.chunks, c + 1)));
+                RT_TRY(dw_gemm_rows(P, l, chunk_row_of(P.d + 1, P.chunks, c), chunk_row_of(P.d + 1, P.chunks, c + 1),
+                                    c == 0 && l > 0 ? PDL_WAIT_EPILOGUE
+                                    : c == 0 && l == nl - 1 ? PDL_WAIT_START
+                                                            : PDL_NO_WAIT));
         }
         return RT_OK;
     }
@@ -633,7 +645,10 @@ struct Enqueuer {
             const int64_t rows = P.d + 1;
             for (int c = 0; c < P.chunks; ++c) {
                 const int64_t r0 = chunk_row_of(rows, P.chunks, c), r1 = chunk_row_of(rows, P.chunks, c + 1);
-                RT_TRY(dw_gemm_rows(P, l, r0, r1));
+                // chunk 0 reads delta_l, which the GEMM launched just before it
+                // (dX_{l+1}, or softmax-CE) writes; the other chunks read only
+                // what was complete when chunk 0 passed its wait
+                RT_TRY(dw_gemm_rows(P, l, r0, r1, c == 0 ? PDL_WAIT_START : PDL_NO_WAIT));
                 RT_CUDA(cudaEventRecord(P.ev_ready[c], st));
                 if (m->comm) {
                     RT_CUDA(cudaStreamWaitEvent(m->comm_stream, P.ev_ready[c], 0));
@@ -654,7 +669,9 @@ struct Enqueuer {
             // until the previous layer's dX GEMM and updates were done.
             if (l + 1 < nl && !m->ag_stream) RT_TRY(gather_layer(m->L[l + 1]));
             if (l > 0) {
-                RT_TRY(dx_gemm(l));
+                // delta_l was complete when this layer's chunk 0 passed its wait,
+                // and no running GEMM writes W_l or the mask
+                RT_TRY(dx_gemm(l, PDL_NO_WAIT));
                 if (update) {
                     RT_CUDA(cudaEventRecord(P.ev_dx, st));
                     RT_CUDA(cudaStreamWaitEvent(m->opt_stream, P.ev_dx, 0));

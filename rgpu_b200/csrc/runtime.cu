@@ -98,8 +98,8 @@ int rt_ctx_create(int device, rt_ctx** out) {
     c->f32_tensor = !(f32_env && f32_env[0] == '0');
     const char* st_env = getenv("RTGPU_TMA_STORE");
     c->tma_store = !(st_env && st_env[0] == '0');
-    const char* ring_env = getenv("RTGPU_SHORT_K_RING");
-    c->short_k_ring = !(ring_env && ring_env[0] == '0');
+    const char* pdl_env = getenv("RTGPU_PDL");
+    c->pdl = !(pdl_env && pdl_env[0] == '0');
     // RTGPU_SKINNY_K_MAX=<k>: narrow-K GEMMs deeper than k go to the tensor
     // cores (default: chosen by dtype and size, see narrow_k_on_tensor_cores)
     const char* sk_env = getenv("RTGPU_SKINNY_K_MAX");

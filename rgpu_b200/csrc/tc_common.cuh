@@ -218,6 +218,7 @@ struct TcParams {
     // plane (tmap_a2) and A itself at each k block; B is the same for both.
     int split_a;
     void* c_lo;  // bf16 output's low-order plane (same ldc): bf16(v - bf16(v)); null = none
+    int pdl;  // PDL_* (internal.h): how this launch waits for the kernel before it
 };
 
 // Epilogue staging: one 32 x 32 output chunk per epilogue warp (4 KB), the
@@ -252,6 +253,12 @@ __device__ __forceinline__ void tile_coords(const TcParams& p, int t, int& split
     mb = first + in % rows;
     nb = in / rows;
 }
+
+// Programmatic dependent launch (PTX griddepcontrol): wait until the grid
+// this one depends on has completed and its writes are visible; let the
+// grids that depend on this one launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ void record_error(int* err, int code, int detail) {
     if (atomicCAS(err, 0, code) == 0) err[1] = detail;
@@ -416,12 +423,12 @@ __device__ __forceinline__ void stage_and_store(const CUtensorMap* tmap_c, uint8
     }
 }
 
-// A warp's staging boxes as a ring of slots: a 32 x 32 chunk takes 4 KB as
-// f32 and 2 KB as bf16, so `boxes` 4 KB boxes hold boxes (f32) or 2 * boxes
-// (bf16) slots.  seq counts the warp's chunks; a chunk waits only until the
-// store that last used its slot (nslots chunks back) has read it, so up to
-// nslots stores are in flight per warp.  split >= 0 stores into slice
-// `split` of the split-K workspace (3-D map).
+// A warp's staging box(es) as a ring of slots: a 32 x 32 chunk takes 4 KB as
+// f32 and 2 KB as bf16, so each 4 KB box holds one f32 or two bf16 slots.
+// seq counts the warp's chunks; a chunk waits only until the store that last
+// used its slot (nslots chunks back) has read it, so consecutive bf16 chunks
+// alternate halves of the box.  split >= 0 stores into slice `split` of the
+// split-K workspace (3-D map).
 template <typename TOut>
 __device__ __forceinline__ void stage_and_store_ring(const CUtensorMap* tmap_c, uint8_t* boxes, int nboxes, int lane,
                                                      int64_t row0, int64_t col0, const float (&v)[32],

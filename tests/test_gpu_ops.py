@@ -503,66 +503,3 @@ def test_few_row_gemms(gpu, m, n, k):
         ref = _skinny_ref((hi.astype(np.float64) + lo), w, G.RT_EPI_BIAS_RELU, bias, None)
         got = gpu.download(chi).astype(np.float64) + gpu.download(clo)
         assert rel_l2(got, ref) <= 1e-5, f"split {m}x{n}x{k}: {rel_l2(got, ref):.2e}"
-
-
-@pytest.mark.parametrize("dtype", ["bf16", "f32"])
-@pytest.mark.parametrize("k,split", [(256, 1), (1000, 1), (2048, 2), (19, 1)])
-def test_short_k_staging_ring_is_bit_identical(gpu, dtype, k, split):
-    # Pair GEMMs with a short k loop (<= 32 k blocks per tile, 256-wide tiles)
-    # stage their output chunks in a ring of four boxes per epilogue warp
-    # (three operand stages instead of six).  Only where the chunks wait
-    # changes, so every layout, f32 partials of a k split, and the bf16
-    # outputs with the ReLU-mask and bias epilogues must equal, bit for bit,
-    # the same GEMMs on a context with the ring off (RTGPU_SHORT_K_RING=0),
-    # and both must track the exact product.
-    import os
-
-    m, n = 2048, 2304
-    rng = np.random.default_rng(k + split)
-    a = rng.standard_normal((m, k)).astype(np.float32)
-    b = rng.standard_normal((k, n)).astype(np.float32)
-    mask = rng.standard_normal((m, n)).astype(np.float32)
-    bias = rng.standard_normal((1, n)).astype(np.float32)
-    os.environ["RTGPU_SHORT_K_RING"] = "0"
-    try:
-        plain = rgpu_b200.Gpu(0)
-    finally:
-        del os.environ["RTGPU_SHORT_K_RING"]
-    try:
-        outs = []
-        for g in (gpu, plain):
-            ga, gb = g.upload(a, dtype), g.upload(b, dtype)
-            gat, gbt = g.upload(np.ascontiguousarray(a.T), dtype), g.upload(np.ascontiguousarray(b.T), dtype)
-            gmask, gbias = g.upload(mask, "bf16"), g.upload(bias)
-            res = []
-            for layout, x, y in ((G.RT_NN, ga, gb), (G.RT_TN, gat, gb), (G.RT_NT, ga, gbt)):
-                c = g.zeros((m, n))
-                args = G.GemmArgs(layout, G.RT_BF16 if dtype == "bf16" else G.RT_F32, G.RT_F32, m, n, k,
-                                  x.ptr, x.ld, y.ptr, y.ld, c.ptr, c.ld, G.RT_EPI_NONE, None, None, 0, split, None, 0)
-                ws = None
-                if split > 1:
-                    ws = g.zeros((split * m, n))
-                    args.workspace, args.workspace_bytes = ws.ptr, split * m * n * 4
-                g.gemm(args)
-                res.append(g.download(c))
-            if dtype == "bf16":
-                for epi, bptr, mptr in ((G.RT_EPI_RELU_MASK, None, gmask.ptr), (G.RT_EPI_BIAS_RELU, gbias.ptr, None)):
-                    c16 = g.zeros((m, n), "bf16")
-                    args = G.GemmArgs(G.RT_NT, G.RT_BF16, G.RT_BF16, m, n, k, ga.ptr, ga.ld, gbt.ptr, gbt.ld,
-                                      c16.ptr, c16.ld, epi, bptr, mptr, gmask.ld if mptr else 0, 1, None, 0)
-                    g.gemm(args)
-                    res.append(g.download(c16))
-            g.sync()
-            outs.append(res)
-        for i, (r_ring, r_plain) in enumerate(zip(*outs)):
-            assert np.array_equal(r_ring, r_plain), f"output {i} differs with the staging ring"
-        if dtype == "bf16":
-            qa = rgpu_b200.bf16_to_f32(rgpu_b200.f32_to_bf16(a)).astype(np.float64)
-            qb = rgpu_b200.bf16_to_f32(rgpu_b200.f32_to_bf16(b)).astype(np.float64)
-        else:
-            qa, qb = a.astype(np.float64), b.astype(np.float64)
-        ref = qa @ qb
-        for i in range(3):
-            assert rel_l2(outs[0][i], ref) <= 1e-5, f"layout {i}: {rel_l2(outs[0][i], ref):.2e}"
-    finally:
-        plain.close()
