@@ -50,6 +50,8 @@ template <typename TD, int VPL>
 __global__ void xent_reg_kernel(const float* __restrict__ logits, int64_t ldz, const uint32_t* __restrict__ labels,
                                 int64_t n, int64_t C, float scale, TD* __restrict__ delta, int64_t ldd,
                                 float* __restrict__ loss) {
+    pdl_wait();  // programmatic dependent launch: the kernel before this one is done
+    pdl_launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
     if (r >= n) return;
@@ -91,6 +93,8 @@ template <typename TD>
 __global__ void xent_kernel(const float* __restrict__ logits, int64_t ldz, const uint32_t* __restrict__ labels,
                             int64_t n, int64_t C, float scale, TD* __restrict__ delta, int64_t ldd,
                             float* __restrict__ loss) {
+    pdl_wait();  // programmatic dependent launch: the kernel before this one is done
+    pdl_launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
     if (r >= n) return;
@@ -216,6 +220,8 @@ __global__ void opt_scalars_at_kernel(OptScalars* s, int t, float beta1, float b
 }
 
 __global__ void opt_step_begin_kernel(OptScalars* s, float beta1, float beta2) {
+    pdl_wait();  // programmatic dependent launch: the kernel before this one is done
+    pdl_launch_dependents();
     int t = s->t + 1;
     s->t = t;
     float c1 = __fsub_rn(1.0f, powi_f32(beta1, t));
@@ -398,19 +404,20 @@ int launch_xent(rt_ctx* ctx, const float* logits, int64_t ldz, const uint32_t* l
                 float scale, void* delta, rt_dtype ddt, int64_t ldd, float* loss_rows, cudaStream_t st) {
     if (n == 0) return RT_OK;
     unsigned blocks = (unsigned)((n + 7) / 8);
+    const bool pdl = ctx->plan_pdl;
     if (classes <= 32 * 32) {
         if (ddt == RT_BF16)
-            xent_reg_kernel<__nv_bfloat16, 32><<<blocks, 256, 0, st>>>(logits, ldz, labels, n, classes, scale,
-                                                                        (__nv_bfloat16*)delta, ldd, loss_rows);
+            RT_CUDA(launch_k(pdl, xent_reg_kernel<__nv_bfloat16, 32>, dim3(blocks), dim3(256), 0, st, logits, ldz, labels,
+                             n, classes, scale, (__nv_bfloat16*)delta, ldd, loss_rows));
         else
-            xent_reg_kernel<float, 32><<<blocks, 256, 0, st>>>(logits, ldz, labels, n, classes, scale, (float*)delta,
-                                                                ldd, loss_rows);
+            RT_CUDA(launch_k(pdl, xent_reg_kernel<float, 32>, dim3(blocks), dim3(256), 0, st, logits, ldz, labels, n,
+                             classes, scale, (float*)delta, ldd, loss_rows));
     } else if (ddt == RT_BF16) {
-        xent_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(logits, ldz, labels, n, classes, scale,
-                                                            (__nv_bfloat16*)delta, ldd, loss_rows);
+        RT_CUDA(launch_k(pdl, xent_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, st, logits, ldz, labels, n, classes,
+                         scale, (__nv_bfloat16*)delta, ldd, loss_rows));
     } else {
-        xent_kernel<float><<<blocks, 256, 0, st>>>(logits, ldz, labels, n, classes, scale, (float*)delta, ldd,
-                                                    loss_rows);
+        RT_CUDA(launch_k(pdl, xent_kernel<float>, dim3(blocks), dim3(256), 0, st, logits, ldz, labels, n, classes, scale,
+                         (float*)delta, ldd, loss_rows));
     }
     count_launch(ctx);
     RT_CUDA(cudaGetLastError());
@@ -584,7 +591,7 @@ int launch_fill_column(rt_ctx* ctx, void* p, rt_dtype dt, int64_t rows, int64_t 
 }
 
 int launch_opt_step_begin(rt_ctx* ctx, OptScalars* s, float beta1, float beta2, cudaStream_t st) {
-    opt_step_begin_kernel<<<1, 1, 0, st>>>(s, beta1, beta2);
+    RT_CUDA(launch_k(ctx->plan_pdl, opt_step_begin_kernel, dim3(1), dim3(1), 0, st, s, beta1, beta2));
     count_launch(ctx);
     RT_CUDA(cudaGetLastError());
     return RT_OK;

@@ -213,6 +213,8 @@ __global__ void __launch_bounds__(THREADS) gemm_simt_kernel(SimtParams p) {
 // Deterministic split-K reduction: slices summed in ascending order, then the
 // epilogue (splitk.rs:240-256 REDUZ, plus bias/ReLU/mask).
 __global__ void splitk_reduce_kernel(SimtParams p, int slices) {
+    pdl_wait();  // programmatic dependent launch: the kernel before this one is done
+    pdl_launch_dependents();
     int64_t total = p.m * p.n;
     for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
          idx += (int64_t)gridDim.x * blockDim.x) {
@@ -240,6 +242,8 @@ __global__ void splitk_reduce_kernel(SimtParams p, int slices) {
 // rows, the x threads walk 4-column groups, every load and store 16 bytes.
 // Slices are summed in the same fixed order.
 __global__ void splitk_reduce4_kernel(SimtParams p, int slices) {
+    pdl_wait();  // programmatic dependent launch: the kernel before this one is done
+    pdl_launch_dependents();
     const int64_t total = p.m * p.n;
     const int64_t groups = p.n / 4;
     for (int64_t i = blockIdx.y; i < p.m; i += gridDim.y) {
@@ -336,7 +340,8 @@ int launch_splitk_reduce(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream) {
         const int threads = groups >= 256 ? 256 : (int)((groups + 31) / 32 * 32);
         const int64_t gx = (groups + threads - 1) / threads;
         int64_t gy = g.m < 65535 ? g.m : 65535;
-        splitk_reduce4_kernel<<<dim3((unsigned)gx, (unsigned)gy), threads, 0, stream>>>(p, g.split_k);
+        RT_CUDA(launch_k(ctx->plan_pdl, splitk_reduce4_kernel, dim3((unsigned)gx, (unsigned)gy), dim3(threads), 0, stream, p,
+                         g.split_k));
         count_launch(ctx);
         RT_CUDA(cudaGetLastError());
         return RT_OK;
@@ -346,7 +351,7 @@ int launch_splitk_reduce(rt_ctx* ctx, const GemmDesc& g, cudaStream_t stream) {
     int64_t cap = (int64_t)ctx->sm_count * 16;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    splitk_reduce_kernel<<<(unsigned)blocks, 256, 0, stream>>>(p, g.split_k);
+    RT_CUDA(launch_k(ctx->plan_pdl, splitk_reduce_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, p, g.split_k));
     count_launch(ctx);
     RT_CUDA(cudaGetLastError());
     return RT_OK;

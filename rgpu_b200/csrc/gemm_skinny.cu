@@ -182,6 +182,8 @@ __device__ __forceinline__ float warp_sum16_scatter(float (&v)[16], int lane) {
 // MLPs (k <= 1024), so their A and B loads are a single round trip.
 template <typename TIn, bool B_KMAJOR>
 __global__ void __launch_bounds__(kThreads) skinny_n_kernel(SkinnyParams p) {
+    pdl_wait();  // programmatic dependent launch: the kernel before this one is done
+    pdl_launch_dependents();
     constexpr int U = 32, KC = 32 * U, BP = 20;  // k rows per chunk, padded row length of staged B
     extern __shared__ __align__(16) float sb_raw[];
     float(*sb)[BP] = reinterpret_cast<float(*)[BP]>(sb_raw);
@@ -258,6 +260,8 @@ __global__ void __launch_bounds__(kThreads) skinny_n_kernel(SkinnyParams p) {
 // reduction finishes them.
 template <typename TIn, int NMAX>
 __global__ void __launch_bounds__(kThreads) skinny_n_tn_kernel(SkinnyParams p) {
+    pdl_wait();  // programmatic dependent launch: the kernel before this one is done
+    pdl_launch_dependents();
     constexpr int KC = 64;  // k rows of B staged per pass
     constexpr int U = 16;
     __shared__ __align__(16) float sb[KC][NMAX];
@@ -323,6 +327,8 @@ __global__ void __launch_bounds__(kThreads) skinny_n_tn_kernel(SkinnyParams p) {
 // with 16-byte loads and stores.
 template <typename TIn, int KMAX, bool A_KMAJOR, bool B_KMAJOR>
 __global__ void __launch_bounds__(kThreads) skinny_k_kernel(SkinnyParams p) {
+    pdl_wait();  // programmatic dependent launch: the kernel before this one is done
+    pdl_launch_dependents();
     constexpr int TM = 32, TN = 4 * 64, RPT = TM / (kThreads / 64);  // rows per thread
     __shared__ __align__(16) float sa[TM][KMAX];
     const TIn* A = static_cast<const TIn*>(p.a);
@@ -441,6 +447,8 @@ __device__ __forceinline__ float2 ld2_f<__nv_bfloat16>(const __nv_bfloat16* p) {
 template <typename TIn, bool A_KM>
 __global__ void __cluster_dims__(kClusterK, 1, 1) __launch_bounds__(kThreads)
     skinny_m_kernel(SkinnyParams p) {
+    pdl_wait();  // programmatic dependent launch: the kernel before this one is done
+    pdl_launch_dependents();
     // A_KM: A is stored [k, m] (layout TN), else [m, k] (layout NN)
     // sa (A rows of the k chunk) during the k loop; red (the warps' sums)
     // after it, in the same shared memory
@@ -566,12 +574,13 @@ SkinnyParams make_params(const GemmDesc& g) {
 }
 
 template <typename TIn, int KMAX>
-void launch_narrow_k(const GemmDesc& g, const SkinnyParams& p, dim3 grid, cudaStream_t st) {
+cudaError_t launch_narrow_k(bool pdl, const GemmDesc& g, const SkinnyParams& p, dim3 grid, cudaStream_t st) {
     switch (g.layout) {
-        case RT_NN: skinny_k_kernel<TIn, KMAX, true, false><<<grid, kThreads, 0, st>>>(p); break;
-        case RT_NT: skinny_k_kernel<TIn, KMAX, true, true><<<grid, kThreads, 0, st>>>(p); break;
-        case RT_TN: skinny_k_kernel<TIn, KMAX, false, false><<<grid, kThreads, 0, st>>>(p); break;
+        case RT_NN: return launch_k(pdl, skinny_k_kernel<TIn, KMAX, true, false>, grid, dim3(kThreads), 0, st, p);
+        case RT_NT: return launch_k(pdl, skinny_k_kernel<TIn, KMAX, true, true>, grid, dim3(kThreads), 0, st, p);
+        case RT_TN: return launch_k(pdl, skinny_k_kernel<TIn, KMAX, false, false>, grid, dim3(kThreads), 0, st, p);
     }
+    return cudaErrorInvalidValue;
 }
 
 template <typename TIn>
@@ -580,10 +589,11 @@ int launch_typed(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     if (few_rows(g)) {
         const int64_t groups = (g.n + 63) / 64;
         if (groups * kClusterK > (int64_t)INT32_MAX) return fail(RT_ERR_INVALID, "few-row GEMM n too large");
+        const dim3 grid((unsigned)(groups * kClusterK));
         if (g.layout == RT_TN)
-            skinny_m_kernel<TIn, true><<<(unsigned)(groups * kClusterK), kThreads, 0, st>>>(p);
+            RT_CUDA(launch_k(ctx->plan_pdl, skinny_m_kernel<TIn, true>, grid, dim3(kThreads), 0, st, p));
         else
-            skinny_m_kernel<TIn, false><<<(unsigned)(groups * kClusterK), kThreads, 0, st>>>(p);
+            RT_CUDA(launch_k(ctx->plan_pdl, skinny_m_kernel<TIn, false>, grid, dim3(kThreads), 0, st, p));
         count_launch(ctx);
         RT_CUDA(cudaGetLastError());
         return RT_OK;
@@ -597,7 +607,7 @@ int launch_typed(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
             p.k_per_slice = kps;
             p.ws = slices > 1 ? g.workspace : nullptr;
             dim3 grid((unsigned)((g.m + kThreads - 1) / kThreads), (unsigned)slices);
-            skinny_n_tn_kernel<TIn, kSkinnyMax><<<grid, kThreads, 0, st>>>(p);
+            RT_CUDA(launch_k(ctx->plan_pdl, skinny_n_tn_kernel<TIn, kSkinnyMax>, grid, dim3(kThreads), 0, st, p));
             count_launch(ctx);
             RT_CUDA(cudaGetLastError());
             if (slices > 1) {
@@ -609,18 +619,20 @@ int launch_typed(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
         }
         const int64_t blocks = (g.m * 32 + kThreads - 1) / kThreads;  // one warp per row
         if (g.layout == RT_NT)
-            skinny_n_kernel<TIn, true><<<(unsigned)blocks, kThreads, kSkinnyNSmem, st>>>(p);
+            RT_CUDA(launch_k(ctx->plan_pdl, skinny_n_kernel<TIn, true>, dim3((unsigned)blocks), dim3(kThreads),
+                             kSkinnyNSmem, st, p));
         else
-            skinny_n_kernel<TIn, false><<<(unsigned)blocks, kThreads, kSkinnyNSmem, st>>>(p);
+            RT_CUDA(launch_k(ctx->plan_pdl, skinny_n_kernel<TIn, false>, dim3((unsigned)blocks), dim3(kThreads),
+                             kSkinnyNSmem, st, p));
     } else {
         dim3 grid((unsigned)((g.n + 255) / 256), (unsigned)((g.m + 31) / 32));
         if (grid.y > 65535u) return fail(RT_ERR_INVALID, "narrow-k GEMM m=%lld too large for its grid", (long long)g.m);
         if (g.k <= 4)
-            launch_narrow_k<TIn, 4>(g, p, grid, st);
+            RT_CUDA((launch_narrow_k<TIn, 4>(ctx->plan_pdl, g, p, grid, st)));
         else if (g.k <= 8)
-            launch_narrow_k<TIn, 8>(g, p, grid, st);
+            RT_CUDA((launch_narrow_k<TIn, 8>(ctx->plan_pdl, g, p, grid, st)));
         else
-            launch_narrow_k<TIn, 16>(g, p, grid, st);
+            RT_CUDA((launch_narrow_k<TIn, 16>(ctx->plan_pdl, g, p, grid, st)));
     }
     count_launch(ctx);
     RT_CUDA(cudaGetLastError());

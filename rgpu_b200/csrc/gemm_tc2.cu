@@ -57,6 +57,19 @@ __device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v
     asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 
+// Orders this thread's accesses at cluster scope (here: a ring slot's tile
+// id, written by the pair leader, read after the slot's barrier completed).
+__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+
+// Dynamic tile schedule (TcParams::tile_ctr set): the pair leader's producer
+// claims each next tile with an atomic add and publishes its id in a ring of
+// kRing slots held by both CTAs; the producer of the other CTA, the MMA issuer
+// and the epilogue warps of both CTAs read the ids in order and release each
+// slot on the leader's barrier.  A pair that starts late (its SMs still busy
+// with other kernels) then simply takes fewer tiles.
+constexpr int kRing = 12;
+constexpr int kRingConsumers = 2 * kEpiWarps + 2;  // epilogue warps of both CTAs, MMA issuer, peer producer
+
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -118,7 +131,7 @@ struct Geo2 {
     static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int EPI_BYTES = kEpiWarps * kStageBytes;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 512 /*barriers, tile ring*/;
 };
 
 // Split bf16 A (p.split_a) and a bf16 output's low-order plane (p.c_lo): as
@@ -145,9 +158,13 @@ __global__ void __launch_bounds__(kThreads2, 1)
     uint64_t* tfull = bars + 2 * STAGES;       // each CTA: accumulator ready
     uint64_t* tempty = bars + 2 * STAGES + 2;  // leader: accumulator drained by both epilogues
     uint64_t* drain = bars + 2 * STAGES + 4;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+    uint64_t* rfull = bars + 2 * STAGES + 5;            // each CTA: ring slot holds the next tile id
+    uint64_t* rempty = bars + 2 * STAGES + 5 + kRing;   // leader: ring slot read by every consumer
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5 + 2 * kRing);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     uint32_t* last_phase = tmem_slot + 2;
+    int* ring_tile = reinterpret_cast<int*>(last_phase + STAGES);
+    static_assert((2 * STAGES + 5 + 2 * kRing) * 8 + (2 + STAGES + kRing) * 4 <= 512, "barrier area");
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -167,6 +184,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
             mbar_init(smem_u32(&tempty[s]), 2 * kEpiWarps);  // epilogue warps of both CTAs
         }
         mbar_init(smem_u32(drain), 1);
+        for (int r = 0; r < kRing; ++r) {
+            mbar_init(smem_u32(&rfull[r]), 1);
+            mbar_init(smem_u32(&rempty[r]), kRingConsumers);
+        }
         *abort_flag = 0;
         fence_barrier_init();
         prefetch_tmap(&tmap_a);
@@ -193,6 +214,23 @@ __global__ void __launch_bounds__(kThreads2, 1)
     };
 
     const int total_tiles = p.tiles_m * p.tiles_n * p.splits;
+    const bool dyn = p.tile_ctr != nullptr;
+
+    // A consumer's next tile id from its CTA's ring (-1: no tiles left).  All
+    // lanes of a calling warp wait; one arrival per consumer releases the
+    // slot on the leader's barrier.  False if the wait gave up.
+    auto ring_next = [&](uint32_t& slot, uint32_t& ph, bool arrive, int& t) -> bool {
+        if (!mbar_wait(smem_u32(&rfull[slot]), ph, abort_flag)) return false;
+        fence_acq_rel_cluster();
+        t = reinterpret_cast<volatile int*>(ring_tile)[slot];
+        __syncwarp(__activemask());
+        if (arrive) mbar_arrive_cluster(mapa_shared(smem_u32(&rempty[slot]), 0));
+        if (++slot == kRing) {
+            slot = 0;
+            ph ^= 1;
+        }
+        return true;
+    };
 
     // Programmatic dependent launch (PDL_* in internal.h).  The set-up above
     // touched no global memory.  Dependents may launch once this CTA is past
@@ -206,7 +244,34 @@ __global__ void __launch_bounds__(kThreads2, 1)
         int stage = 0;
         uint32_t phase = 0;
         bool ok = true;
-        for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
+        uint32_t rs = 0, rph = 0;
+        // the leader claims one tile ahead, so the atomic's latency overlaps the current tile's loads
+        int claimed = dyn && rank == 0 ? atomicAdd(p.tile_ctr, 1) : 0;
+        for (int ts = cluster_id; ok; ts += num_clusters) {
+            int t = ts;
+            if (dyn && rank == 0) {
+                // publish the claimed tile's id to both CTAs' rings, then claim the next
+                if (!mbar_wait(smem_u32(&rempty[rs]), rph ^ 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                t = claimed < total_tiles ? claimed : -1;
+                if (t >= 0) claimed = atomicAdd(p.tile_ctr, 1);
+                ring_tile[rs] = t;
+                st_cluster_u32(mapa_shared(smem_u32(&ring_tile[rs]), 1), (uint32_t)t);
+                mbar_arrive_cluster(mapa_shared(smem_u32(&rfull[rs]), 0));
+                mbar_arrive_cluster(mapa_shared(smem_u32(&rfull[rs]), 1));
+                if (++rs == kRing) {
+                    rs = 0;
+                    rph ^= 1;
+                }
+            } else if (dyn) {
+                if (!ring_next(rs, rph, true, t)) {
+                    ok = false;
+                    break;
+                }
+            }
+            if (t < 0 || t >= total_tiles) break;
             int split, mb, nb;
             tile_coords(p, t, split, mb, nb);
             int kb0 = split * p.kb_per_split;
@@ -274,7 +339,14 @@ __global__ void __launch_bounds__(kThreads2, 1)
         constexpr uint32_t B_KSTEP = B_MN ? G::UK * 128 : 32;
         constexpr uint32_t A_LBO = A_MN ? G::BK * 128 : 16;
         constexpr uint32_t B_LBO = B_MN ? G::BK * 128 : 16;
-        for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
+        uint32_t rs = 0, rph = 0;
+        for (int ts = cluster_id; ok; ts += num_clusters) {
+            int t = ts;
+            if (dyn && !ring_next(rs, rph, true, t)) {
+                ok = false;
+                break;
+            }
+            if (t < 0 || t >= total_tiles) break;
             int split, mb, nb;
             tile_coords(p, t, split, mb, nb);
             int kb0 = split * p.kb_per_split;
@@ -333,7 +405,17 @@ __global__ void __launch_bounds__(kThreads2, 1)
         uint32_t acc_phase = 0;
         uint32_t store_seq = 0;  // chunks this warp has staged (its slot ring position)
         bool ok = true;
-        for (int t = cluster_id; t < total_tiles; t += num_clusters) {
+        uint32_t rs = 0, rph = 0;
+        for (int ts = cluster_id;; ts += num_clusters) {
+            int t = ts;
+            if (dyn) {
+                bool got_tile = ring_next(rs, rph, lane == 0, t);
+                if (!__all_sync(0xffffffffu, got_tile)) {
+                    ok = false;
+                    break;
+                }
+            }
+            if (t < 0 || t >= total_tiles) break;
             int split, mb, nb;
             tile_coords(p, t, split, mb, nb);
             bool got = mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag);
@@ -508,6 +590,7 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X
     p.p2p = g.p2p;
     // the 3xTF32 planes come from the split kernel launched just before
     p.pdl = X3 && g.pdl != PDL_NONE ? PDL_WAIT_START : g.pdl;
+    p.tile_ctr = ctx->dyn_tiles != 0 ? g.tile_ctr : nullptr;
     tc = ta;  // unused unless a staged store is chosen
     tc2 = ta;
     if (g.p2p.world > 0) {

@@ -99,6 +99,8 @@ constexpr int kT = 64;  // transposing tile: 64 k x 64 mn
 // blockIdx.y selects the operand (uniform per block, so the barriers of the
 // transposing form are reached by every thread of the block).
 __global__ void __launch_bounds__(kSplitThreads) split_planes_kernel(Operand a, Operand b) {
+    pdl_wait();  // programmatic dependent launch: the kernel before this one is done
+    pdl_launch_dependents();
     __shared__ float tile[kT][kT + 1];
     const Operand& o = blockIdx.y == 0 ? a : b;
     float* hi_plane = o.dst;
@@ -221,9 +223,8 @@ int launch_gemm_x3(rt_ctx* ctx, const GemmDesc& g, float* ws, size_t ws_bytes, c
     const int64_t cap = (int64_t)ctx->sm_count * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    split_planes_kernel<<<dim3((unsigned)blocks, 2), kSplitThreads, 0, st>>>(a, b);
+    RT_CUDA(launch_k(ctx->plan_pdl, split_planes_kernel, dim3((unsigned)blocks, 2), dim3(kSplitThreads), 0, st, a, b));
     count_launch(ctx);
-    RT_CUDA(cudaGetLastError());
     X3Planes x3{a.dst, a.ldw, (int64_t)plane_floats(a), b.dst, b.ldw, (int64_t)plane_floats(b)};
     return launch_gemm_tc_x3(ctx, g, x3, st);
 }

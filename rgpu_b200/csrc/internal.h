@@ -57,6 +57,9 @@ struct rt_ctx {
     bool f32_tensor = true;  // f32 GEMMs on the tensor cores (3xTF32) when fast_gemm is on
     bool tma_store = true;   // tensor-core GEMM epilogues store C through shared memory and TMA
     bool pdl = true;  // plan GEMMs may launch as programmatic dependents (GemmDesc::pdl)
+    bool plan_pdl = false;  // a plan pass is being captured: its small kernels launch as programmatic dependents
+    int dyn_tiles = -1;  // plan GEMMs hand out tiles dynamically (GemmDesc::tile_ctr): 1 always, 0 never,
+                         // -1 under data parallelism (where other streams' kernels hold SMs at GEMM starts)
     int skinny_k_max = -1;   // narrow-K GEMMs (n > 16) deeper than this go to the tensor cores; -1: by size
     // Grow-only workspace for the hi/lo operand copies of 3xTF32 GEMMs that
     // bring none of their own.  A replaced buffer is kept until the context
@@ -126,6 +129,10 @@ struct GemmDesc {
     // (PDL_NONE: an ordinary launch).  The plan sets it from what the GEMM
     // reads and writes relative to the kernel launched just before it.
     int pdl;
+    // A zeroed int that only this launch uses: the pair kernel then hands out
+    // tiles dynamically (an atomic counter) instead of round robin.  Null:
+    // round robin.
+    int* tile_ctr;
 };
 
 // How a GEMM launched as a programmatic dependent of the previous kernel on
@@ -144,6 +151,37 @@ struct GemmDesc {
 // A kernel lets its dependents launch only once it has passed its own wait,
 // so "complete before the previous kernel's wait" carries down the chain.
 enum { PDL_NONE = 0, PDL_WAIT_START = 1, PDL_WAIT_EPILOGUE = 2, PDL_NO_WAIT = 3 };
+
+// Programmatic dependent launch in device code (PTX griddepcontrol): wait
+// until the grid this one depends on has completed and its writes are
+// visible; let the grids that depend on this one launch.  Both are no-ops in
+// a kernel launched the ordinary way.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// The small kernels of a captured plan pass (operand split, skinny and
+// few-row GEMMs, split-K reduce, softmax-CE, Adam scalars) start with
+// pdl_wait(); pdl_launch_dependents(); and, while rt_ctx::plan_pdl is set,
+// launch as programmatic dependents of the kernel before them: their launch
+// and set-up overlap that kernel's tail, and each waits for it before it
+// touches memory.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                     Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (pdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 
 // Peer memory of a communicator's ranks (comm.cu).
 int comm_share_buffer(rt_comm* comm, void* local, void** peers);

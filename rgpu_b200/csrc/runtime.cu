@@ -100,6 +100,8 @@ int rt_ctx_create(int device, rt_ctx** out) {
     c->tma_store = !(st_env && st_env[0] == '0');
     const char* pdl_env = getenv("RTGPU_PDL");
     c->pdl = !(pdl_env && pdl_env[0] == '0');
+    const char* dyn_env = getenv("RTGPU_DYN_TILES");
+    c->dyn_tiles = dyn_env && dyn_env[0] == '0' ? 0 : dyn_env && dyn_env[0] == '1' ? 1 : -1;
     // RTGPU_SKINNY_K_MAX=<k>: narrow-K GEMMs deeper than k go to the tensor
     // cores (default: chosen by dtype and size, see narrow_k_on_tensor_cores)
     const char* sk_env = getenv("RTGPU_SKINNY_K_MAX");

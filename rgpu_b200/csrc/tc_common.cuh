@@ -219,6 +219,7 @@ struct TcParams {
     int split_a;
     void* c_lo;  // bf16 output's low-order plane (same ldc): bf16(v - bf16(v)); null = none
     int pdl;  // PDL_* (internal.h): how this launch waits for the kernel before it
+    int* tile_ctr;  // pair kernel: zeroed tile counter of this launch (dynamic schedule); null = static
 };
 
 // Epilogue staging: one 32 x 32 output chunk per epilogue warp (4 KB), the
@@ -253,12 +254,6 @@ __device__ __forceinline__ void tile_coords(const TcParams& p, int t, int& split
     mb = first + in % rows;
     nb = in / rows;
 }
-
-// Programmatic dependent launch (PTX griddepcontrol): wait until the grid
-// this one depends on has completed and its writes are visible; let the
-// grids that depend on this one launch.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ void record_error(int* err, int code, int detail) {
     if (atomicCAS(err, 0, code) == 0) err[1] = detail;
