@@ -64,6 +64,12 @@ int rt_ctx_info(const rt_ctx* ctx, char* buf, size_t len);
 /* Gpu::sync (gpu/mod.rs:564-566); also reports RT_ERR_DEVICE_TIMEOUT when a
  * kernel's bounded wait expired since the last sync. */
 int rt_ctx_sync(rt_ctx* ctx);
+/* No counterpart in the reference.  Exercises the device-timeout path without
+ * a fault: enqueues a kernel whose one thread waits on a barrier that nothing
+ * signals, with the GEMMs' bounded wait (2 s), and records a timeout when it
+ * gives up.  The next rt_ctx_sync returns RT_ERR_DEVICE_TIMEOUT; the context
+ * stays usable. */
+int rt_ctx_selftest_timeout(rt_ctx* ctx);
 /* The cudaStream_t work is enqueued on (Gpu::queue, gpu/mod.rs:422-424). */
 void* rt_ctx_stream(rt_ctx* ctx);
 /* Use a caller-owned cudaStream_t instead (NULL restores the context's own). */

@@ -38,7 +38,7 @@ int fail(int code, const char* fmt, ...);
 
 // Device-side error codes written to ctx->dev_err[0] by kernels whose
 // bounded waits expire (never a trap: the context stays usable).
-enum DevErr : int { DEV_OK = 0, DEV_TIMEOUT_PRODUCER = 1, DEV_TIMEOUT_MMA = 2, DEV_TIMEOUT_EPILOGUE = 3 };
+enum DevErr : int { DEV_OK = 0, DEV_TIMEOUT_PRODUCER = 1, DEV_TIMEOUT_MMA = 2, DEV_TIMEOUT_EPILOGUE = 3, DEV_TIMEOUT_SELFTEST = 4 };
 
 inline size_t dtype_size(rt_dtype d) { return d == RT_BF16 ? 2 : 4; }
 

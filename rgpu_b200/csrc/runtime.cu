@@ -31,6 +31,8 @@ static int check_device_error(rt_ctx* ctx) {
     if (h[0] != DEV_OK) {
         int zero[4] = {0, 0, 0, 0};
         RT_CUDA(cudaMemcpy(ctx->dev_err, zero, sizeof zero, cudaMemcpyHostToDevice));
+        if (h[0] == DEV_TIMEOUT_SELFTEST)
+            return fail(RT_ERR_DEVICE_TIMEOUT, "the self-test wait expired on the device, as it is meant to");
         const char* role = h[0] == DEV_TIMEOUT_PRODUCER ? "TMA producer"
                            : h[0] == DEV_TIMEOUT_MMA    ? "MMA issuer"
                                                         : "epilogue";

@@ -70,6 +70,7 @@ _SIGS = [
     ("rt_ctx_destroy", C.c_int, [C.c_void_p]),
     ("rt_ctx_info", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
     ("rt_ctx_sync", C.c_int, [C.c_void_p]),
+    ("rt_ctx_selftest_timeout", C.c_int, [C.c_void_p]),
     ("rt_ctx_stream", C.c_void_p, [C.c_void_p]),
     ("rt_ctx_set_stream", C.c_int, [C.c_void_p, C.c_void_p]),
     ("rt_ctx_set_fast_gemm", C.c_int, [C.c_void_p, C.c_int]),
@@ -292,6 +293,11 @@ class Gpu:
 
     def sync(self):
         _check(lib().rt_ctx_sync(self.handle))
+
+    def selftest_timeout(self):
+        """Enqueue the device-timeout self-test (rt_ctx_selftest_timeout): the
+        next sync raises RtError with RT_ERR_DEVICE_TIMEOUT."""
+        _check(lib().rt_ctx_selftest_timeout(self.handle))
 
     def stream(self) -> int:
         return lib().rt_ctx_stream(self.handle)

@@ -503,3 +503,25 @@ def test_few_row_gemms(gpu, m, n, k):
         ref = _skinny_ref((hi.astype(np.float64) + lo), w, G.RT_EPI_BIAS_RELU, bias, None)
         got = gpu.download(chi).astype(np.float64) + gpu.download(clo)
         assert rel_l2(got, ref) <= 1e-5, f"split {m}x{n}x{k}: {rel_l2(got, ref):.2e}"
+
+
+def test_device_wait_timeout_is_reported_and_the_context_stays_usable(gpu):
+    # A kernel whose bounded barrier wait runs out (nothing signals the
+    # barrier) records a timeout instead of spinning or faulting; the next
+    # sync reports RT_ERR_DEVICE_TIMEOUT, clears it, and the context keeps
+    # working.
+    import time
+
+    t0 = time.perf_counter()
+    gpu.selftest_timeout()
+    with pytest.raises(rgpu_b200.RtError) as e:
+        gpu.sync()
+    waited = time.perf_counter() - t0
+    assert e.value.code == G.RT_ERR_DEVICE_TIMEOUT and "self-test" in str(e.value)
+    assert 1.5 < waited < 30.0, waited  # the 2 s wait limit, not a hang
+    gpu.sync()  # the error word was cleared
+    a, b = _ab(64, 48, 32)
+    c = gpu.zeros((64, 48))
+    gpu.matmul(gpu.upload(a), gpu.upload(b), c)
+    gpu.sync()
+    assert erro_rel(oracle.matmul(a, b), gpu.download(c)) < 1e-5
