@@ -601,13 +601,35 @@ def run_infer(args):
     gpu.close()
 
 
+# B200 L2: a step whose working set is smaller runs with L2 flushed before each
+# timed step (flush_l2_between_steps); larger ones stream it every step.
+L2_BYTES = 126 << 20
+
+
+def working_set_bytes(cfg, rows):
+    """Bytes a train step touches: parameters with their gradients and
+    optimiser state, the input rows, and each layer's activations and
+    adjoints."""
+    dims, es = cfg["dims"], 2 if cfg["dtype"] == "bf16" else 4
+    params = sum((dims[l] + 1) * dims[l + 1] for l in range(len(dims) - 1))
+    per_param = 4 + 4 + (8 if cfg["optimizer"] == "adam" else 0) + (2 if cfg["dtype"] == "bf16" else 0)
+    return params * per_param + rows * dims[0] * es + rows * sum(dims[1:]) * es * 2
+
+
+def flush_l2_between_steps(cfg, rows):
+    return working_set_bytes(cfg, rows) < L2_BYTES
+
+
 def config_dict(cfg_name, cfg, n, global_batch):
     d = cfg["dims"]
+    rows = global_batch // n
+    l2 = ("working set smaller than L2: L2 flushed (256 MB write, then 256 MB read) before every timed step, "
+          "each step timed by its own events" if flush_l2_between_steps(cfg, rows)
+          else "inputs larger than L2 (each step streams several GB)")
     return {"workload": ("wide MLP " if cfg_name == "wide" else "MLP ") + "->".join(map(str, d)),
-            "global_batch": global_batch, "batch_per_gpu": global_batch // n, "dtype_policy":
+            "global_batch": global_batch, "batch_per_gpu": rows, "dtype_policy":
             "bf16 operands, f32 accumulate, f32 master weights" if cfg["dtype"] == "bf16" else "f32",
-            "optimizer": f"{cfg['optimizer']}(lr={cfg['lr']})", "parallelism": f"dp{n}",
-            "l2": "inputs larger than L2 (each step streams several GB)"}
+            "optimizer": f"{cfg['optimizer']}(lr={cfg['lr']})", "parallelism": f"dp{n}", "l2": l2}
 
 
 def main():
@@ -722,16 +744,43 @@ def main():
         gpu.sync()
         torch.cuda.synchronize()
 
+    cold = flush_l2_between_steps(cfg, batch)
+    if cold:
+        flush_w = torch.empty(256 << 20, dtype=torch.uint8, device=torch.device("cuda", local))
+        flush_r = torch.ones(64 << 20, dtype=torch.float32, device=torch.device("cuda", local))
+        flush_s = torch.empty((), dtype=torch.float32, device=torch.device("cuda", local))
+
+    def flush_l2():
+        # a write larger than L2, then a read of another buffer, so the next step
+        # starts with an L2 that holds none of its data and no dirty lines
+        with torch.cuda.stream(stream):
+            flush_w.fill_(1)
+            torch.sum(flush_r, dim=None, out=flush_s)
+
     def timed(fn, k):
         barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(k):
-            fn()
-        e1.record(stream)
-        gpu.sync()
-        ms = e0.elapsed_time(e1)
+        if cold:
+            # small working set: L2 flushed before every step, outside its events
+            evs = []
+            for _ in range(k):
+                flush_l2()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                fn()
+                e1.record(stream)
+                evs.append((e0, e1))
+            gpu.sync()
+            ms = sum(a.elapsed_time(b) for a, b in evs)
+        else:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(k):
+                fn()
+            e1.record(stream)
+            gpu.sync()
+            ms = e0.elapsed_time(e1)
         t = torch.tensor([ms], dtype=torch.float64, device="cuda")
         if dist:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -768,6 +817,8 @@ def main():
     barrier()
     op_sum = None
     for _ in range(args.steps):
+        if cold:
+            flush_l2()
         step_dev()
         gpu.sync()
         ops_i = mlp.op_times()

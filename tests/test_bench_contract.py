@@ -1,0 +1,41 @@
+"""The benchmark's JSON contract, checked on CPU: `bench.py --impl reference`
+(the reference's CPU step, restated by the oracle) on the small config prints
+one JSON line with the keys the benchmark driver reads, times real steps, and
+reports how many it ran.  Also the L2 rule: a config whose working set fits in
+L2 is timed with L2 flushed before every step, and says so."""
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_reference_arm_prints_one_complete_json_line():
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--config", "small",
+                        "--steps", "2", "--warmup", "1"], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1, r.stdout
+    d = json.loads(lines[0])
+    for key in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["impl"] == "reference" and d["unit"] == "samples/s" and d["higher_is_better"] is True
+    assert d["steps"] == 2 and d["steps_requested"] == 2
+    assert d["value"] > 0 and abs(d["value"] - 2048 / (d["ms_per_step"] / 1e3)) < 1e-6 * d["value"]
+    cb = d["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["cpu_model"]
+    assert d["e2e"] == {"value": d["value"], "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert d["config"]["workload"] == "MLP 512->1024->1024->10"
+
+
+def test_l2_rule_follows_the_working_set():
+    sys.path.insert(0, ROOT)
+    import bench
+
+    small, wide = bench.CONFIGS["small"], bench.CONFIGS["wide"]
+    assert bench.flush_l2_between_steps(small, small["batch"])
+    assert not bench.flush_l2_between_steps(wide, wide["batch"])
+    assert "flushed" in bench.config_dict("small", small, 1, small["batch"])["l2"]
+    assert "larger than L2" in bench.config_dict("wide", wide, 1, wide["batch"])["l2"]
