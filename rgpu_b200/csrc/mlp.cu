@@ -16,16 +16,22 @@
 //     separate column reduction runs;
 //   - W_l and b_l share one [d_l + 1, ld] block (b in the last row), and so do
 //     their gradients and Adam moments, so one optimiser launch updates both;
-//   - per layer the dW GEMM runs first (under data parallelism its allreduce
-//     then starts while the dX GEMM computes), the dX GEMM second; the layer's
-//     optimiser update runs on a side stream once the dX GEMM, the last reader
-//     of W_l, is done (and, under data parallelism, the allreduce), so the
-//     update's HBM traffic overlaps the remaining backward GEMMs; the comm
-//     stream carries the allreduces (and, when gradients are summed in bf16,
-//     their casts).  dW GEMMs run in row chunks: the first layer's always (it
-//     is the last GEMM of the step, so its update then trails it by one chunk
-//     only), every layer's under data parallelism (each chunk's allreduce
-//     starts while the next chunk computes).
+//   - on one device with SGD or Adam, per layer the dX GEMM (the last reader
+//     of W_l) runs first and the dW GEMM second, with the update fused into
+//     its epilogue (backward_fused);
+//   - otherwise (data parallelism, no optimiser, RTGPU_FUSED_OPT=0) the dW
+//     GEMM runs first, in row chunks whose gradient sums (allreduce, or the
+//     sharded optimiser's reduce-scatter by NCCL or copy engines) start on the
+//     comm stream while the next chunk computes; the dX GEMM second; each
+//     chunk's update on the optimiser stream once the dX GEMM is done and the
+//     chunk is summed (backward_and_update).  The first layer's dW is chunked
+//     there too: it is the last GEMM of the step, so its update then trails
+//     it by one chunk only;
+//   - bf16 plans keep hidden activations that feed another hidden layer as
+//     hi + lo bf16 planes (the next forward GEMM's second k segment);
+//   - the pair-kernel GEMMs launch as programmatic dependents of the kernel
+//     before them (GemmDesc::pdl), and under data parallelism take their tiles
+//     from per-GEMM counters that the pass zeroes at its start;
 //   - two input slots: a host step copies the next batch on a copy stream
 //     while the previous step computes.
 #include <cstdlib>
