@@ -118,7 +118,7 @@ __device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t adesc, uin
     }
 }
 
-template <typename TIn, int BN>
+template <typename TIn, int BN, bool SPLIT_A = false>
 struct Geo2 {
     static constexpr int ES = sizeof(TIn);
     static constexpr int BK = 128 / ES;
@@ -127,22 +127,28 @@ struct Geo2 {
     static constexpr int BNH = BN / 2;  // B rows (n) held by each CTA
     static constexpr int A_BYTES = 128 * 128;
     static constexpr int B_BYTES = BNH * 128;
-    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int A_PLANES = SPLIT_A ? 2 : 1;  // SPLIT_A: A and its low-order plane share a stage
+    static constexpr int STAGE_BYTES = A_PLANES * A_BYTES + B_BYTES;
     static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int EPI_BYTES = kEpiWarps * kStageBytes;
     static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 512 /*barriers, tile ring*/;
 };
 
-// Split bf16 A (p.split_a) and a bf16 output's low-order plane (p.c_lo): as
-// in the one-CTA kernel, through tmap_a2 and tmap_c2.
-template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false, bool SPLIT_C = false>
+// Split bf16 A (A + a_lo, through tmap_a2) and a bf16 output's low-order
+// plane (p.c_lo, through tmap_c2).  SPLIT_A (the NN forward GEMM of a layer
+// fed by split activations): each stage holds A's low-order plane, A and the
+// B tile, and the MMAs run the lo products, then A's, on that one B tile, so
+// B crosses L2 -> SMEM once per k block (4 stages of 48 KB instead of 6 of
+// 32 KB).  Other layouts given a_lo keep the interleaved form (p.split_a: the
+// k loop alternates a lo and a hi k block, loading B twice).
+template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false, bool SPLIT_C = false, bool SPLIT_A = false>
 __global__ void __launch_bounds__(kThreads2, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CUtensorMap tmap_a2,
                     const __grid_constant__ CUtensorMap tmap_c2, TcParams p) {
     static_assert(!X3 || (sizeof(TIn) == 4 && !A_MN && !B_MN), "3xTF32 planes are f32 and K-major");
-    using G = Geo2<TIn, BN>;
+    using G = Geo2<TIn, BN, SPLIT_A>;
     constexpr bool kTF32 = sizeof(TIn) == 4;
     constexpr int STAGES = G::STAGES;
     constexpr uint32_t IDESC = make_idesc(kTF32, A_MN, B_MN, BN, BM2);
@@ -150,7 +156,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* smem_a = smem;
-    uint8_t* smem_b = smem + STAGES * G::A_BYTES;
+    uint8_t* smem_alo = smem + STAGES * G::A_BYTES;  // SPLIT_A: A's low-order plane of each stage
+    uint8_t* smem_b = smem + STAGES * G::A_PLANES * G::A_BYTES;
     uint8_t* smem_epi = smem + STAGES * G::STAGE_BYTES;  // [8 epilogue warps][32 x 32] output staging
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem_epi + G::EPI_BYTES);
     uint64_t* full = bars;                     // leader: both CTAs' bytes of a stage
@@ -193,7 +200,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
         prefetch_tmap(&tmap_a);
         prefetch_tmap(&tmap_b);
         if (p.tma_store) prefetch_tmap(&tmap_c);
-        if (p.split_a) prefetch_tmap(&tmap_a2);
+        if (SPLIT_A || p.split_a) prefetch_tmap(&tmap_a2);
         if (SPLIT_C && p.tma_store) prefetch_tmap(&tmap_c2);
     }
     if (warp == 2) {
@@ -297,7 +304,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
                 } else {
                     int k0 = kb * G::BK;
                     const CUtensorMap* map_a = &tmap_a;
-                    if (p.split_a) {
+                    if constexpr (SPLIT_A) {
+                        // A's low-order plane of this k block into the stage's second A slot
+                        tma_load_2d_pair(smem_u32(smem_alo + stage * G::A_BYTES), &tmap_a2, k0, m0, leader_full);
+                    } else if (p.split_a) {
                         // k blocks alternate: A's low-order plane at k block kb / 2, then A at
                         // the same k block, so the second load of each B tile hits L2
                         k0 = (kb >> 1) * G::BK;
@@ -365,11 +375,21 @@ __global__ void __launch_bounds__(kThreads2, 1)
                 tc_fence_after();
                 const uint32_t sa = smem_u32(smem_a + stage * G::A_BYTES);
                 const uint32_t sb = smem_u32(smem_b + stage * G::B_BYTES);
+                if constexpr (SPLIT_A) {
+                    // the low-order products first (small terms), then A's, on the same B
+                    const uint32_t sl = smem_u32(smem_alo + stage * G::A_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < G::BK / G::UK; ++kk) {
+                        uint64_t ad = smem_desc(sl + kk * A_KSTEP, A_LBO, 1024);
+                        uint64_t bd = smem_desc(sb + kk * B_KSTEP, B_LBO, 1024);
+                        tc_mma_pair<kTF32>(d_tmem, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+                    }
+                }
 #pragma unroll
                 for (int kk = 0; kk < G::BK / G::UK; ++kk) {
                     uint64_t ad = smem_desc(sa + kk * A_KSTEP, A_LBO, 1024);
                     uint64_t bd = smem_desc(sb + kk * B_KSTEP, B_LBO, 1024);
-                    tc_mma_pair<kTF32>(d_tmem, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+                    tc_mma_pair<kTF32>(d_tmem, ad, bd, IDESC, (SPLIT_A || kb > kb0 || kk > 0) ? 1u : 0u);
                 }
                 // release the stage in both CTAs once these MMAs have read it
                 tc_commit_pair(smem_u32(&empty[stage]));
@@ -523,9 +543,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
     }
 }
 
-template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false, bool SPLIT_C = false>
+template <typename TIn, bool A_MN, bool B_MN, int BN, bool X3 = false, bool SPLIT_C = false, bool SPLIT_A = false>
 int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X3Planes* x3 = nullptr) {
-    using G = Geo2<TIn, BN>;
+    using G = Geo2<TIn, BN, SPLIT_A>;
     const bool bf16 = sizeof(TIn) == 2;
     CUtensorMap ta, tb, tc, ta2, tc2;
     if constexpr (X3) {
@@ -563,7 +583,7 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X
         p.kb_seg = p.kblocks;
         p.kblocks *= 3;
     } else {
-        if (g.a_lo) {
+        if (g.a_lo && !SPLIT_A) {
             p.split_a = 1;
             p.kblocks *= 2;  // each k block twice: A's low-order plane, then A
         }
@@ -632,7 +652,7 @@ int launch_pair_variant(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st, const X
     } else {
         p.pdl = PDL_NONE;  // an ordinary launch: nothing to wait for
     }
-    RT_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3, SPLIT_C>, ta, tb, tc, ta2, tc2, p));
+    RT_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3, SPLIT_C, SPLIT_A>, ta, tb, tc, ta2, tc2, p));
     count_launch(ctx);
     if (splits > 1) return launch_splitk_reduce(ctx, gr, st);
     return RT_OK;
@@ -644,8 +664,10 @@ template <int BN>
 int launch_pair_layout(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
     if (g.c_lo) {
         if (g.layout != RT_NN) return fail(RT_ERR_UNSUPPORTED, "c_lo is supported for the NN layout only");
+        if (g.a_lo) return launch_pair_variant<__nv_bfloat16, false, true, BN, false, true, true>(ctx, g, st);
         return launch_pair_variant<__nv_bfloat16, false, true, BN, false, true>(ctx, g, st);
     }
+    if (g.a_lo && g.layout == RT_NN) return launch_pair_variant<__nv_bfloat16, false, true, BN, false, false, true>(ctx, g, st);
     switch (g.layout) {
         case RT_NN: return launch_pair_variant<__nv_bfloat16, false, true, BN>(ctx, g, st);
         case RT_NT: return launch_pair_variant<__nv_bfloat16, false, false, BN>(ctx, g, st);
@@ -655,10 +677,11 @@ int launch_pair_layout(rt_ctx* ctx, const GemmDesc& g, cudaStream_t st) {
 }
 
 
-template <bool A_MN, bool B_MN, int BN, typename TIn = __nv_bfloat16, bool X3 = false, bool SPLIT_C = false>
+template <bool A_MN, bool B_MN, int BN, typename TIn = __nv_bfloat16, bool X3 = false, bool SPLIT_C = false,
+          bool SPLIT_A = false>
 int set_attr_pair() {
-    RT_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3, SPLIT_C>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Geo2<TIn, BN>::SMEM));
+    RT_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<TIn, A_MN, B_MN, BN, X3, SPLIT_C, SPLIT_A>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Geo2<TIn, BN, SPLIT_A>::SMEM));
     return RT_OK;
 }
 
@@ -676,6 +699,10 @@ int gemm_tc2_init(rt_ctx* ctx) {
     RT_TRY((set_attr_pair<false, false, 256, float, true>()));
     RT_TRY((set_attr_pair<false, true, 128, __nv_bfloat16, false, true>()));  // forward with c_lo
     RT_TRY((set_attr_pair<false, true, 256, __nv_bfloat16, false, true>()));
+    RT_TRY((set_attr_pair<false, true, 128, __nv_bfloat16, false, true, true>()));  // split A (+ c_lo)
+    RT_TRY((set_attr_pair<false, true, 256, __nv_bfloat16, false, true, true>()));
+    RT_TRY((set_attr_pair<false, true, 128, __nv_bfloat16, false, false, true>()));
+    RT_TRY((set_attr_pair<false, true, 256, __nv_bfloat16, false, false, true>()));
     return RT_OK;
 }
 

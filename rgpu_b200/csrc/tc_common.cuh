@@ -214,8 +214,9 @@ struct TcParams {
                     // 3 = fused optimiser through the staging boxes (opt_chunk), 4 = rows scattered to
                     // their owners' receive buffers over peer memory (p2p_chunk), 0 = direct stores
     P2PScatter p2p;
-    // Split bf16 A (a_lo): the k loop runs twice the k blocks, alternating A's low-order
-    // plane (tmap_a2) and A itself at each k block; B is the same for both.
+    // Split bf16 A (a_lo) outside the pair kernel's SPLIT_A form: the k loop runs twice the
+    // k blocks, alternating A's low-order plane (tmap_a2) and A itself at each k block; B is
+    // the same for both.
     int split_a;
     void* c_lo;  // bf16 output's low-order plane (same ldc): bf16(v - bf16(v)); null = none
     int pdl;  // PDL_* (internal.h): how this launch waits for the kernel before it
