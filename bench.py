@@ -56,7 +56,7 @@ CPU_SAMPLE_ROWS = {"wide": 256, "small": 2048, "probe_dw": 256}
 TRAFFIC_PER_LAUNCH = {
     "dw_gemm": (1.099e9 + 0.251e9, "bench.py --gemm TN --mnk 8192 8192 8192"),
     "dw_gemm_adam": (2.087e9 + 1.182e9, "the dW launch of bench.py --config probe_dw"),
-    "fwd_gemm_bias_relu_split": (1.694e9 + 0.256e9, "bench.py --gemm NN --split --mnk 8192 8192 8192"),
+    "fwd_gemm_bias_relu_split": (1.742e9 + 0.255e9, "bench.py --gemm NN --split --mnk 8192 8192 8192"),
 }
 TRAFFIC_FLOPS = 2.0 * 8192 ** 3
 
