@@ -133,6 +133,8 @@ struct Geo2 {
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int EPI_BYTES = kEpiWarps * kStageBytes;
     static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 512 /*barriers, tile ring*/;
+    static_assert(STAGES >= 3, "the operand ring needs at least three stages to overlap loads and MMAs");
+    static_assert(SMEM <= 227 * 1024, "dynamic shared memory above the per-CTA limit");
 };
 
 // Split bf16 A (A + a_lo, through tmap_a2) and a bf16 output's low-order
@@ -148,6 +150,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
                     const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CUtensorMap tmap_a2,
                     const __grid_constant__ CUtensorMap tmap_c2, TcParams p) {
     static_assert(!X3 || (sizeof(TIn) == 4 && !A_MN && !B_MN), "3xTF32 planes are f32 and K-major");
+    static_assert(!SPLIT_A || (sizeof(TIn) == 2 && !A_MN && !X3), "split A planes are bf16 and K-major");
     using G = Geo2<TIn, BN, SPLIT_A>;
     constexpr bool kTF32 = sizeof(TIn) == 4;
     constexpr int STAGES = G::STAGES;
