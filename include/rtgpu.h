@@ -145,7 +145,8 @@ int64_t rt_split_k_workspace(int64_t m, int64_t n, int slices);
  * that capacity fail with RT_ERR_INVALID.  All calls on a device share the
  * array, so calls whose kernels overlap on the GPU race and must be
  * serialised.  The first call on a context looks up the array's device
- * address (cudaGetSymbolAddress) and keeps it in the context. */
+ * address (cudaGetSymbolAddress) and keeps it in the context; make that first
+ * call before any stream capture begins. */
 int rt_matmul_split_k_noalloc(rt_ctx* ctx, const rt_tensor* a, const rt_tensor* b, rt_tensor* c,
                               int slices, int transposed);
 int64_t rt_split_k_static_capacity(void);

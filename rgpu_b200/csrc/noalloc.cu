@@ -22,7 +22,8 @@
 //     is looked up with cudaGetSymbolAddress, with the context's device
 //     current, the first time this entry point runs on a context, and kept in
 //     the context (a context created after a cudaDeviceReset looks it up
-//     again).
+//     again).  Make that first call on a context before any stream capture
+//     begins, so that the lookup is not made while a capture is open.
 #include "internal.h"
 
 namespace rt {
