@@ -212,7 +212,7 @@ int rt_adam(rt_ctx* ctx, rt_tensor* theta, rt_tensor* m, rt_tensor* v, const rt_
 /* Sgd::step without momentum (optim.rs:80-95): theta -= g * lr.  The
  * reference has no GPU kernel for it. */
 int rt_sgd(rt_ctx* ctx, rt_tensor* theta, const rt_tensor* g, float lr);
-/* Gpu::op_empacota_f16 (gpu/mod.rs:1170-1182), bf16 instead of f16:
+/* Gpu::op_empacota_f16 (gpu/mod.rs:1165-1176), bf16 instead of f16:
  * dst (bf16) = round-to-nearest-even(src (f32)). */
 int rt_cast(rt_ctx* ctx, const rt_tensor* src, rt_tensor* dst);
 
@@ -371,7 +371,7 @@ int64_t rt_plan_shard_slice(int64_t d, int64_t units, int64_t r0, int64_t r1, in
 typedef struct rt_tape rt_tape;   /* tape::Tape  (tape.rs:43-67) */
 typedef struct rt_var rt_var;     /* tape::Var   (tape.rs:136-184); owned by its tape */
 typedef struct rt_param rt_param; /* tape::Param (tape.rs:76-132) */
-typedef struct rt_adam_state rt_adam_state; /* optim::Adam (optim.rs:540-558) */
+typedef struct rt_adam_state rt_adam_state; /* optim::Adam (optim.rs:142-160) */
 
 /* Param::new (tape.rs:86-92): rows x cols f32 from host (NULL = zeros). */
 int rt_param_create(rt_ctx* ctx, const float* host, int64_t rows, int64_t cols, rt_param** out);
@@ -441,9 +441,9 @@ int rt_var_backward(rt_var* root);
 /* Grads::of (tape.rs:238-243): device view of the parameter's gradient, or
  * *view = NULL when the parameter took no part in the graph. */
 int rt_grads_of(rt_tape* t, rt_param* p, rt_tensor** view);
-/* Sgd::step without momentum (optim.rs:479-493). */
+/* Sgd::step without momentum (optim.rs:80-95). */
 int rt_sgd_step(rt_ctx* ctx, int n, rt_param* const* params, rt_tape* grads, float lr);
-/* Adam::with_betas (optim.rs:555-557) and Adam::step (optim.rs:561-597). */
+/* Adam::with_betas (optim.rs:157-159) and Adam::step (optim.rs:162-198). */
 int rt_adam_create(rt_ctx* ctx, float lr, float beta1, float beta2, float eps, rt_adam_state** out);
 int rt_adam_destroy(rt_adam_state* a);
 int rt_adam_step(rt_adam_state* a, int n, rt_param* const* params, rt_tape* grads);

@@ -210,7 +210,7 @@ __device__ float powi_f32(float a, int b) {
     return recip ? 1.0f / r : r;
 }
 
-// Bias-correction scalars of Adam step t (optim.rs:574-583), t from the host.
+// Bias-correction scalars of Adam step t (optim.rs:164-172), t from the host.
 __global__ void opt_scalars_at_kernel(OptScalars* s, int t, float beta1, float beta2) {
     s->t = t;
     float c1 = __fsub_rn(1.0f, powi_f32(beta1, t));
@@ -231,7 +231,7 @@ __global__ void opt_step_begin_kernel(OptScalars* s, float beta1, float beta2) {
 }
 
 // One fused pass per element (adam_one: the rounding sequence of
-// optim.rs:586-593), 128-bit vector loads where the buffers allow.
+// optim.rs:189-195), 128-bit vector loads where the buffers allow.
 // 128-thread blocks of <= 48 registers per thread: small enough to co-reside
 // with a running tensor-core GEMM CTA on the same SM, so a layer's update
 // overlaps the next layer's GEMMs.
@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(kOptThreads) adam_kernel(OptBatch batch, const
     }
 }
 
-// optim.rs:486-493: theta -= g * lr.
+// optim.rs:88-95: theta -= g * lr.
 __global__ void __launch_bounds__(kOptThreads) sgd_kernel(OptBatch batch, float lr) {
     const OptTensor& T = batch.t[blockIdx.y];
     const int64_t n = T.n;

@@ -1,7 +1,7 @@
 // Per-element optimiser arithmetic shared by the stand-alone SGD/Adam kernels
 // and by the GEMM epilogues that apply the update to a dW tile as it leaves
 // the accumulator.  Rounding sequence of rtensor's CPU optimiser
-// (crates/rtensor/src/optim.rs:486-493 SGD, 586-593 Adam): every product and
+// (crates/rtensor/src/optim.rs:88-95 SGD, 189-195 Adam): every product and
 // sum rounded separately (__fmul_rn / __fadd_rn forbid FMA contraction), so
 // the GPU update is bit-identical to the CPU one for the same gradient.
 #pragma once

@@ -376,7 +376,7 @@ const Buf* grad_of(rt_tape* t, rt_param* p) {
 
 extern "C" {
 
-// Sgd::step without momentum (optim.rs:479-493): theta -= g * lr for every
+// Sgd::step without momentum (optim.rs:80-95): theta -= g * lr for every
 // parameter that has a gradient.
 int rt_sgd_step(rt_ctx* ctx, int n, rt_param* const* params, rt_tape* grads, float lr) {
     RT_CHECK(ctx && (n == 0 || params) && grads && grads->backward_done, "rt_sgd_step: bad arguments");
@@ -422,7 +422,7 @@ int rt_adam_destroy(rt_adam_state* a) {
     return RT_OK;
 }
 
-// Adam::step (optim.rs:561-597): t += 1 on the device, then one fused pass
+// Adam::step (optim.rs:162-198): t += 1 on the device, then one fused pass
 // per parameter with a gradient; moments are created zeroed on first use.
 int rt_adam_step(rt_adam_state* a, int n, rt_param* const* params, rt_tape* grads) {
     RT_CHECK(a && (n == 0 || params) && grads && grads->backward_done, "rt_adam_step: bad arguments");

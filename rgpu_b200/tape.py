@@ -322,7 +322,7 @@ class Sgd:
 
 
 class Adam:
-    """Adam::new / with_betas (optim.rs:550-558)."""
+    """Adam::new / with_betas (optim.rs:152-160)."""
 
     def __init__(self, gpu: Gpu, lr: float, beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8):
         h = C.c_void_p()
@@ -398,7 +398,7 @@ class Sequential:
         return [p for layer in self.layers for p in layer.params()]
 
     def predict(self, gpu: Gpu, x: np.ndarray) -> np.ndarray:
-        """Sequential::predict (nn.rs:196-199): a forward pass on a fresh tape."""
+        """Sequential::predict (nn.rs:184-188): a forward pass on a fresh tape."""
         tape = Tape(gpu)
         try:
             return self.forward(constant(tape, x)).value()
