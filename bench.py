@@ -617,6 +617,48 @@ def run_infer(args):
 L2_BYTES = 126 << 20
 
 
+def dominant_kernel_roofline(ops, cfg, pk):
+    """`roofline` of the step's dominant kernel: the GEMM label with the
+    largest total time.  `ops` holds (label, algorithmic FLOPs, mean ms) per
+    launch of one step, `pk` the peaks (`peaks()`)."""
+    by_label = {}
+    for lab, fl, t in ops:
+        a = by_label.setdefault(lab, [0.0, 0.0, 0])
+        a[0] += fl
+        a[1] += t
+        a[2] += 1
+    dom = max(by_label.items(), key=lambda kv: kv[1][1]) if by_label else None
+    roof = None
+    if dom:
+        lab, (fl, t, cnt) = dom
+        ach = fl / (t / 1e3) / 1e12 if t > 0 else 0.0
+        # The denominator is the burst bf16 figure (cuBLAS timed alone): the
+        # timed region is a fraction of a second, shorter than the seconds-long
+        # loop behind the sustained figure.  The wide step does reach the power
+        # cap (sw_power_cap in its clock record), so the sustained figure is
+        # given beside it.  f32 GEMMs run as 3xTF32: three tf32 products at
+        # half the bf16 rate.
+        scale = 1.0 if cfg["dtype"] == "bf16" else 1.0 / 6.0
+        peak = pk["bf16"] * scale
+        sustained = pk["bf16_sus"] * scale if cfg["dtype"] == "bf16" and pk["bf16_sus"] else None
+        traffic, traffic_src = None, None
+        if cfg["dtype"] == "bf16" and lab in TRAFFIC_PER_LAUNCH:
+            tb, traffic_src = TRAFFIC_PER_LAUNCH[lab]
+            traffic = tb * (fl / cnt) / TRAFFIC_FLOPS
+        # split-activation forward GEMMs run two bf16 products per algorithmic one
+        executed = 2.0 if lab.endswith("_split") else 1.0
+        roof = {"bound": "tensor", "kernel": lab, "launches_per_step": cnt, "achieved": ach, "peak": peak,
+                "unit": "TFLOP/s", "frac": ach / peak, "peak_sustained": sustained,
+                "frac_of_sustained": ach / sustained if sustained else None,
+                "executed_tensor_tflops": ach * executed, "executed_frac": ach * executed / peak,
+                "traffic": traffic,
+                "traffic_note": (f"DRAM bytes per launch: ncu capture of {traffic_src}, scaled by FLOPs"
+                                 if traffic_src else "no ncu capture for this kernel"),
+                "peak_source": pk["source"] + (" bf16 dense burst (cuBLAS timed alone)" if cfg["dtype"] == "bf16"
+                                               else " bf16 dense burst / 2 (tf32 rate) / 3 (3xTF32 products)")}
+    return roof
+
+
 def working_set_bytes(cfg, rows):
     """Bytes a train step touches: parameters with their gradients and
     optimiser state, the input rows, and each layer's activations and
@@ -881,42 +923,7 @@ def main():
     e2e_value = global_batch / (ms_e2e / args.steps / 1e3)
     pk = peaks()
     step_flops = exact_flops(dims, batch)
-    # dominant kernel: the GEMM label with the largest total time in the step
-    by_label = {}
-    for lab, fl, t in ops:
-        a = by_label.setdefault(lab, [0.0, 0.0, 0])
-        a[0] += fl
-        a[1] += t
-        a[2] += 1
-    dom = max(by_label.items(), key=lambda kv: kv[1][1]) if by_label else None
-    roof = None
-    if dom:
-        lab, (fl, t, cnt) = dom
-        ach = fl / (t / 1e3) / 1e12 if t > 0 else 0.0
-        # The wide step runs at the power cap (sw_power_cap in its clock
-        # record), so its kernels' denominator is the sustained bf16 figure
-        # (cuBLAS back to back under the cap), with the burst one beside it.
-        # The small f32 step is short and stays below the cap: burst.  f32
-        # GEMMs run as 3xTF32: three tf32 products at half the bf16 rate.
-        sustained = cfg["dtype"] == "bf16" and bool(pk["bf16_sus"])
-        scale = 1.0 if cfg["dtype"] == "bf16" else 1.0 / 6.0
-        burst = pk["bf16"] * scale
-        peak = (pk["bf16_sus"] if sustained else pk["bf16"]) * scale
-        traffic, traffic_src = None, None
-        if cfg["dtype"] == "bf16" and lab in TRAFFIC_PER_LAUNCH:
-            tb, traffic_src = TRAFFIC_PER_LAUNCH[lab]
-            traffic = tb * (fl / cnt) / TRAFFIC_FLOPS
-        # split-activation forward GEMMs run two bf16 products per algorithmic one
-        executed = 2.0 if lab.endswith("_split") else 1.0
-        roof = {"bound": "tensor", "kernel": lab, "launches_per_step": cnt, "achieved": ach, "peak": peak,
-                "unit": "TFLOP/s", "frac": ach / peak, "peak_burst": burst, "frac_of_burst": ach / burst,
-                "executed_tensor_tflops": ach * executed, "executed_frac_of_burst": ach * executed / burst,
-                "traffic": traffic,
-                "traffic_note": (f"DRAM bytes per launch: ncu capture of {traffic_src}, scaled by FLOPs"
-                                 if traffic_src else "no ncu capture for this kernel"),
-                "peak_source": pk["source"] + (" bf16 dense sustained (cuBLAS back to back under the power cap)"
-                                               if sustained else
-                                               " bf16 dense burst / 2 (tf32 rate) / 3 (3xTF32 products)")}
+    roof = dominant_kernel_roofline(ops, cfg, pk)
     gemm_t = sum(t for lab, fl, t in ops if fl > 0)
     gemm_f = sum(fl for lab, fl, t in ops if fl > 0)
     step_tflops = step_flops / (ms_step / 1e3) / 1e12

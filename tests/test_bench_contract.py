@@ -39,3 +39,27 @@ def test_l2_rule_follows_the_working_set():
     assert not bench.flush_l2_between_steps(wide, wide["batch"])
     assert "flushed" in bench.config_dict("small", small, 1, small["batch"])["l2"]
     assert "larger than L2" in bench.config_dict("wide", wide, 1, wide["batch"])["l2"]
+
+
+def test_roofline_names_the_dominant_kernel_against_the_burst_peak():
+    sys.path.insert(0, ROOT)
+    import bench
+
+    f = 2.0 * 8192 ** 3
+    # (label, algorithmic FLOPs, mean ms) per launch, shaped like a wide step
+    ops = [("fwd_gemm_bias_relu_split", f, 1.385), ("fwd_gemm_bias_relu_split", f, 1.346),
+           ("dw_gemm_adam", f, 0.970), ("dw_gemm_adam", f, 0.965), ("softmax_xent", 0.0, 0.063)]
+    pk = {"hbm": 6553.6, "bf16": 1642.0, "bf16_sus": 1380.2, "source": "measured"}
+    r = bench.dominant_kernel_roofline(ops, bench.CONFIGS["wide"], pk)
+    assert r["kernel"] == "fwd_gemm_bias_relu_split" and r["launches_per_step"] == 2
+    ach = 2 * f / ((1.385 + 1.346) / 1e3) / 1e12
+    assert abs(r["achieved"] - ach) < 1e-9 * ach
+    assert r["peak"] == 1642.0 and abs(r["frac"] - ach / 1642.0) < 1e-12
+    assert abs(r["frac_of_sustained"] - ach / 1380.2) < 1e-12
+    assert abs(r["executed_tensor_tflops"] - 2 * ach) < 1e-9 * ach  # two bf16 products per algorithmic one
+    tb = bench.TRAFFIC_PER_LAUNCH["fwd_gemm_bias_relu_split"][0]
+    assert abs(r["traffic"] - tb) < 1e-6 * tb  # each launch is one 8192^3 GEMM
+    # f32 configs: the 3xTF32 rate, no sustained figure
+    r32 = bench.dominant_kernel_roofline([("fwd_gemm_bias_relu", 1e9, 0.01)], bench.CONFIGS["small"], pk)
+    assert abs(r32["peak"] - 1642.0 / 6) < 1e-9 and r32["peak_sustained"] is None and r32["traffic"] is None
+    assert bench.dominant_kernel_roofline([], bench.CONFIGS["small"], pk) is None
