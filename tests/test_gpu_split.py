@@ -36,6 +36,8 @@ def _split(x):
 CASES = [
     (2048, 2048, 512),  # two-CTA kernel, 256-wide tiles
     (2048, 1024, 320),  # two-CTA kernel, 128-wide tiles
+    (2000, 1500, 136),  # two-CTA kernel, 256-wide tiles, ragged m, n and k
+    (1000, 1200, 200),  # two-CTA kernel, 128-wide tiles, ragged m, n and k
     (512, 384, 1000),   # one-CTA kernel, 128 x 64 tiles (few tiles)
     (200, 136, 72),     # one-CTA kernel, ragged edges
     (300, 10, 512),     # skinny narrow-N kernel (n <= 16)
@@ -96,8 +98,8 @@ def test_split_a_on_the_narrow_k_cuda_core_kernel(monkeypatch, m, n, k):
 
 
 @pytest.mark.parametrize("fast", [True, False])
-@pytest.mark.parametrize("m,n,k", [(2048, 2048, 512), (2048, 1024, 320), (512, 384, 1000), (200, 136, 72),
-                                   (300, 200, 16)])
+@pytest.mark.parametrize("m,n,k", [(2048, 2048, 512), (2048, 1024, 320), (2000, 1500, 136), (1000, 1200, 200),
+                                   (512, 384, 1000), (200, 136, 72), (300, 200, 16)])
 def test_c_lo_plane_carries_the_rounding_residual(gpu, fast, m, n, k):
     # bias + ReLU epilogue with a bf16 output and its low-order plane: the
     # forward GEMM of a hidden layer in the split-activation plan, whose
