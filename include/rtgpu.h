@@ -72,7 +72,8 @@ int rt_ctx_sync(rt_ctx* ctx);
 int rt_ctx_selftest_timeout(rt_ctx* ctx);
 /* The cudaStream_t work is enqueued on (Gpu::queue, gpu/mod.rs:422-424). */
 void* rt_ctx_stream(rt_ctx* ctx);
-/* Use a caller-owned cudaStream_t instead (NULL restores the context's own). */
+/* Use a caller-owned cudaStream_t instead (NULL restores the context's own).
+ * No counterpart in the reference: wgpu owns its one queue. */
 int rt_ctx_set_stream(rt_ctx* ctx, void* stream);
 /* Gpu::set_fast_gemm (gpu/mod.rs:442-448): 1 = tcgen05/TMA tensor-core GEMM
  * where the operands allow it (default), 0 = tiled SIMT GEMM everywhere. */
@@ -84,10 +85,12 @@ int rt_ctx_set_fast_gemm(rt_ctx* ctx, int on);
 int rt_ctx_set_f32_tensor(rt_ctx* ctx, int on);
 /* Gpu::set_grupo_l2 (gpu/mod.rs:452-458): tile rows per L2 raster group. */
 int rt_ctx_set_l2_group(rt_ctx* ctx, int group);
-/* Number of kernels this context has launched so far (evidence counter). */
+/* Number of kernels this context has launched so far (evidence counter).  No
+ * counterpart in the reference. */
 int rt_ctx_launch_count(const rt_ctx* ctx, uint64_t* out);
 
-/* Page-locked host memory for asynchronous copies. */
+/* Page-locked host memory for asynchronous copies.  No counterpart in the
+ * reference (wgpu stages host data itself); used with rt_mlp_step_host. */
 int rt_host_alloc(size_t bytes, void** out);
 int rt_host_free(void* p);
 
@@ -105,12 +108,16 @@ int rt_upload_labels(rt_ctx* ctx, const uint32_t* labels, int64_t n, rt_tensor**
  * holds rows*cols floats, packed (no padding). */
 int rt_tensor_download(rt_ctx* ctx, const rt_tensor* t, float* host);
 /* Non-owning view of caller memory (cudarc-style raw handle).  `ld` in
- * elements; 0 means packed. */
+ * elements; 0 means packed.  The reference's GpuTensor always owns its buffer
+ * (gpu/mod.rs:191-195); rt_tensor_free releases what rt_tensor_zeros,
+ * rt_tensor_upload and rt_upload_labels allocated, and only the handle of a
+ * view. */
 int rt_tensor_wrap(rt_ctx* ctx, void* device_ptr, rt_dtype dtype, int rank, const int64_t* shape,
                    int64_t ld, rt_tensor** out);
 int rt_tensor_free(rt_tensor* t);
 void* rt_tensor_ptr(const rt_tensor* t);
-/* rows, cols, ld (rank-1 tensors report rows = 1). */
+/* GpuTensor's shape fields (gpu/mod.rs:191-195): rows, cols, ld (rank-1
+ * tensors report rows = 1). */
 int rt_tensor_dims(const rt_tensor* t, int64_t* rows, int64_t* cols, int64_t* ld);
 
 /* ------------------------------------------------------------------- ops */
@@ -152,7 +159,10 @@ int rt_matmul_split_k_noalloc(rt_ctx* ctx, const rt_tensor* a, const rt_tensor* 
 int64_t rt_split_k_static_capacity(void);
 
 /* Full-control GEMM used by the plan (and by Rust callers that manage their
- * own buffers).  Logical A is [m,k], logical B is [k,n]:
+ * own buffers).  It folds the reference's GEMM builders into one call:
+ * op_matmul / op_matmul_at_b / op_matmul_a_bt (gpu/mod.rs:685-700) by layout,
+ * op_matmul_bias (722-749) and op_relu_bwd (778-788) by epilogue, ops_split_k
+ * (1095-1146) by split_k.  Logical A is [m,k], logical B is [k,n]:
  *   RT_NN: A stored [m,k] (lda), B stored [k,n] (ldb)      Y  = X W
  *   RT_NT: A stored [m,k],       B stored [n,k]            dX = dY W^T
  *   RT_TN: A stored [k,m],       B stored [k,n]            dW = X^T dY
@@ -255,7 +265,9 @@ int rt_mlp_destroy(rt_mlp* mlp);
  * GpuMlp::carregar does, gpu/mod.rs:1486-1495), then forward, backward,
  * (allreduce,) update.  x_dtype is RT_F32 or RT_BF16. */
 int rt_mlp_step(rt_mlp* mlp, const void* x_dev, rt_dtype x_dtype, const uint32_t* labels_dev);
-/* The same step from page-locked or pageable HOST buffers: the host->device
+/* No counterpart in the reference (GpuMlp::step takes device buffers, and
+ * carregar copies them device to device).  The same step from page-locked or
+ * pageable HOST buffers: the host->device
  * copies and, when loss_rows_host != NULL, the device->host copy of the
  * per-row losses ([batch] f32) are enqueued with the step.  Returns once
  * enqueued; the loss buffer is valid after rt_ctx_sync. */
@@ -275,7 +287,8 @@ int rt_mlp_forward_host(rt_mlp* mlp, const void* x_host, rt_dtype x_dtype, float
 int rt_mlp_logits(rt_mlp* mlp, float* host);
 /* GpuMlp::last_loss (gpu/mod.rs:1529-1531): mean row loss, blocking. */
 int rt_mlp_last_loss(rt_mlp* mlp, float* out);
-/* The last step's mean loss over the global batch: with a communicator the
+/* No counterpart in the reference (GpuMlp is single-device).  The last step's
+ * mean loss over the global batch: with a communicator the
  * ranks' per-row losses are all-gathered and summed in global row order
  * (collective: every rank calls it); without one, rt_mlp_last_loss. */
 int rt_mlp_global_loss(rt_mlp* mlp, float* out);
@@ -317,7 +330,8 @@ int rt_mlp_dispatches_per_step(rt_mlp* mlp, int* out);
 int rt_mlp_enable_timing(rt_mlp* mlp, int on);
 int rt_mlp_op_count(rt_mlp* mlp, int* count);
 int rt_mlp_op_time(rt_mlp* mlp, int i, const char** label, double* flops, float* ms);
-/* Attach a communicator: dW/db are summed over ranks on a second stream,
+/* No counterpart in the reference (GpuMlp is single-device).  Attach a
+ * communicator: dW/db are summed over ranks on a second stream,
  * chunk by chunk as backward produces them.  f32 plans, plans without an
  * optimiser and RTGPU_GRAD_COMM=bf16 allreduce the gradients.  bf16 plans with
  * SGD or Adam shard the optimiser (ZeRO stage 1; RTGPU_SHARDED_OPT=0 turns it
@@ -380,7 +394,7 @@ int rt_param_destroy(rt_param* p);
 int rt_param_read(rt_param* p, float* host);
 /* Param::set (tape.rs:119-121). */
 int rt_param_write(rt_param* p, const float* host);
-/* Device view of the parameter's value (non-owning rt_tensor). */
+/* Param::value (tape.rs:102-104) as a device view (non-owning rt_tensor). */
 int rt_param_value(rt_param* p, rt_tensor** view);
 /* Tape::new (tape.rs:50-52) / drop. */
 int rt_tape_create(rt_ctx* ctx, rt_tape** out);
@@ -455,7 +469,9 @@ int rt_sgd_destroy(rt_sgd_state* s);
 int rt_sgd_state_step(rt_sgd_state* s, int n, rt_param* const* params, rt_tape* grads);
 
 /* ------------------------------------------------------------------ NCCL */
-/* 128-byte ncclUniqueId, created on one rank and shared out of band. */
+/* No counterpart in the reference (single-device).  NCCL communicator over
+ * NVLink, one process per GPU.  128-byte ncclUniqueId, created on one rank and
+ * shared out of band. */
 int rt_comm_unique_id(unsigned char id[128]);
 int rt_comm_init(rt_ctx* ctx, int rank, int world, const unsigned char id[128], rt_comm** out);
 int rt_comm_destroy(rt_comm* comm);
