@@ -659,6 +659,65 @@ def dominant_kernel_roofline(ops, cfg, pk):
     return roof
 
 
+# Child runs that put BASELINE configs[1] (the f32 batch-2048 step) and
+# configs[3] (the dW sweep) into the default benchmark line, each bounded by
+# its own time limit (seconds).
+EXTRA_RUNS = {
+    "config2_small": (["--config", "small"], 120),
+    "config4_dw_sweep": (["--sweep"], 240),
+}
+
+
+def summarize_extra(key, lines):
+    """The part of a child run's JSON lines that goes into the main line."""
+    if key == "config2_small":
+        d = lines[-1]
+        return {k: d.get(k) for k in ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "dtype", "config",
+                                      "e2e", "roofline", "cpu_baseline", "gpu_launches", "clocks")}
+    pts = [d for d in lines if "summary" not in d]
+    return {"summaries": [d for d in lines if "summary" in d], "points": len(pts),
+            "columns": ["dtype", "M", "N", "K", "ms", "tflops", "frac_of_roofline", "bound"],
+            "per_point": [[d["dtype"], d["M"], d["N"], d["K"], d["ms"], d["tflops"], d["frac"], d["bound"]]
+                          for d in pts]}
+
+
+def run_extra(key, cmd, limit):
+    """Runs one child benchmark; its JSON lines are summarised, and a failure
+    or an overrun comes back as {"error": ...} instead of an exception."""
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=limit, cwd=ROOT)
+    except subprocess.TimeoutExpired:
+        return {"error": f"did not finish within {limit} s"}
+    except Exception as e:
+        return {"error": f"could not start: {e}"}
+    lines = []
+    for ln in r.stdout.splitlines():
+        if ln.startswith("{"):
+            try:
+                lines.append(json.loads(ln))
+            except ValueError:
+                pass
+    if r.returncode != 0 or not lines:
+        return {"error": f"exit {r.returncode}: {r.stderr.strip()[-300:]}"}
+    try:
+        return summarize_extra(key, lines)
+    except Exception as e:
+        return {"error": f"unreadable output: {e}"}
+
+
+def run_extra_configs(args):
+    """configs[1] and configs[3] as child processes of the default 1-GPU run,
+    after its own timed regions: the f32 step with the driver's step counts,
+    and the whole dW sweep."""
+    out = {}
+    for key, (extra, limit) in EXTRA_RUNS.items():
+        cmd = [sys.executable, os.path.abspath(__file__)] + extra
+        if key == "config2_small":
+            cmd += ["--steps", str(args.steps), "--warmup", str(max(3, args.warmup))]
+        out[key] = run_extra(key, cmd, limit)
+    return out
+
+
 def working_set_bytes(cfg, rows):
     """Bytes a train step touches: parameters with their gradients and
     optimiser state, the input rows, and each layer's activations and
@@ -695,6 +754,8 @@ def main():
     ap.add_argument("--global-batch", type=int, default=0, help="strong scaling: fixed global batch")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-strong", action="store_true", help="skip the fixed-global-batch (65536) leg")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the configs[1] step and the configs[3] sweep that the default 1-GPU run adds")
     ap.add_argument("--gemm", choices=["NN", "NT", "TN"], help="profile one bf16 GEMM instead of the step")
     ap.add_argument("--mnk", type=int, nargs=3, default=[8192, 8192, 8192], metavar=("M", "N", "K"))
     ap.add_argument("--reps", type=int, default=3)
@@ -935,6 +996,9 @@ def main():
                 cpu = cpu_baseline(args.config, cfg)
             except Exception as e:  # the baseline must not hide the GPU line
                 cpu = {"value": None, "unit": "samples/s", "cores": 1, "kind": "port", "sample": f"failed: {e}"}
+        extra = None
+        if world == 1 and args.config == "wide" and not args.global_batch and not args.no_extra:
+            extra = run_extra_configs(args)
         in_bytes = xh.nbytes + labels.nbytes
         line = {
             "metric": "train samples/sec (fwd+bwd+update)", "value": value, "unit": "samples/s",
@@ -961,6 +1025,8 @@ def main():
                                          "tflops": round(fl / (t / 1e3) / 1e12, 1) if fl and t else None}
                                         for lab, fl, t in ops],
         }
+        if extra is not None:
+            line["other_configs"] = extra
         print(json.dumps(line), flush=True)
 
     if mlp:

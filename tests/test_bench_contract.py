@@ -63,3 +63,30 @@ def test_roofline_names_the_dominant_kernel_against_the_burst_peak():
     r32 = bench.dominant_kernel_roofline([("fwd_gemm_bias_relu", 1e9, 0.01)], bench.CONFIGS["small"], pk)
     assert abs(r32["peak"] - 1642.0 / 6) < 1e-9 and r32["peak_sustained"] is None and r32["traffic"] is None
     assert bench.dominant_kernel_roofline([], bench.CONFIGS["small"], pk) is None
+
+
+def test_other_configs_are_summarised_and_failures_reported():
+    sys.path.insert(0, ROOT)
+    import bench
+
+    # a child that prints a sweep's lines
+    pts = [{"dtype": "bf16", "M": 1024, "N": 512, "K": k, "ms": 0.01, "tflops": 1.0, "gbs": 1.0, "roofline_ms": 0.005,
+            "frac": 0.5, "bound": "hbm", "workspace_bytes": 0} for k in (1, 8)]
+    lines = pts + [{"summary": "bf16", "points": 2, "frac_median": 0.5, "frac_min": 0.5, "peak_source": "measured"}]
+    script = "import json\n" + "".join(f"print(json.dumps({d!r}))\n" for d in lines)
+    r = bench.run_extra("config4_dw_sweep", [sys.executable, "-c", script], 60)
+    assert r["points"] == 2 and r["summaries"][0]["frac_median"] == 0.5
+    assert r["per_point"][1] == ["bf16", 1024, 512, 8, 0.01, 1.0, 0.5, "hbm"]
+    # the f32 step's line keeps its measurement keys
+    step = {"metric": "m", "value": 6.6e6, "unit": "samples/s", "ms_per_step": 0.31, "steps": 5, "warmup": 3,
+            "dtype": "f32", "config": {"workload": "w"}, "e2e": {}, "roofline": {}, "cpu_baseline": None,
+            "gpu_launches": 40, "clocks": None, "kernels_mean_over_steps": []}
+    r = bench.run_extra("config2_small", [sys.executable, "-c", f"print({json.dumps(json.dumps(step))})"], 60)
+    assert r["value"] == 6.6e6 and r["gpu_launches"] == 40 and "kernels_mean_over_steps" not in r
+    # failures and overruns come back as errors, not exceptions
+    r = bench.run_extra("config2_small", [sys.executable, "-c", "import sys; sys.exit(3)"], 60)
+    assert r["error"].startswith("exit 3")
+    r = bench.run_extra("config2_small", [sys.executable, "-c", "import time; time.sleep(30)"], 1)
+    assert "within 1 s" in r["error"]
+    r = bench.run_extra("config2_small", [sys.executable, "-c", "print('{not json')"], 60)
+    assert "error" in r
