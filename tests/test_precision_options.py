@@ -15,8 +15,9 @@ Rounding points, as the GPU plan stores its tensors:
   ReLU masks and the dW GEMMs read hi;
 - every adjoint delta is stored as bf16.
 
-`step_gradients` is the whole emulation; run at batch 8192 it gives the
-table of gradient errors quoted for the fp8 option.  The test runs it at
+`step_gradients` is the whole emulation.  `python tests/test_precision_options.py`
+runs it on the inputs of the GPU's config-3 parity test (batch 8192, a few
+minutes) and prints the relative L2 error of every W and b per option.  The test runs it at
 batch 1024 (under a minute on 8 threads) and checks the ordering and the bar:
 the bf16 lo plane and the e4m3 one stay within the 2e-2 gradient bar, a
 single rounding does not."""
@@ -115,3 +116,31 @@ def test_low_order_plane_options_against_the_gradient_bar():
     assert err["none"][0] > 2e-2
     # the output layer reads hi only, so its error does not depend on lo
     assert err["bf16"][3] == pytest.approx(err["e4m3"][3], rel=0.05)
+
+
+def config3_table(batch=8192, seed=2024 + 3):
+    """Relative L2 error of every W and b for each low-order plane option, on
+    the inputs of the GPU's config-3 parity test (rtensor's Rng, Kaiming
+    weights and x given as bf16 values)."""
+    from tests.helpers import bf16_baseline_inputs
+
+    model_, x, labels = bf16_baseline_inputs(DIMS, batch, seed)
+    params = model_.params()
+    ws = [np.ascontiguousarray(params[i], np.float32) for i in range(0, len(params), 2)]
+    x = np.ascontiguousarray(x, np.float32)
+    labels = np.asarray(labels).astype(np.int64)
+    ref = step_gradients(ws, x, labels, "f32")
+    rows = {}
+    for lo in ("bf16", "e4m3", "none"):
+        got = step_gradients(ws, x, labels, lo)
+        rows[lo] = [float(np.linalg.norm(g[i] - r[i]) / np.linalg.norm(r[i])) for g, r in zip(got, ref) for i in (0, 1)]
+    return rows
+
+
+if __name__ == "__main__":
+    import os
+    import sys
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    for lo, errs in config3_table().items():
+        print(f"{lo:5s} " + " ".join(f"{e:.2e}" for e in errs), flush=True)
